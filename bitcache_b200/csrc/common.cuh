@@ -1,0 +1,160 @@
+// Shared device/host definitions for the bitcache B200 kernels (sm_100a).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#include "bitcache_b200.h"
+
+namespace bc {
+
+// ---------------------------------------------------------------------------
+// Reference record formats (byte-compatible with the reference structs).
+//   BinaryVec   : uint32 words[8]; __half scale;          sizeof 36, align 4
+//   ResidualVec : uint8 nibbles[128]; __half scale;        sizeof 130, align 2
+// (binary_encode.cuh:13-18, residual.cuh:11-16 of the reference.)
+// ---------------------------------------------------------------------------
+constexpr int kMaxHeadDim = 256;
+constexpr int kBinRecBytes = 36;
+constexpr int kBinScaleOff = 32;
+constexpr int kResRecBytes = 130;
+constexpr int kResScaleOff = 128;
+
+// ---------------------------------------------------------------------------
+// Device-side error word.  Kernels never trap: a bounded wait that gives up
+// ORs a code into the error word (defined once, in decode.cu, whose kernels
+// own every bounded wait) and the kernel returns; bc_get_device_error() reads
+// and clears it from the host.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void raise_device_error(unsigned int* word, unsigned int code) { atomicOr(word, code); }
+
+// Iteration cap for every spin on an mbarrier or a flag.  try_wait already
+// suspends for a hardware-defined interval per attempt, so this bounds a wait
+// to well under a minute while never triggering on a healthy GPU.
+constexpr uint32_t kSpinLimit = 1u << 24;
+
+// ---------------------------------------------------------------------------
+// mbarrier + 1-D bulk copy (TMA) helpers.  No multicast anywhere.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait: true when the phase completed, false after kSpinLimit tries.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
+    for (uint32_t it = 0; it < kSpinLimit; ++it)
+        if (mbar_try_wait(bar, parity)) return true;
+    return false;
+}
+
+// 1-D bulk global->shared copy completing on an mbarrier.  dst, src and bytes
+// must all be multiples of 16.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// ---------------------------------------------------------------------------
+// Packed fp32x2 arithmetic (sm_100).  Written without .ftz so that denormal
+// operands are honoured: the V accumulation feeds sign bits and INT4 codes in
+// as denormal bit patterns (value = pattern * 2^-149) and rescales them with
+// power-of-two coefficients, which is exact.
+// ---------------------------------------------------------------------------
+struct f2 {
+    float x, y;
+};
+
+__device__ __forceinline__ void ffma2(f2& acc, f2 a, f2 b) {
+    unsigned long long r, ua, ub, uc;
+    ua = *reinterpret_cast<unsigned long long*>(&a);
+    ub = *reinterpret_cast<unsigned long long*>(&b);
+    uc = *reinterpret_cast<unsigned long long*>(&acc);
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(ua), "l"(ub), "l"(uc));
+    acc = *reinterpret_cast<f2*>(&r);
+}
+
+__device__ __forceinline__ void fmul2(f2& acc, f2 a) {
+    unsigned long long r, ua, uc;
+    ua = *reinterpret_cast<unsigned long long*>(&a);
+    uc = *reinterpret_cast<unsigned long long*>(&acc);
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(uc), "l"(ua));
+    acc = *reinterpret_cast<f2*>(&r);
+}
+
+__device__ __forceinline__ float bits_f(uint32_t u) { return __uint_as_float(u); }
+
+// Exact power of two 2^e for e in [-126, 127].
+__device__ __forceinline__ float exp2i(int e) { return __uint_as_float((uint32_t)(e + 127) << 23); }
+
+__device__ __forceinline__ int dp4a_us(uint32_t a_u8, uint32_t b_s8, int c) {
+    int r;
+    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(r) : "r"(a_u8), "r"(b_s8), "r"(c));
+    return r;
+}
+__device__ __forceinline__ int dp4a_uu(uint32_t a_u8, uint32_t b_u8, int c) {
+    int r;
+    asm("dp4a.u32.u32 %0, %1, %2, %3;" : "=r"(r) : "r"(a_u8), "r"(b_u8), "r"(c));
+    return r;
+}
+
+__device__ __forceinline__ float fast_exp2(float x) {
+    float r;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+    return r;
+}
+
+// Streaming 16-byte read-only global load.
+__device__ __forceinline__ uint4 ldg_nc_v4(const void* p) {
+    uint4 r;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(p));
+    return r;
+}
+
+}  // namespace bc
+
+// ---------------------------------------------------------------------------
+// Host-side helpers shared by the entry points.
+// ---------------------------------------------------------------------------
+#define BC_LAUNCH_CHECK()                                  \
+    do {                                                   \
+        cudaError_t _e = cudaGetLastError();               \
+        if (_e != cudaSuccess) return BC_ERR_CUDA_BASE + (int)_e; \
+    } while (0)
+
+static inline bool bc_valid_head_dim(int d) { return d > 0 && d % 32 == 0 && d <= bc::kMaxHeadDim; }
+static inline bool bc_aligned(const void* p, uintptr_t a) { return ((uintptr_t)p % a) == 0; }

@@ -1,0 +1,472 @@
+// Encoders: sign-bit packing + mean|x| scale, INT4 residual, online (decode
+// step) append, and record <-> plane converters.  sm_100a.
+//
+// One warp encodes one vector.  Lane l holds elements l + 32k (k < head_dim/32),
+// so __ballot_sync(x >= 0) yields sign word k directly (bit i%32 of word i/32,
+// reference binary_encode.cu:36-39), and the mean-|x| reduction is evaluated in
+// exactly the reference's order: per-thread strided sums over a 128-thread
+// block followed by the stride-halving tree (binary_encode.cu:32-50).  Both
+// divisions (sum / head_dim and 7 / absmax) are written as in the reference
+// with runtime operands and the library is compiled with --use_fast_math like
+// the reference, so they lower to the same instruction and the encodings are
+// bit-identical.
+#include "common.cuh"
+
+namespace bc {
+
+template <int NW>
+struct WarpVec {
+    float x[NW];
+};
+
+template <int NW>
+__device__ __forceinline__ void load_vec(const __half* __restrict__ v, int lane, float (&x)[NW]) {
+#pragma unroll
+    for (int k = 0; k < NW; ++k) x[k] = __half2float(v[32 * k + lane]);
+}
+
+template <int NW>
+__device__ __forceinline__ void sign_words(const float (&x)[NW], uint32_t (&w)[NW]) {
+#pragma unroll
+    for (int k = 0; k < NW; ++k) w[k] = __ballot_sync(0xffffffffu, x[k] >= 0.0f);
+}
+
+// Sum of |x_i| in the reference block order (see file comment).  Thread t of
+// the reference's 128-thread block owns t and t + 128; here t = lane + 32k.
+template <int NW>
+__device__ __forceinline__ float tree_abs_sum(const float (&x)[NW]) {
+    float p7[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        float s = 0.0f;
+        if (k < NW) s += fabsf(x[k]);
+        if (k + 4 < NW) s += fabsf(x[k + 4]);
+        p7[k] = s;
+    }
+    const float p6a = p7[0] + p7[2];  // stride 64
+    const float p6b = p7[1] + p7[3];
+    float v = p6a + p6b;              // stride 32
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);  // strides 16..1
+    return v;
+}
+
+// INT4 residual of x against sign bits w and binary scale s (residual.cu:30-77,
+// online_encode.cu:85-119).  On return lanes 8m (m < 4) hold nibble word 4k+m
+// in nw[k] (8 codes, element 8j low nibble first) and lanes 4m (m < 8) hold the
+// 16-bit pair of bytes 16k+2m, 16k+2m+1 in nh[k].
+template <int NW>
+__device__ __forceinline__ float quantise_residual(const float (&x)[NW], const uint32_t (&w)[NW], float s, int lane,
+                                                   uint32_t (&nw)[NW], uint32_t (&nh)[NW]) {
+    float r[NW];
+    float lm = 0.0f;
+#pragma unroll
+    for (int k = 0; k < NW; ++k) {
+        const uint32_t bit = (w[k] >> lane) & 1u;
+        const float rec = bit ? s : -s;
+        r[k] = x[k] - rec;
+        lm = fmaxf(lm, fabsf(r[k]));
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) lm = fmaxf(lm, __shfl_xor_sync(0xffffffffu, lm, off));
+    const float absmax = lm;
+    const float inv_absmax = (absmax > 0.0f) ? (7.0f / absmax) : 0.0f;
+#pragma unroll
+    for (int k = 0; k < NW; ++k) {
+        int q = __float2int_rn(r[k] * inv_absmax);
+        q = max(-7, min(7, q));
+        const uint32_t nb = (uint32_t)q & 0xFu;
+        const uint32_t hi = __shfl_down_sync(0xffffffffu, nb, 1);
+        const uint32_t byte = nb | (hi << 4);
+        const uint32_t t1 = byte | (__shfl_down_sync(0xffffffffu, byte, 2) << 8);
+        const uint32_t t2 = t1 | (__shfl_down_sync(0xffffffffu, t1, 4) << 16);
+        nh[k] = t1;
+        nw[k] = t2;
+    }
+    return absmax;
+}
+
+__device__ __forceinline__ uint16_t f2h_bits(float f) { return __half_as_ushort(__float2half(f)); }
+
+// ---------------------------------------------------------------------------
+// Reference-record writers
+// ---------------------------------------------------------------------------
+template <int NW>
+__device__ __forceinline__ void store_binvec(uint8_t* rec, const uint32_t (&w)[NW], uint16_t scale, int lane) {
+    uint32_t* rw = reinterpret_cast<uint32_t*>(rec);
+    if (lane < 8) {
+        uint32_t v = 0;
+#pragma unroll
+        for (int k = 0; k < NW; ++k)
+            if (lane == k) v = w[k];
+        rw[lane] = v;  // words NW..7 zeroed
+    } else if (lane == 8) {
+        rw[8] = (uint32_t)scale;  // scale + zeroed padding
+    }
+}
+
+template <int NW>
+__device__ __forceinline__ void store_resvec(uint8_t* rec, const uint32_t (&nh)[NW], uint16_t scale, int lane) {
+    uint16_t* rh = reinterpret_cast<uint16_t*>(rec);  // records are 2-byte aligned
+#pragma unroll
+    for (int k = 0; k < NW; ++k)
+        if ((lane & 3) == 0) rh[8 * k + (lane >> 2)] = (uint16_t)nh[k];
+    for (int i = 8 * NW + lane; i < 64; i += 32) rh[i] = 0;  // unused nibbles zeroed
+    if (lane == 0) rh[64] = scale;
+}
+
+// ---------------------------------------------------------------------------
+// Plane writers
+// ---------------------------------------------------------------------------
+template <int NW>
+__device__ __forceinline__ void store_sign_row(uint32_t* row, const uint32_t (&w)[NW], int lane) {
+#pragma unroll
+    for (int k = 0; k < NW; ++k)
+        if (lane == k) row[k] = w[k];
+}
+
+template <int NW>
+__device__ __forceinline__ void store_nib_row(uint32_t* row, const uint32_t (&nw)[NW], int lane) {
+#pragma unroll
+    for (int k = 0; k < NW; ++k)
+        if ((lane & 7) == 0 && lane < 32) row[4 * k + (lane >> 3)] = nw[k];
+}
+
+// ---------------------------------------------------------------------------
+// Kernels
+// ---------------------------------------------------------------------------
+constexpr int kEncWarps = 8;
+
+template <int NW>
+__global__ void __launch_bounds__(kEncWarps * 32) k_binary_encode_rec(const __half* __restrict__ src,
+                                                                      uint8_t* __restrict__ out, int64_t n,
+                                                                      int head_dim) {
+    const int lane = threadIdx.x & 31;
+    const int64_t v = (int64_t)blockIdx.x * kEncWarps + (threadIdx.x >> 5);
+    if (v >= n) return;
+    float x[NW];
+    load_vec<NW>(src + v * head_dim, lane, x);
+    uint32_t w[NW];
+    sign_words<NW>(x, w);
+    const float mean_abs = tree_abs_sum<NW>(x) / (float)head_dim;
+    store_binvec<NW>(out + v * kBinRecBytes, w, f2h_bits(mean_abs), lane);
+}
+
+template <int NW>
+__global__ void __launch_bounds__(kEncWarps * 32) k_residual_encode_rec(const __half* __restrict__ src,
+                                                                        const uint8_t* __restrict__ bin,
+                                                                        uint8_t* __restrict__ out, int64_t n,
+                                                                        int head_dim) {
+    const int lane = threadIdx.x & 31;
+    const int64_t v = (int64_t)blockIdx.x * kEncWarps + (threadIdx.x >> 5);
+    if (v >= n) return;
+    float x[NW];
+    load_vec<NW>(src + v * head_dim, lane, x);
+    const uint8_t* brec = bin + v * kBinRecBytes;
+    uint32_t w[NW];
+#pragma unroll
+    for (int k = 0; k < NW; ++k) w[k] = reinterpret_cast<const uint32_t*>(brec)[k];
+    const float s = __half2float(__ushort_as_half(*reinterpret_cast<const uint16_t*>(brec + kBinScaleOff)));
+    uint32_t nw[NW], nh[NW];
+    const float absmax = quantise_residual<NW>(x, w, s, lane, nw, nh);
+    store_resvec<NW>(out + v * kResRecBytes, nh, f2h_bits(absmax), lane);
+}
+
+// Online token encode into reference-record ring buffers (online_encode.cu:17-120).
+template <int NW>
+__global__ void __launch_bounds__(kEncWarps * 32) k_online_encode_rec(const __half* __restrict__ kv,
+                                                                      uint8_t* __restrict__ bin,
+                                                                      uint8_t* __restrict__ res, int n_slots,
+                                                                      int head_dim, int write_slot, int max_seq) {
+    const int lane = threadIdx.x & 31;
+    const int slot = blockIdx.x * kEncWarps + (threadIdx.x >> 5);
+    if (slot >= n_slots) return;
+    float x[NW];
+    load_vec<NW>(kv + (int64_t)slot * head_dim, lane, x);
+    uint32_t w[NW];
+    sign_words<NW>(x, w);
+    const float scale_bin = tree_abs_sum<NW>(x) / (float)head_dim;
+    const int64_t cache_idx = (int64_t)slot * max_seq + write_slot;
+    store_binvec<NW>(bin + cache_idx * kBinRecBytes, w, f2h_bits(scale_bin), lane);
+    if (res != nullptr) {
+        uint32_t nw[NW], nh[NW];
+        const float absmax = quantise_residual<NW>(x, w, scale_bin, lane, nw, nh);
+        store_resvec<NW>(res + cache_idx * kResRecBytes, nh, f2h_bits(absmax), lane);
+    }
+}
+
+// Encode one vector into plane row `row`.
+template <int NW, int RES>
+__device__ __forceinline__ void encode_row_planes(const float (&x)[NW], int lane, int head_dim, bc_kv_planes P,
+                                                  int64_t row) {
+    uint32_t w[NW];
+    sign_words<NW>(x, w);
+    const float mean_abs = tree_abs_sum<NW>(x) / (float)head_dim;
+    const uint16_t sb = f2h_bits(mean_abs);
+    store_sign_row<NW>(reinterpret_cast<uint32_t*>(P.sign) + row * NW, w, lane);
+    if (lane == 0) reinterpret_cast<uint16_t*>(P.bscale)[row] = sb;
+    if (RES != BC_RES_NONE) {
+        const float s = (RES == BC_RES_FP16_SCALE) ? __half2float(__ushort_as_half(sb)) : mean_abs;
+        uint32_t nw[NW], nh[NW];
+        const float absmax = quantise_residual<NW>(x, w, s, lane, nw, nh);
+        store_nib_row<NW>(reinterpret_cast<uint32_t*>(P.nib) + row * (4 * NW), nw, lane);
+        if (lane == 0) reinterpret_cast<uint16_t*>(P.rscale)[row] = f2h_bits(absmax);
+    }
+}
+
+template <int NW, int RES>
+__global__ void __launch_bounds__(kEncWarps * 32) k_encode_planes(const __half* __restrict__ src, bc_kv_planes P,
+                                                                  int n_slots, int seq_len, int64_t kv_stride,
+                                                                  int head_dim) {
+    const int lane = threadIdx.x & 31;
+    const int64_t n = (int64_t)n_slots * seq_len;
+    const int64_t nwarps = (int64_t)gridDim.x * kEncWarps;
+    for (int64_t v = (int64_t)blockIdx.x * kEncWarps + (threadIdx.x >> 5); v < n; v += nwarps) {
+        float x[NW];
+        load_vec<NW>(src + v * head_dim, lane, x);
+        const int64_t slot = v / seq_len, s = v - slot * seq_len;
+        encode_row_planes<NW, RES>(x, lane, head_dim, P, slot * kv_stride + s);
+    }
+}
+
+// Append one K and one V token per slot: warps [0, n_slots) encode K, the rest V.
+template <int NW, int RES>
+__global__ void __launch_bounds__(kEncWarps * 32) k_append_kv(const __half* __restrict__ k,
+                                                              const __half* __restrict__ v, bc_kv_planes K,
+                                                              bc_kv_planes V, int n_slots, int head_dim,
+                                                              int64_t kv_stride, int64_t pos) {
+    const int lane = threadIdx.x & 31;
+    const int wid = blockIdx.x * kEncWarps + (threadIdx.x >> 5);
+    if (wid >= 2 * n_slots) return;
+    const bool is_v = wid >= n_slots;
+    const int slot = is_v ? wid - n_slots : wid;
+    float x[NW];
+    load_vec<NW>((is_v ? v : k) + (int64_t)slot * head_dim, lane, x);
+    encode_row_planes<NW, RES>(x, lane, head_dim, is_v ? V : K, (int64_t)slot * kv_stride + pos);
+}
+
+// Record <-> plane conversion (pure data movement, one warp per vector).
+template <int NW>
+__global__ void __launch_bounds__(kEncWarps * 32) k_records_to_planes(const uint8_t* __restrict__ bin,
+                                                                      const uint8_t* __restrict__ res,
+                                                                      bc_kv_planes P, int64_t n) {
+    const int lane = threadIdx.x & 31;
+    const int64_t v = (int64_t)blockIdx.x * kEncWarps + (threadIdx.x >> 5);
+    if (v >= n) return;
+    const uint8_t* b = bin + v * kBinRecBytes;
+    if (lane < NW) reinterpret_cast<uint32_t*>(P.sign)[v * NW + lane] = reinterpret_cast<const uint32_t*>(b)[lane];
+    if (lane == 0)
+        reinterpret_cast<uint16_t*>(P.bscale)[v] = *reinterpret_cast<const uint16_t*>(b + kBinScaleOff);
+    if (res != nullptr && P.nib != nullptr) {
+        const uint16_t* r = reinterpret_cast<const uint16_t*>(res + v * kResRecBytes);
+        uint16_t* dst = reinterpret_cast<uint16_t*>(P.nib) + v * (8 * NW);
+        for (int i = lane; i < 8 * NW; i += 32) dst[i] = r[i];
+        if (lane == 0) reinterpret_cast<uint16_t*>(P.rscale)[v] = r[64];
+    }
+}
+
+template <int NW>
+__global__ void __launch_bounds__(kEncWarps * 32) k_planes_to_records(bc_kv_planes P, uint8_t* __restrict__ bin,
+                                                                      uint8_t* __restrict__ res, int64_t n) {
+    const int lane = threadIdx.x & 31;
+    const int64_t v = (int64_t)blockIdx.x * kEncWarps + (threadIdx.x >> 5);
+    if (v >= n) return;
+    uint32_t* b = reinterpret_cast<uint32_t*>(bin + v * kBinRecBytes);
+    if (lane < 8) b[lane] = (lane < NW) ? reinterpret_cast<const uint32_t*>(P.sign)[v * NW + lane] : 0u;
+    if (lane == 8) b[8] = (uint32_t)reinterpret_cast<const uint16_t*>(P.bscale)[v];
+    if (res != nullptr && P.nib != nullptr) {
+        uint16_t* r = reinterpret_cast<uint16_t*>(res + v * kResRecBytes);
+        const uint16_t* src = reinterpret_cast<const uint16_t*>(P.nib) + v * (8 * NW);
+        for (int i = lane; i < 64; i += 32) r[i] = (i < 8 * NW) ? src[i] : (uint16_t)0;
+        if (lane == 0) r[64] = reinterpret_cast<const uint16_t*>(P.rscale)[v];
+    }
+}
+
+}  // namespace bc
+
+// ===========================================================================
+// Entry points
+// ===========================================================================
+using namespace bc;
+
+#define BC_DISPATCH_NW(d, KERNEL_CALL)               \
+    switch ((d) / 32) {                              \
+        case 1: { constexpr int NW = 1; KERNEL_CALL; break; } \
+        case 2: { constexpr int NW = 2; KERNEL_CALL; break; } \
+        case 3: { constexpr int NW = 3; KERNEL_CALL; break; } \
+        case 4: { constexpr int NW = 4; KERNEL_CALL; break; } \
+        case 5: { constexpr int NW = 5; KERNEL_CALL; break; } \
+        case 6: { constexpr int NW = 6; KERNEL_CALL; break; } \
+        case 7: { constexpr int NW = 7; KERNEL_CALL; break; } \
+        case 8: { constexpr int NW = 8; KERNEL_CALL; break; } \
+        default: return BC_ERR_HEAD_DIM;            \
+    }
+
+static inline unsigned enc_blocks(int64_t n) { return (unsigned)((n + kEncWarps - 1) / kEncWarps); }
+
+extern "C" {
+
+int64_t bc_sizeof_binary_vec(void) { return kBinRecBytes; }
+int64_t bc_sizeof_residual_vec(void) { return kResRecBytes; }
+
+const char* bc_status_string(int status) {
+    switch (status) {
+        case BC_OK: return "ok";
+        case BC_ERR_HEAD_DIM: return "head_dim must be a multiple of 32 in [32, 256]";
+        case BC_ERR_ARG: return "invalid argument (size, null pointer or mode)";
+        case BC_ERR_ALIGN: return "pointer not 16-byte aligned or kv_stride not a multiple of 8";
+        case BC_ERR_WORKSPACE: return "workspace too small";
+        case BC_ERR_UNSUPPORTED: return "shape not supported by the compiled kernels";
+        case BC_ERR_TOO_LARGE: return "size exceeds the fixed maximum of this entry point";
+        default: break;
+    }
+    if (status >= BC_ERR_CUDA_BASE) return cudaGetErrorString((cudaError_t)(status - BC_ERR_CUDA_BASE));
+    return "unknown status";
+}
+
+int bc_binary_encode(const void* src, void* out, int64_t n_vecs, int head_dim, void* stream) {
+    if (!bc_valid_head_dim(head_dim)) return BC_ERR_HEAD_DIM;
+    if (n_vecs < 0) return BC_ERR_ARG;
+    if (n_vecs == 0) return BC_OK;
+    if (!src || !out) return BC_ERR_ARG;
+    if (!bc_aligned(src, 2) || !bc_aligned(out, 4)) return BC_ERR_ALIGN;
+    cudaStream_t st = (cudaStream_t)stream;
+    BC_DISPATCH_NW(head_dim, (k_binary_encode_rec<NW><<<enc_blocks(n_vecs), kEncWarps * 32, 0, st>>>(
+                                  (const __half*)src, (uint8_t*)out, n_vecs, head_dim)));
+    BC_LAUNCH_CHECK();
+    return BC_OK;
+}
+
+int bc_residual_encode(const void* src, const void* bin, void* out, int64_t n_vecs, int head_dim, void* stream) {
+    if (!bc_valid_head_dim(head_dim)) return BC_ERR_HEAD_DIM;
+    if (n_vecs < 0) return BC_ERR_ARG;
+    if (n_vecs == 0) return BC_OK;
+    if (!src || !bin || !out) return BC_ERR_ARG;
+    if (!bc_aligned(src, 2) || !bc_aligned(bin, 4) || !bc_aligned(out, 2)) return BC_ERR_ALIGN;
+    cudaStream_t st = (cudaStream_t)stream;
+    BC_DISPATCH_NW(head_dim, (k_residual_encode_rec<NW><<<enc_blocks(n_vecs), kEncWarps * 32, 0, st>>>(
+                                  (const __half*)src, (const uint8_t*)bin, (uint8_t*)out, n_vecs, head_dim)));
+    BC_LAUNCH_CHECK();
+    return BC_OK;
+}
+
+int bc_online_encode_token(const void* kv, void* bin_cache, void* res_cache, int batch, int n_heads, int head_dim,
+                           int current_len, int max_seq, void* stream) {
+    if (!bc_valid_head_dim(head_dim)) return BC_ERR_HEAD_DIM;
+    if (batch < 0 || n_heads < 0 || max_seq <= 0 || current_len < 0) return BC_ERR_ARG;
+    const int n_slots = batch * n_heads;
+    if (n_slots == 0) return BC_OK;
+    if (!kv || !bin_cache) return BC_ERR_ARG;
+    if (!bc_aligned(kv, 2) || !bc_aligned(bin_cache, 4) || (res_cache && !bc_aligned(res_cache, 2)))
+        return BC_ERR_ALIGN;
+    const int write_slot = current_len % max_seq;
+    cudaStream_t st = (cudaStream_t)stream;
+    BC_DISPATCH_NW(head_dim, (k_online_encode_rec<NW><<<enc_blocks(n_slots), kEncWarps * 32, 0, st>>>(
+                                  (const __half*)kv, (uint8_t*)bin_cache, (uint8_t*)res_cache, n_slots, head_dim,
+                                  write_slot, max_seq)));
+    BC_LAUNCH_CHECK();
+    return BC_OK;
+}
+
+static int check_planes(const bc_kv_planes& P, bool need_res) {
+    if (!P.sign || !P.bscale) return BC_ERR_ARG;
+    if (need_res && (!P.nib || !P.rscale)) return BC_ERR_ARG;
+    if (!bc_aligned(P.sign, 16) || !bc_aligned(P.bscale, 16)) return BC_ERR_ALIGN;
+    if (need_res && (!bc_aligned(P.nib, 16) || !bc_aligned(P.rscale, 16))) return BC_ERR_ALIGN;
+    return BC_OK;
+}
+
+int bc_encode_planes(const void* src, bc_kv_planes out, int n_slots, int seq_len, int64_t kv_stride, int head_dim,
+                     int residual_mode, void* stream) {
+    if (!bc_valid_head_dim(head_dim)) return BC_ERR_HEAD_DIM;
+    if (n_slots < 0 || seq_len < 0 || kv_stride < seq_len) return BC_ERR_ARG;
+    if (residual_mode < BC_RES_NONE || residual_mode > BC_RES_FP32_SCALE) return BC_ERR_ARG;
+    const int64_t n = (int64_t)n_slots * seq_len;
+    if (n == 0) return BC_OK;
+    if (!src) return BC_ERR_ARG;
+    int rc = check_planes(out, residual_mode != BC_RES_NONE);
+    if (rc) return rc;
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int64_t max_blocks = (int64_t)sms * 8;
+    const unsigned blocks = (unsigned)(enc_blocks(n) < max_blocks ? enc_blocks(n) : max_blocks);
+    cudaStream_t st = (cudaStream_t)stream;
+    switch (residual_mode) {
+        case BC_RES_NONE:
+            BC_DISPATCH_NW(head_dim, (k_encode_planes<NW, BC_RES_NONE><<<blocks, kEncWarps * 32, 0, st>>>(
+                                          (const __half*)src, out, n_slots, seq_len, kv_stride, head_dim)));
+            break;
+        case BC_RES_FP16_SCALE:
+            BC_DISPATCH_NW(head_dim, (k_encode_planes<NW, BC_RES_FP16_SCALE><<<blocks, kEncWarps * 32, 0, st>>>(
+                                          (const __half*)src, out, n_slots, seq_len, kv_stride, head_dim)));
+            break;
+        default:
+            BC_DISPATCH_NW(head_dim, (k_encode_planes<NW, BC_RES_FP32_SCALE><<<blocks, kEncWarps * 32, 0, st>>>(
+                                          (const __half*)src, out, n_slots, seq_len, kv_stride, head_dim)));
+            break;
+    }
+    BC_LAUNCH_CHECK();
+    return BC_OK;
+}
+
+int bc_append_kv(const void* k, const void* v, bc_kv_planes K, bc_kv_planes V, int n_slots, int head_dim,
+                 int64_t kv_stride, int64_t pos, int residual_mode, void* stream) {
+    if (!bc_valid_head_dim(head_dim)) return BC_ERR_HEAD_DIM;
+    if (n_slots < 0 || pos < 0 || pos >= kv_stride) return BC_ERR_ARG;
+    if (residual_mode != BC_RES_NONE && residual_mode != BC_RES_FP32_SCALE && residual_mode != BC_RES_FP16_SCALE)
+        return BC_ERR_ARG;
+    if (n_slots == 0) return BC_OK;
+    if (!k || !v) return BC_ERR_ARG;
+    int rc = check_planes(K, residual_mode != BC_RES_NONE);
+    if (rc) return rc;
+    rc = check_planes(V, residual_mode != BC_RES_NONE);
+    if (rc) return rc;
+    cudaStream_t st = (cudaStream_t)stream;
+    const unsigned blocks = enc_blocks(2 * (int64_t)n_slots);
+    switch (residual_mode) {
+        case BC_RES_NONE:
+            BC_DISPATCH_NW(head_dim, (k_append_kv<NW, BC_RES_NONE><<<blocks, kEncWarps * 32, 0, st>>>(
+                                          (const __half*)k, (const __half*)v, K, V, n_slots, head_dim, kv_stride, pos)));
+            break;
+        case BC_RES_FP16_SCALE:
+            BC_DISPATCH_NW(head_dim, (k_append_kv<NW, BC_RES_FP16_SCALE><<<blocks, kEncWarps * 32, 0, st>>>(
+                                          (const __half*)k, (const __half*)v, K, V, n_slots, head_dim, kv_stride, pos)));
+            break;
+        default:
+            BC_DISPATCH_NW(head_dim, (k_append_kv<NW, BC_RES_FP32_SCALE><<<blocks, kEncWarps * 32, 0, st>>>(
+                                          (const __half*)k, (const __half*)v, K, V, n_slots, head_dim, kv_stride, pos)));
+            break;
+    }
+    BC_LAUNCH_CHECK();
+    return BC_OK;
+}
+
+int bc_records_to_planes(const void* binvec, const void* resvec, bc_kv_planes out, int64_t n_vecs, int head_dim,
+                         void* stream) {
+    if (!bc_valid_head_dim(head_dim)) return BC_ERR_HEAD_DIM;
+    if (n_vecs < 0) return BC_ERR_ARG;
+    if (n_vecs == 0) return BC_OK;
+    if (!binvec || !out.sign || !out.bscale) return BC_ERR_ARG;
+    if (resvec && (!out.nib || !out.rscale)) return BC_ERR_ARG;
+    cudaStream_t st = (cudaStream_t)stream;
+    BC_DISPATCH_NW(head_dim, (k_records_to_planes<NW><<<enc_blocks(n_vecs), kEncWarps * 32, 0, st>>>(
+                                  (const uint8_t*)binvec, (const uint8_t*)resvec, out, n_vecs)));
+    BC_LAUNCH_CHECK();
+    return BC_OK;
+}
+
+int bc_planes_to_records(bc_kv_planes in, void* binvec, void* resvec, int64_t n_vecs, int head_dim, void* stream) {
+    if (!bc_valid_head_dim(head_dim)) return BC_ERR_HEAD_DIM;
+    if (n_vecs < 0) return BC_ERR_ARG;
+    if (n_vecs == 0) return BC_OK;
+    if (!binvec || !in.sign || !in.bscale) return BC_ERR_ARG;
+    if (resvec && (!in.nib || !in.rscale)) return BC_ERR_ARG;
+    cudaStream_t st = (cudaStream_t)stream;
+    BC_DISPATCH_NW(head_dim, (k_planes_to_records<NW><<<enc_blocks(n_vecs), kEncWarps * 32, 0, st>>>(
+                                  in, (uint8_t*)binvec, (uint8_t*)resvec, n_vecs)));
+    BC_LAUNCH_CHECK();
+    return BC_OK;
+}
+
+}  // extern "C"

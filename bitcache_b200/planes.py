@@ -1,0 +1,197 @@
+"""Native plane-layout cache and the B200 decode-path operators on it.
+
+Layout (per K or V cache; include/bitcache_b200.h):
+    sign   uint32 [slots, kv_stride, head_dim/32]
+    nib    uint8  [slots, kv_stride, head_dim/2]    (compensated caches only)
+    bscale fp16   [slots, kv_stride]
+    rscale fp16   [slots, kv_stride]                (compensated caches only)
+kv_stride is the position capacity rounded up to a multiple of 8 so every
+per-slot row of the scale planes starts on a 16-byte boundary (the TMA bulk
+copies in the decode kernel need 16-byte aligned sources and sizes).
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+from . import _lib
+
+RES_NONE, RES_FP16_SCALE, RES_FP32_SCALE = _lib.BC_RES_NONE, _lib.BC_RES_FP16_SCALE, _lib.BC_RES_FP32_SCALE
+MODE_BINARY, MODE_COMPENSATED = _lib.BC_MODE_BINARY, _lib.BC_MODE_COMPENSATED
+
+
+def round_stride(max_seq: int) -> int:
+    return (max_seq + 7) // 8 * 8
+
+
+def vector_bytes(head_dim: int, compensated: bool = True) -> int:
+    """Stored bytes per K or V vector: 5d/8 + 4 (d/8 + 2 binary only)."""
+    return head_dim // 8 + 2 + ((head_dim // 2 + 2) if compensated else 0)
+
+
+@dataclass
+class Planes:
+    """One K or V plane cache."""
+
+    sign: torch.Tensor
+    bscale: torch.Tensor
+    nib: torch.Tensor | None
+    rscale: torch.Tensor | None
+    head_dim: int
+
+    @staticmethod
+    def empty(n_slots: int, kv_stride: int, head_dim: int, compensated: bool, device, zero: bool = True) -> "Planes":
+        assert kv_stride % 8 == 0, "kv_stride must be a multiple of 8"
+        mk = torch.zeros if zero else torch.empty
+        sign = mk((n_slots, kv_stride, head_dim // 32), dtype=torch.int32, device=device)
+        bscale = mk((n_slots, kv_stride), dtype=torch.float16, device=device)
+        nib = rscale = None
+        if compensated:
+            nib = mk((n_slots, kv_stride, head_dim // 2), dtype=torch.uint8, device=device)
+            rscale = mk((n_slots, kv_stride), dtype=torch.float16, device=device)
+        return Planes(sign, bscale, nib, rscale, head_dim)
+
+    @property
+    def n_slots(self) -> int:
+        return self.sign.shape[0]
+
+    @property
+    def kv_stride(self) -> int:
+        return self.sign.shape[1]
+
+    @property
+    def compensated(self) -> bool:
+        return self.nib is not None
+
+    def c(self) -> _lib.KVPlanes:
+        return _lib.KVPlanes(_lib.ptr(self.sign), _lib.ptr(self.nib), _lib.ptr(self.bscale), _lib.ptr(self.rscale))
+
+    def nbytes(self) -> int:
+        return sum(t.numel() * t.element_size() for t in (self.sign, self.bscale, self.nib, self.rscale)
+                   if t is not None)
+
+    def zero_(self) -> None:
+        for t in (self.sign, self.bscale, self.nib, self.rscale):
+            if t is not None:
+                t.zero_()
+
+
+def _stream(t: torch.Tensor) -> int:
+    return _lib.stream_of(t.device)
+
+
+def _check_half(x: torch.Tensor, name: str) -> None:
+    if not x.is_cuda:
+        raise RuntimeError(f"{name} must be a CUDA tensor")
+    if not x.is_contiguous():
+        raise RuntimeError(f"{name} must be contiguous")
+    if x.dtype != torch.float16:
+        raise RuntimeError(f"{name} must be float16")
+
+
+def encode_planes(src: torch.Tensor, out: Planes, residual_mode: int = RES_FP16_SCALE) -> None:
+    """Prefill: encode src fp16 [n_slots, seq_len, head_dim] into rows [slot, 0:seq_len] of out."""
+    _check_half(src, "src")
+    n_slots, seq_len, d = src.shape
+    lib = _lib.load()
+    _lib.check(lib.bc_encode_planes(src.data_ptr(), out.c(), n_slots, seq_len, out.kv_stride, d, residual_mode,
+                                    _stream(src)), "encode_planes")
+
+
+def append_kv(k: torch.Tensor, v: torch.Tensor, K: Planes, V: Planes, pos: int,
+              residual_mode: int = RES_FP32_SCALE) -> None:
+    """Decode-step append of one K and one V token per slot ([n_slots, head_dim]) at position pos."""
+    _check_half(k, "K")
+    _check_half(v, "V")
+    d = k.shape[-1]
+    n_slots = k.numel() // d
+    lib = _lib.load()
+    _lib.check(lib.bc_append_kv(k.data_ptr(), v.data_ptr(), K.c(), V.c(), n_slots, d, K.kv_stride, pos,
+                                residual_mode, _stream(k)), "append_kv")
+
+
+def decode_attention(q: torch.Tensor, K: Planes, V: Planes, seq_len: int, mode: int = MODE_COMPENSATED,
+                     out: torch.Tensor | None = None, partial: torch.Tensor | None = None,
+                     want_out: bool = True) -> torch.Tensor | None:
+    """Fused split-K decode attention.
+
+    q fp16 [n_slots * group, head_dim] (query head h reads KV slot h // group).
+    Returns out fp16 [n_heads, head_dim] (or None when want_out is False and a
+    partial buffer float32 [n_heads, head_dim + 2] is given)."""
+    _check_half(q, "Q")
+    d = q.shape[-1]
+    n_heads = q.numel() // d
+    n_slots = K.n_slots
+    group = n_heads // n_slots
+    if group * n_slots != n_heads:
+        raise RuntimeError("number of query heads must be a multiple of the number of KV slots")
+    if want_out and out is None:
+        out = torch.empty((n_heads, d), dtype=torch.float16, device=q.device)
+    lib = _lib.load()
+    st = _stream(q)
+    wsb = lib.bc_decode_workspace_bytes(n_slots, group, seq_len, d)
+    ws = _lib.workspace(q.device, st, wsb)
+    _lib.check(lib.bc_decode_attention(q.data_ptr(), K.c(), V.c(), _lib.ptr(out) if want_out else None,
+                                       _lib.ptr(partial), n_slots, group, seq_len, K.kv_stride, d, mode,
+                                       _lib.ptr(ws), ws.numel() if ws is not None else 0, st),
+               "decode_attention")
+    return out
+
+
+def lse_merge(parts: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Merge partial triples float32 [n_parts, n_heads, head_dim + 2] -> fp16 [n_heads, head_dim]."""
+    n_parts, n_heads, dp2 = parts.shape
+    d = dp2 - 2
+    parts = parts.contiguous()
+    if out is None:
+        out = torch.empty((n_heads, d), dtype=torch.float16, device=parts.device)
+    lib = _lib.load()
+    _lib.check(lib.bc_lse_merge(parts.data_ptr(), n_parts, n_heads, d, out.data_ptr(), _stream(parts)), "lse_merge")
+    return out
+
+
+def xnor_popcount(q: torch.Tensor, K: Planes, seq_len: int) -> torch.Tensor:
+    """Integer XNOR popcount of each query head against its slot's keys: int32 [n_heads, seq_len]."""
+    _check_half(q, "Q")
+    d = q.shape[-1]
+    n_heads = q.numel() // d
+    group = n_heads // K.n_slots
+    out = torch.empty((n_heads, seq_len), dtype=torch.int32, device=q.device)
+    lib = _lib.load()
+    _lib.check(lib.bc_xnor_popcount(q.data_ptr(), K.sign.data_ptr(), out.data_ptr(), K.n_slots, group, seq_len,
+                                    K.kv_stride, d, _stream(q)), "xnor_popcount")
+    return out
+
+
+def head_entropy(q: torch.Tensor, K: Planes, seq_len: int) -> torch.Tensor:
+    """Entropy of the binary-score softmax per head (query head h reads slot h)."""
+    _check_half(q, "Q")
+    d = q.shape[-1]
+    n_heads = q.numel() // d
+    out = torch.empty((n_heads,), dtype=torch.float32, device=q.device)
+    lib = _lib.load()
+    _lib.check(lib.bc_head_entropy_planes(q.data_ptr(), K.c(), out.data_ptr(), n_heads, seq_len, K.kv_stride, d,
+                                          _stream(q)), "head_entropy")
+    return out
+
+
+def records_to_planes(bin_blob: torch.Tensor, res_blob: torch.Tensor | None, n_vecs: int, head_dim: int) -> Planes:
+    """Reference BinaryVec/ResidualVec blobs (n_vecs records) -> flat planes [1, n_vecs_padded]."""
+    P = Planes.empty(1, round_stride(n_vecs), head_dim, res_blob is not None, bin_blob.device)
+    lib = _lib.load()
+    _lib.check(lib.bc_records_to_planes(bin_blob.data_ptr(), _lib.ptr(res_blob), P.c(), n_vecs, head_dim,
+                                        _stream(bin_blob)), "records_to_planes")
+    return P
+
+
+def planes_to_records(P: Planes, n_vecs: int) -> tuple[torch.Tensor, torch.Tensor | None]:
+    """Flat planes (first n_vecs rows of slot-major storage) -> reference record blobs."""
+    lib = _lib.load()
+    b = torch.empty(n_vecs * lib.bc_sizeof_binary_vec(), dtype=torch.uint8, device=P.sign.device)
+    r = None
+    if P.compensated:
+        r = torch.empty(n_vecs * lib.bc_sizeof_residual_vec(), dtype=torch.uint8, device=P.sign.device)
+    _lib.check(lib.bc_planes_to_records(P.c(), b.data_ptr(), _lib.ptr(r), n_vecs, P.head_dim, _stream(b)),
+               "planes_to_records")
+    return b, r

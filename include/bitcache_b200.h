@@ -1,0 +1,173 @@
+/*
+ * bitcache_b200 -- C ABI of the B200 (sm_100a) implementation of bitcache's
+ * quantized decode-attention path.
+ *
+ * Plain C: raw device pointers, sizes and a CUDA stream passed as void*
+ * (cudaStream_t; NULL = legacy default stream).  Every entry point returns an
+ * int status (BC_OK = 0).  Launches are asynchronous; none synchronises the
+ * host.  No entry point allocates memory unless its comment says so; ops that
+ * need scratch take a caller-provided workspace whose size is given by the
+ * matching *_workspace_bytes() query.  Workspaces must be zero-filled once
+ * when allocated; the kernels leave them zeroed again on completion.
+ *
+ * Two storage formats:
+ *  - reference records: arrays of the reference's BinaryVec (36 B) and
+ *    ResidualVec (130 B) structs, byte-compatible with anishesg/bitcache
+ *    (src/binary_encode.cuh:13-18, src/residual.cuh:11-16).  The bc_* ops
+ *    below that take "record" pointers are drop-ins for the reference
+ *    launchers named beside them.
+ *  - planes (native): per K or V cache, four 16-byte-aligned arrays indexed
+ *    [slot][position] with a row stride kv_stride (positions per slot):
+ *        sign   uint32 [slots][kv_stride][head_dim/32]   bit i%32 of word i/32 = (x_i >= 0)
+ *        nib    uint8  [slots][kv_stride][head_dim/2]    INT4 residual, element 2i low nibble
+ *        bscale fp16   [slots][kv_stride]                mean |x| (binary scale)
+ *        rscale fp16   [slots][kv_stride]                residual absmax
+ *    5*head_dim/8 + 4 bytes per vector (84 B at head_dim 128).  The field
+ *    values are bit-identical to the reference records; only the layout differs.
+ */
+#ifndef BITCACHE_B200_H
+#define BITCACHE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ---------------------------------------------------- */
+#define BC_OK 0
+#define BC_ERR_HEAD_DIM 1    /* head_dim not a multiple of 32 in [32, 256] */
+#define BC_ERR_ARG 2         /* negative/zero size, null pointer, bad mode */
+#define BC_ERR_ALIGN 3       /* pointer not 16-byte aligned, or kv_stride % 8 != 0 */
+#define BC_ERR_WORKSPACE 4   /* workspace smaller than the *_workspace_bytes() query */
+#define BC_ERR_UNSUPPORTED 5 /* shape outside the compiled kernel set (e.g. GQA group) */
+#define BC_ERR_TOO_LARGE 6   /* size exceeds a documented fixed maximum */
+#define BC_ERR_CUDA_BASE 1000 /* BC_ERR_CUDA_BASE + cudaError_t of a failed launch/call */
+
+/* device-side error bits, read with bc_get_device_error() */
+#define BC_DEVERR_TIMEOUT 1u /* a bounded wait in a kernel gave up; outputs are invalid */
+
+/* residual modes for the encoders */
+#define BC_RES_NONE 0       /* binary only: sign + bscale */
+#define BC_RES_FP16_SCALE 1 /* residual against the fp16-rounded scale (reference residual.cu:28) */
+#define BC_RES_FP32_SCALE 2 /* residual against the fp32 scale (reference online_encode.cu:74) */
+
+/* attention modes */
+#define BC_MODE_BINARY 0      /* xnor-popcount scores, sign*scale values (binary_attention.cu) */
+#define BC_MODE_COMPENSATED 1 /* + INT4 residual in scores and values (compensated_attention.cu) */
+
+const char* bc_status_string(int status);
+/* Reads (and when clear != 0 resets) the device error word of the current device.
+ * Synchronises the current device. */
+unsigned int bc_get_device_error(int clear);
+
+/* ====================================================================== */
+/* Reference-record operations (drop-ins for the reference launchers)     */
+/* ====================================================================== */
+
+/* sizeof(BinaryVec) = 36 and sizeof(ResidualVec) = 130, as
+ * sizeof_binary_vec / sizeof_residual_vec, reference torch_binding.cpp:165-166. */
+int64_t bc_sizeof_binary_vec(void);
+int64_t bc_sizeof_residual_vec(void);
+
+/* launch_binary_encode, reference binary_encode.cuh:26-32 / binary_encode.cu:62-80.
+ * src fp16 [n_vecs][head_dim] -> BinaryVec[n_vecs].  Unused words and padding are zeroed. */
+int bc_binary_encode(const void* src, void* out_binvec, int64_t n_vecs, int head_dim, void* stream);
+
+/* launch_residual_encode, reference residual.cuh:26-33 / residual.cu:80-98.
+ * The residual is taken against the binary record's stored (fp16) scale and sign bits. */
+int bc_residual_encode(const void* src, const void* binvec, void* out_resvec, int64_t n_vecs, int head_dim,
+                       void* stream);
+
+/* launch_online_encode_token, reference online_encode.cuh:15-25 / online_encode.cu:122-149.
+ * kv fp16 [batch*n_heads][head_dim] written at record slot*max_seq + current_len % max_seq.
+ * res_cache may be NULL (binary-only cache). */
+int bc_online_encode_token(const void* kv, void* bin_cache, void* res_cache, int batch, int n_heads,
+                           int head_dim, int current_len, int max_seq, void* stream);
+
+/* launch_binary_attention, reference binary_attention.cuh:15-25, and
+ * launch_compensated_attention, reference compensated_attention.cuh:16-28.
+ * q/out fp16 [batch*n_heads][head_dim]; records [batch*n_heads][seq_len].
+ * Unlike the reference kernels these guard batch*n_heads (no 32-row padding needed). */
+size_t bc_attention_workspace_bytes(int batch, int n_heads, int seq_len, int head_dim);
+int bc_binary_attention(const void* q, const void* k_bin, const void* v_bin, void* out, int batch, int n_heads,
+                        int seq_len, int head_dim, void* workspace, size_t workspace_bytes, void* stream);
+int bc_compensated_attention(const void* q, const void* k_bin, const void* k_res, const void* v_bin,
+                             const void* v_res, void* out, int batch, int n_heads, int seq_len, int head_dim,
+                             void* workspace, size_t workspace_bytes, void* stream);
+
+/* launch_compute_head_entropy, reference adaptive_precision.cuh:14-23:
+ * entropy of the softmax over binary scores (no 1/sqrt(d)) per (batch, head). */
+size_t bc_entropy_workspace_bytes(int batch, int n_heads, int seq_len);
+int bc_compute_head_entropy(const void* q, const void* k_bin, float* entropy, int batch, int n_heads,
+                            int seq_len, int head_dim, void* workspace, size_t workspace_bytes, void* stream);
+
+/* launch_adaptive_select, reference adaptive_precision.cuh:42-49:
+ * modes[i] = entropy[i] >= threshold ? 0 (BINARY) : 1 (COMPENSATED). */
+int bc_adaptive_select(const float* entropy, uint8_t* modes, int batch, int n_heads, float threshold,
+                       void* stream);
+
+/* ====================================================================== */
+/* Native plane layout                                                    */
+/* ====================================================================== */
+
+typedef struct bc_kv_planes {
+    void* sign;   /* uint32 [slots][kv_stride][head_dim/32] */
+    void* nib;    /* uint8  [slots][kv_stride][head_dim/2]  (NULL for binary-only caches) */
+    void* bscale; /* fp16   [slots][kv_stride] */
+    void* rscale; /* fp16   [slots][kv_stride]              (NULL for binary-only caches) */
+} bc_kv_planes;
+
+/* Prefill encode (binary_encode.cu + residual.cu, or online_encode.cu arithmetic with
+ * BC_RES_FP32_SCALE) of src fp16 [n_slots][seq_len][head_dim] into plane rows
+ * slot*kv_stride + s.  Nothing in the reference fuses these two passes. */
+int bc_encode_planes(const void* src, bc_kv_planes out, int n_slots, int seq_len, int64_t kv_stride,
+                     int head_dim, int residual_mode, void* stream);
+
+/* Decode-step append: online_encode.cu arithmetic (BC_RES_FP32_SCALE) or binary only, for
+ * one K and one V token per slot (k, v fp16 [n_slots][head_dim]) at plane position pos, in one
+ * launch.  The reference needs two launches (one per tensor, bitcache/__init__.py:104-111). */
+int bc_append_kv(const void* k, const void* v, bc_kv_planes K, bc_kv_planes V, int n_slots, int head_dim,
+                 int64_t kv_stride, int64_t pos, int residual_mode, void* stream);
+
+/* Fused split-K decode attention over plane caches (compensated_attention.cu:42-109 or
+ * binary_attention.cu:8-82 arithmetic) with grouped-query heads: query head
+ * slot*group + g reads KV slot `slot`, keys [0, seq_len).  q fp16 [n_slots*group][head_dim].
+ * Output: out fp16 [n_slots*group][head_dim] when out != NULL, and/or the per-head
+ * log-sum-exp partial triples when partial != NULL: partial[h*(head_dim+2) + {0: m, 1: l,
+ * 2..: o}] with m = max score (natural log units), l = sum exp(score - m),
+ * o = sum exp(score - m) * v (unnormalised); merge with bc_lse_merge.
+ * Requirements: kv_stride % 8 == 0, seq_len <= kv_stride, plane pointers 16-byte aligned,
+ * group in {1, 2, 4, 8}. */
+size_t bc_decode_workspace_bytes(int n_slots, int group, int seq_len, int head_dim);
+int bc_decode_attention(const void* q, bc_kv_planes K, bc_kv_planes V, void* out, float* partial, int n_slots,
+                        int group, int seq_len, int64_t kv_stride, int head_dim, int mode, void* workspace,
+                        size_t workspace_bytes, void* stream);
+
+/* Log-sum-exp merge of n_parts partial triples per head (the cross-GPU sequence split):
+ * parts[(p*n_heads + h)*(head_dim+2) + ...] as written by bc_decode_attention;
+ * out fp16 [n_heads][head_dim]. */
+int bc_lse_merge(const float* parts, int n_parts, int64_t n_heads, int head_dim, void* out, void* stream);
+
+/* Head entropy over a plane cache's binary scores (same arithmetic as
+ * bc_compute_head_entropy): entropy float [n_heads], query head h reads slot h. */
+int bc_head_entropy_planes(const void* q, bc_kv_planes K, float* entropy, int n_heads, int seq_len,
+                           int64_t kv_stride, int head_dim, void* stream);
+
+/* XNOR popcount scores sum_w popc(~(q_w ^ k_w)) (xnor_dot.cuh:20-27) of each query head
+ * against its slot's keys: out int32 [n_slots*group][seq_len]. */
+int bc_xnor_popcount(const void* q, const void* k_sign, int32_t* out, int n_slots, int group, int seq_len,
+                     int64_t kv_stride, int head_dim, void* stream);
+
+/* Layout converters between reference records and planes (n vectors, flat). */
+int bc_records_to_planes(const void* binvec, const void* resvec, bc_kv_planes out, int64_t n_vecs,
+                         int head_dim, void* stream);
+int bc_planes_to_records(bc_kv_planes in, void* binvec, void* resvec, int64_t n_vecs, int head_dim,
+                         void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* BITCACHE_B200_H */

@@ -1,0 +1,137 @@
+"""CPU: host-side logic -- workload generators, shard planning, the log-sum-exp
+merge, and the sequence-split step over gloo with world_size 2."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from bitcache_b200 import dist as bdist
+from bitcache_b200 import workloads
+from oracle import oracle as O
+
+
+def test_workloads_deterministic_and_shaped():
+    a = workloads.make("C1")
+    b = workloads.make("C1")
+    assert torch.equal(a.k, b.k) and torch.equal(a.q, b.q)
+    assert a.q.shape == (1, 8, 128) and a.k.shape == (1, 8, 1024, 128) and a.k.dtype == torch.float16
+    std = a.k.float().std().item()
+    assert abs(std - 1 / np.sqrt(128)) < 0.01
+    c2 = workloads.make("C2", seq_len=256)  # correlated keys present
+    qh = c2.q[0, 0].float()
+    corr = (c2.k[0, 0].float() @ qh) / (c2.k[0, 0].float().norm(dim=1) * qh.norm())
+    assert (corr > 0.1).sum() >= 16
+
+
+def test_c3_outlier_channels():
+    w = workloads.make("C3", seq_len=512, n_heads=2, n_kv_heads=2)
+    per_ch = w.k[0, 0].float().std(dim=0)
+    assert (per_ch > 4 / np.sqrt(128)).sum() == 2
+
+
+def test_c5_student_t_variance():
+    w = workloads.make("C5", batch=1, n_heads=2, n_kv_heads=2, seq_len=4096, head_dim=64)
+    var = w.k.float().var().item()
+    assert abs(var - 1 / 64) < 0.002
+
+
+@pytest.mark.parametrize("seq_len,world", [(65536, 8), (65536, 3), (1000, 4), (7, 2), (0, 2)])
+def test_seq_range_partition(seq_len, world):
+    rs = [bdist.seq_range(seq_len, world, r) for r in range(world)]
+    assert rs[0][0] == 0 and rs[-1][1] == seq_len
+    for (a, b), (c, _) in zip(rs, rs[1:]):
+        assert b == c
+    for a, _ in rs:
+        assert a % 8 == 0 or a == seq_len
+
+
+@pytest.mark.parametrize("n,world", [(32, 8), (33, 8), (5, 8), (128, 3)])
+def test_slot_range_partition(n, world):
+    rs = [bdist.slot_range(n, world, r) for r in range(world)]
+    assert rs[0][0] == 0 and rs[-1][1] == n
+    sizes = [b - a for a, b in rs]
+    assert max(sizes) - min(sizes) <= 1
+
+
+def _attn_partial_np(q, k, v):
+    """float64 partial triple (m, l, o) of exact attention of q [H, d] over k, v [H, S, d]."""
+    d = q.shape[-1]
+    s = np.einsum("hd,hsd->hs", q, k) / np.sqrt(d)
+    if s.shape[1] == 0:
+        return np.concatenate([np.full((q.shape[0], 1), -np.inf), np.zeros((q.shape[0], 1 + d))], 1)
+    m = s.max(1)
+    e = np.exp(s - m[:, None])
+    return np.concatenate([m[:, None], e.sum(1)[:, None], np.einsum("hs,hsd->hd", e, v)], 1)
+
+
+def test_lse_merge_equals_unsplit():
+    rng = np.random.default_rng(0)
+    H, S, d = 4, 1000, 64
+    q = rng.standard_normal((H, d))
+    k = rng.standard_normal((H, S, d))
+    v = rng.standard_normal((H, S, d))
+    full = _attn_partial_np(q, k, v)
+    want = full[:, 2:] / full[:, 1:2]
+    cuts = [0, 100, 101, 512, 1000, 1000]  # includes an empty part
+    parts = np.stack([_attn_partial_np(q, k[:, a:b], v[:, a:b]) for a, b in zip(cuts, cuts[1:])])
+    got = O.lse_merge(parts.astype(np.float32))
+    np.testing.assert_allclose(got, want, rtol=1e-4, atol=1e-5)
+    got_t = bdist.merge_partials_torch(torch.from_numpy(parts)).numpy()
+    np.testing.assert_allclose(got_t, want, rtol=1e-5, atol=1e-6)
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _seq_split_worker(rank, world, port, q, k, v, out_q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        S = k.shape[1]
+        a, b = bdist.seq_range(S, world, rank)
+
+        def local(qq):
+            return torch.from_numpy(_attn_partial_np(qq.numpy(), k[:, a:b], v[:, a:b]))
+
+        def gather(t):
+            lst = [torch.empty_like(t) for _ in range(world)]
+            dist.all_gather(lst, t)
+            return torch.stack(lst)
+
+        step = bdist.SeqSplitStep(local, gather, bdist.merge_partials_torch)
+        out = step(torch.from_numpy(q))
+        out_q.put((rank, out.numpy()))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_seq_split_gloo_world2():
+    rng = np.random.default_rng(1)
+    H, S, d = 3, 77, 32
+    q = rng.standard_normal((H, d))
+    k = rng.standard_normal((H, S, d))
+    v = rng.standard_normal((H, S, d))
+    full = _attn_partial_np(q, k, v)
+    want = full[:, 2:] / full[:, 1:2]
+    ctx = mp.get_context("spawn")
+    out_q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_seq_split_worker, args=(r, 2, port, q, k, v, out_q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(out_q.get(timeout=120) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for r in range(2):
+        np.testing.assert_allclose(res[r], want, rtol=1e-4, atol=1e-5)
