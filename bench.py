@@ -52,6 +52,8 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-ref-gpu", action="store_true")
     ap.add_argument("--cpu-sample-s", type=float, default=12.0)
+    ap.add_argument("--profile", action="store_true",
+                    help="small profiling run: one cache copy, only the decode kernel, warmup+steps launches")
     return ap.parse_args()
 
 
@@ -190,10 +192,40 @@ def run_reference(args):
 # ---------------------------------------------------------------------------
 # Our arm
 # ---------------------------------------------------------------------------
+def run_profile(args):
+    """Minimal run for ncu: one cache copy of the workload (> L2), fp16 inputs freed,
+    then warmup + steps launches of the decode kernel and nothing else."""
+    from bitcache_b200 import planes, workloads
+
+    dev = torch.device("cuda", 0)
+    comp = not args.binary
+    w = workloads.make(args.config, device=dev)
+    S, d, n = w.seq_len, w.head_dim, w.n_slots
+    K = planes.Planes.empty(n, planes.round_stride(S), d, comp, dev, zero=False)
+    V = planes.Planes.empty(n, planes.round_stride(S), d, comp, dev, zero=False)
+    rm = planes.RES_FP16_SCALE if comp else planes.RES_NONE
+    planes.encode_planes(w.k.reshape(n, S, d), K, rm)
+    planes.encode_planes(w.v.reshape(n, S, d), V, rm)
+    q = w.q.reshape(-1, d).contiguous()
+    del w
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+    mode = planes.MODE_COMPENSATED if comp else planes.MODE_BINARY
+    out = torch.empty((q.shape[0], d), dtype=torch.float16, device=dev)
+    for _ in range(args.warmup + args.steps):
+        planes.decode_attention(q, K, V, S, mode, out=out)
+    torch.cuda.synchronize()
+    print(json.dumps({"profile": args.config, "launches": args.warmup + args.steps,
+                      "bytes_per_launch": workloads.step_cache_bytes(1, n, S, d, comp)}))
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         run_reference(args)
+        return
+    if args.profile:
+        run_profile(args)
         return
 
     from bitcache_b200 import BitCache, _lib, planes, workloads

@@ -733,9 +733,12 @@ int run_decode_t(DecodeArgs a, bool records, void* ws, size_t ws_bytes, cudaStre
     if (p.n_splits > 1) {
         const size_t need = ws_bytes_for(a.n_slots, a.group, p.n_splits, D, p.n_hgroups);
         if (ws == nullptr || ws_bytes < need) return BC_ERR_WORKSPACE;
-        const size_t part = (size_t)a.n_slots * a.group * p.n_splits * (D + 2) * sizeof(float);
-        a.ws_part = reinterpret_cast<float*>(ws);
-        a.ws_cnt = reinterpret_cast<unsigned*>(reinterpret_cast<uint8_t*>(ws) + ((part + 255) & ~(size_t)255));
+        // Ticket counters first, at a fixed offset: calls of any shape find them
+        // zero (every completed call resets its own); partials follow and are
+        // always written before they are read.
+        const size_t cnt = (size_t)a.n_slots * p.n_hgroups * sizeof(unsigned);
+        a.ws_cnt = reinterpret_cast<unsigned*>(ws);
+        a.ws_part = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(ws) + ((cnt + 255) & ~(size_t)255));
     } else {
         a.ws_part = nullptr;
         a.ws_cnt = nullptr;

@@ -8,7 +8,10 @@
  * host.  No entry point allocates memory unless its comment says so; ops that
  * need scratch take a caller-provided workspace whose size is given by the
  * matching *_workspace_bytes() query.  Workspaces must be zero-filled once
- * when allocated; the kernels leave them zeroed again on completion.
+ * when allocated.  Their leading bytes hold ticket counters that every
+ * completed call returns to zero, so a workspace can be reused by later calls
+ * of any shape on the same stream; calls that overlap on the GPU must not share
+ * one.  After a BC_DEVERR_TIMEOUT the workspace must be zero-filled again.
  *
  * Two storage formats:
  *  - reference records: arrays of the reference's BinaryVec (36 B) and

@@ -276,8 +276,8 @@ def test_bitcache_prefill_then_decode(cuda):
     close(out.view(-1, w.head_dim), want.view(np.float16).astype(np.float32), "prefill+decode GQA")
 
 
-def test_workspace_left_zero_and_no_device_error(cuda):
+def test_workspace_counters_left_zero_and_no_device_error(cuda):
     torch.cuda.synchronize()
-    for t in _lib._ws.values():
-        assert not t.any(), "split-K workspace not returned to zero"
+    for t in _lib._ws.values():  # ticket counters lead the workspace
+        assert not t[:16384].any(), "split-K ticket counters not returned to zero"
     assert _lib.device_error() == 0

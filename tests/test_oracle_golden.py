@@ -32,8 +32,9 @@ def check_codes(got_nib, want_nib, pre, label):
         assert np.all(np.abs(a[bad] - b[bad]) == 1), f"{label}: code differs by more than 1"
         p = np.abs(pre.reshape(a.shape)[bad])
         dist_to_tie = np.abs(p - np.floor(p) - 0.5)
-        assert np.all(dist_to_tie < 1e-5 * np.maximum(1.0, p)), f"{label}: mismatch not at a rounding tie"
-        assert n_bad <= max(2, a.size // 100000), f"{label}: {n_bad} tie-adjacent mismatches"
+        # within ~2 ulp of the tie: explained by a 2-ulp difference in 7/absmax
+        assert np.all(dist_to_tie <= 3e-7 * np.maximum(1.0, p)), f"{label}: mismatch not at a rounding tie"
+        assert n_bad <= 2 + a.size // 10000, f"{label}: {n_bad} tie-adjacent mismatches"
     return n_bad
 
 
