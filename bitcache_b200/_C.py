@@ -95,7 +95,8 @@ def binary_attention(Q: torch.Tensor, K_bin: torch.Tensor, V_bin: torch.Tensor, 
     out = torch.empty_like(Q)
     lib = _lib.load()
     st = _stream(Q)
-    ws = _lib.workspace(Q.device, st, lib.bc_attention_workspace_bytes(batch, n_heads, seq_len, head_dim))
+    ws = _lib.workspace(Q.device, st, lib.bc_attention_workspace_bytes(batch, n_heads, seq_len, head_dim),
+                        ("records", batch * n_heads))
     _lib.check(lib.bc_binary_attention(Q.data_ptr(), K_bin.data_ptr(), V_bin.data_ptr(), out.data_ptr(), batch,
                                        n_heads, seq_len, head_dim, _lib.ptr(ws),
                                        ws.numel() if ws is not None else 0, st), "binary_attention")
@@ -115,7 +116,8 @@ def compensated_attention(Q: torch.Tensor, K_bin: torch.Tensor, K_res: torch.Ten
     out = torch.empty_like(Q)
     lib = _lib.load()
     st = _stream(Q)
-    ws = _lib.workspace(Q.device, st, lib.bc_attention_workspace_bytes(batch, n_heads, seq_len, head_dim))
+    ws = _lib.workspace(Q.device, st, lib.bc_attention_workspace_bytes(batch, n_heads, seq_len, head_dim),
+                        ("records", batch * n_heads))
     _lib.check(lib.bc_compensated_attention(Q.data_ptr(), K_bin.data_ptr(), K_res.data_ptr(), V_bin.data_ptr(),
                                             V_res.data_ptr(), out.data_ptr(), batch, n_heads, seq_len, head_dim,
                                             _lib.ptr(ws), ws.numel() if ws is not None else 0, st),
@@ -143,7 +145,7 @@ def compute_head_entropy(Q: torch.Tensor, K_bin: torch.Tensor, batch: int, n_hea
     ent = torch.empty((batch, n_heads), dtype=torch.float32, device=Q.device)
     lib = _lib.load()
     st = _stream(Q)
-    ws = _lib.workspace(Q.device, st, lib.bc_entropy_workspace_bytes(batch, n_heads, seq_len))
+    ws = _lib.workspace(Q.device, st, lib.bc_entropy_workspace_bytes(batch, n_heads, seq_len), ("entropy",))
     _lib.check(lib.bc_compute_head_entropy(Q.data_ptr(), K_bin.data_ptr(), ent.data_ptr(), batch, n_heads, seq_len,
                                            head_dim, _lib.ptr(ws), ws.numel() if ws is not None else 0, st),
                "compute_head_entropy")

@@ -114,16 +114,18 @@ def stream_of(device: torch.device) -> int:
     return torch.cuda.current_stream(device).cuda_stream
 
 
-# Per (device, stream) zero-filled workspace, grown on demand.  The kernels
-# return it to all-zero on completion, so it is reused across calls on the
-# same stream without clearing.
-_ws: dict[tuple[int, int], torch.Tensor] = {}
+# Zero-filled split-K workspaces, one per (device, stream, shape key).  The
+# kernels return their ticket counters to zero on completion, so a workspace
+# is reused without clearing by later calls of the same (n_slots, group) on
+# the same stream; a different shape gets its own buffer because its partials
+# could land on this shape's counters.
+_ws: dict[tuple, torch.Tensor] = {}
 
 
-def workspace(device: torch.device, stream: int, nbytes: int) -> torch.Tensor | None:
+def workspace(device: torch.device, stream: int, nbytes: int, shape_key: tuple = ()) -> torch.Tensor | None:
     if nbytes <= 0:
         return None
-    key = (device.index if device.index is not None else torch.cuda.current_device(), stream)
+    key = (device.index if device.index is not None else torch.cuda.current_device(), stream) + tuple(shape_key)
     t = _ws.get(key)
     if t is None or t.numel() < nbytes:
         t = torch.zeros(max(nbytes, 1 << 16), dtype=torch.uint8, device=device)

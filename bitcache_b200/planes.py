@@ -131,7 +131,7 @@ def decode_attention(q: torch.Tensor, K: Planes, V: Planes, seq_len: int, mode: 
     lib = _lib.load()
     st = _stream(q)
     wsb = lib.bc_decode_workspace_bytes(n_slots, group, seq_len, d)
-    ws = _lib.workspace(q.device, st, wsb)
+    ws = _lib.workspace(q.device, st, wsb, ("decode", n_slots, group))
     _lib.check(lib.bc_decode_attention(q.data_ptr(), K.c(), V.c(), _lib.ptr(out) if want_out else None,
                                        _lib.ptr(partial), n_slots, group, seq_len, K.kv_stride, d, mode,
                                        _lib.ptr(ws), ws.numel() if ws is not None else 0, st),

@@ -7,11 +7,12 @@
  * int status (BC_OK = 0).  Launches are asynchronous; none synchronises the
  * host.  No entry point allocates memory unless its comment says so; ops that
  * need scratch take a caller-provided workspace whose size is given by the
- * matching *_workspace_bytes() query.  Workspaces must be zero-filled once
- * when allocated.  Their leading bytes hold ticket counters that every
- * completed call returns to zero, so a workspace can be reused by later calls
- * of any shape on the same stream; calls that overlap on the GPU must not share
- * one.  After a BC_DEVERR_TIMEOUT the workspace must be zero-filled again.
+ * matching *_workspace_bytes() query.  A workspace holds one ticket counter
+ * per (slot, head group) followed by split partials; every completed call
+ * returns its counters to zero.  Zero-fill a workspace before its first use
+ * and again before using it with a different (n_slots, group) -- another
+ * shape's partials may overlap this shape's counters -- or after a
+ * BC_DEVERR_TIMEOUT.  Calls that overlap on the GPU must not share one.
  *
  * Two storage formats:
  *  - reference records: arrays of the reference's BinaryVec (36 B) and

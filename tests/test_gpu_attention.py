@@ -276,8 +276,20 @@ def test_bitcache_prefill_then_decode(cuda):
     close(out.view(-1, w.head_dim), want.view(np.float16).astype(np.float32), "prefill+decode GQA")
 
 
-def test_workspace_counters_left_zero_and_no_device_error(cuda):
+@pytest.mark.parametrize("slots,group", [(32, 1), (3, 4), (5, 8)])
+def test_workspace_counters_left_zero_and_no_device_error(cuda, slots, group):
+    d, S = 128, 2048
+    g = torch.Generator().manual_seed(slots)
+    K = planes.Planes.empty(slots, S, d, True, cuda)
+    V = planes.Planes.empty(slots, S, d, True, cuda)
+    planes.encode_planes((torch.randn(slots, S, d, generator=g) * 0.1).half().to(cuda), K)
+    planes.encode_planes((torch.randn(slots, S, d, generator=g) * 0.1).half().to(cuda), V)
+    q = (torch.randn(slots * group, d, generator=g) * 0.1).half().to(cuda)
+    first = planes.decode_attention(q, K, V, S)
+    for _ in range(3):  # reuse of the same workspace gives the same answer
+        assert torch.equal(planes.decode_attention(q, K, V, S), first)
     torch.cuda.synchronize()
-    for t in _lib._ws.values():  # ticket counters lead the workspace
-        assert not t[:16384].any(), "split-K ticket counters not returned to zero"
+    key = (cuda.index or 0, _lib.stream_of(cuda), "decode", slots, group)
+    n_cnt = slots * (1 if group == 1 else group // 2)
+    assert not _lib._ws[key][: 4 * n_cnt].any(), "split-K ticket counters not returned to zero"
     assert _lib.device_error() == 0
