@@ -31,6 +31,8 @@
 // (pattern * 2^-149); packed fma.rn.f32x2 with power-of-two-rescaled
 // coefficients turns them into exact multiples of 2^-64, and the constant
 // parts sum_s (a_s + 8 c_s) are subtracted once at the end.
+#include <mutex>
+
 #include "common.cuh"
 
 namespace bc {
@@ -887,6 +889,76 @@ int bc_xnor_popcount(const void* q, const void* k_sign, int32_t* out, int n_slot
                                                             group, seq_len, kv_stride, head_dim);
     BC_LAUNCH_CHECK();
     return BC_OK;
+}
+
+}  // extern "C"
+
+// ===========================================================================
+// Allocation-free decode attention.
+//
+// Some callers cannot allocate device memory at the point where they run
+// attention: an inference server that reserves all of its GPU memory up
+// front and forbids allocation in the decode loop, or a plugin whose host
+// framework owns every device buffer and hands it only inputs and outputs.
+// They get this one extra entry point.  Its split-K scratch (ticket counters
+// and partial results) lives in a fixed array inside the library instead of
+// a caller workspace; every GPU that loads the library holds the array until
+// the process exits.
+// ===========================================================================
+namespace {
+
+constexpr size_t kStaticScratchBytes = size_t(4) << 20;  // 4 MiB
+static __device__ __align__(256) unsigned char g_bc_static_scratch[kStaticScratchBytes];
+
+constexpr int kStaticMaxDevices = 64;
+std::mutex g_static_mu;
+void* g_static_scratch_addr[kStaticMaxDevices] = {};
+
+// Device address of the array on the current device.  In host code the
+// array's name is only a host-side stand-in, so the address is looked up once
+// per device (with that device current) and cached.
+int static_scratch_address(void** addr) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return BC_ERR_CUDA_BASE + (int)e;
+    if (dev < 0 || dev >= kStaticMaxDevices) return BC_ERR_UNSUPPORTED;
+    std::lock_guard<std::mutex> lock(g_static_mu);
+    if (g_static_scratch_addr[dev] == nullptr) {
+        void* p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_bc_static_scratch);
+        if (e != cudaSuccess) return BC_ERR_CUDA_BASE + (int)e;
+        g_static_scratch_addr[dev] = p;
+    }
+    *addr = g_static_scratch_addr[dev];
+    return BC_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+size_t bc_decode_noalloc_max_scratch_bytes(void) { return kStaticScratchBytes; }
+
+int bc_decode_attention_noalloc(const void* q, bc_kv_planes K, bc_kv_planes V, void* out, float* partial,
+                                int n_slots, int group, int seq_len, int64_t kv_stride, int head_dim, int mode,
+                                void* stream) {
+    if (n_slots > 0 && valid_group(group) && bc_valid_head_dim(head_dim) && seq_len >= 0 &&
+        bc_decode_workspace_bytes(n_slots, group, seq_len, head_dim) > kStaticScratchBytes)
+        return BC_ERR_TOO_LARGE;
+    if (n_slots <= 0 || !valid_group(group) || !bc_valid_head_dim(head_dim))
+        return bc_decode_attention(q, K, V, out, partial, n_slots, group, seq_len, kv_stride, head_dim, mode, nullptr,
+                                   0, stream);  // argument errors and empty calls, reported as usual
+    void* scratch = nullptr;
+    int rc = static_scratch_address(&scratch);
+    if (rc != BC_OK) return rc;
+    // The ticket counters must start at zero.  The array keeps the previous
+    // call's contents, and a previous call of another shape may have written
+    // partial results over this shape's counters, so they are cleared here.
+    const size_t counter_bytes = (size_t)n_slots * (group / heads_per_cta(group)) * sizeof(unsigned);
+    cudaError_t e = cudaMemsetAsync(scratch, 0, counter_bytes, (cudaStream_t)stream);
+    if (e != cudaSuccess) return BC_ERR_CUDA_BASE + (int)e;
+    return bc_decode_attention(q, K, V, out, partial, n_slots, group, seq_len, kv_stride, head_dim, mode, scratch,
+                               kStaticScratchBytes, stream);
 }
 
 }  // extern "C"

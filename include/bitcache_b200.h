@@ -149,6 +149,24 @@ int bc_decode_attention(const void* q, bc_kv_planes K, bc_kv_planes V, void* out
                         int group, int seq_len, int64_t kv_stride, int head_dim, int mode, void* workspace,
                         size_t workspace_bytes, void* stream);
 
+/* Allocation-free bc_decode_attention, for callers that cannot allocate
+ * device memory where they run attention (an engine that reserves all of its
+ * GPU memory at start-up and forbids allocation in the decode loop, or a
+ * plugin whose host framework owns every device buffer).  No counterpart in
+ * the reference (its launchers need no scratch).  Same arguments and results
+ * as bc_decode_attention without the workspace: the split-K scratch is a
+ * fixed array of bc_decode_noalloc_max_scratch_bytes() (4 MiB) inside the
+ * library, held by every GPU that loads it until the process exits.  Shapes
+ * whose bc_decode_workspace_bytes() exceeds that return BC_ERR_TOO_LARGE.
+ * The first call on a device looks up the array's device address (with that
+ * device current), so make it before any stream capture.  All calls on a
+ * device share the array: calls that overlap on the GPU (concurrent streams)
+ * race and must be serialised by the caller.  Calls nothing that allocates. */
+size_t bc_decode_noalloc_max_scratch_bytes(void);
+int bc_decode_attention_noalloc(const void* q, bc_kv_planes K, bc_kv_planes V, void* out, float* partial,
+                                int n_slots, int group, int seq_len, int64_t kv_stride, int head_dim, int mode,
+                                void* stream);
+
 /* Log-sum-exp merge of n_parts partial triples per head (the cross-GPU sequence split):
  * parts[(p*n_heads + h)*(head_dim+2) + ...] as written by bc_decode_attention;
  * out fp16 [n_heads][head_dim]. */
