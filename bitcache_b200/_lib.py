@@ -13,7 +13,8 @@ import threading
 import torch
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(HERE, "libbitcache_b200.so")
+# The in-tree build; BITCACHE_B200_LIB may name another build of the same library.
+LIB_PATH = os.environ.get("BITCACHE_B200_LIB") or os.path.join(HERE, "libbitcache_b200.so")
 
 BC_OK = 0
 BC_ERR_WORKSPACE = 4

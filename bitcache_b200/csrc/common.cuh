@@ -21,6 +21,19 @@ constexpr int kBinScaleOff = 32;
 constexpr int kResRecBytes = 130;
 constexpr int kResScaleOff = 128;
 
+// Nibble plane layout: offset-binary codes (each nibble holds code + 8, so
+// the reference's two's-complement byte XOR 0x88), interleaved in blocks of 8
+// positions.  Chunk c (16 bytes = 32 dims, element 2i in the low nibble of
+// byte i) of plane row p
+// lives at byte (p/8)*(8*d/2) + c*128 + (p%8)*16, so one block of 8 rows is
+// d/32 runs of 8 consecutive 16-byte chunks.  Tiles that start at a multiple
+// of 8 rows are still contiguous byte ranges, and both the key-per-lane and
+// the chunk-per-lane readers of the decode kernel hit distinct shared-memory
+// banks.
+__host__ __device__ __forceinline__ int64_t nib_chunk_offset(int64_t row, int c, int d) {
+    return (row >> 3) * (int64_t)(4 * d) + (int64_t)c * 128 + (row & 7) * 16;
+}
+
 // ---------------------------------------------------------------------------
 // Device-side error word.  Kernels never trap: a bounded wait that gives up
 // ORs a code into the error word (defined once, in decode.cu, whose kernels

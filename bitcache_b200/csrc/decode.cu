@@ -9,28 +9,31 @@
 //   out     = sum_s softmax(score)_s * (sign_v*scale_v + (n_v/7)*res_scale_v)
 // evaluated in one pass with an online softmax instead of the reference's two.
 //
-// Work decomposition.  A CTA of 256 threads owns one KV slot (batch, kv head),
-// a contiguous key range (its split) and GC query heads of that slot's group.
-// Tiles of T keys stream into a 4-stage shared-memory ring by 1-D TMA bulk
-// copies (cp.async.bulk, no multicast) completing on mbarriers.  Each thread
-// handles 32 consecutive dims of a key; QPK = d/32 threads form a key group
-// and KPAR = 256/QPK groups walk the tile.  Every key group keeps its own
-// online-softmax state; groups are merged once per CTA and splits once per
-// slot by the last CTA to finish (atomic ticket), so one launch produces the
-// final fp16 output.
+// Work decomposition.  A CTA of 4 warps owns one KV slot (batch, kv head), a
+// contiguous key range (its split) and GC query heads of that slot's group.
+// Tiles of 128 keys stream into a shared-memory ring by 1-D TMA bulk copies
+// (cp.async.bulk, no multicast) completing on "full" mbarriers; each warp
+// releases a stage through an "empty" mbarrier, so warps never meet at a
+// CTA-wide barrier inside the loop.  A warp owns 32 keys of every tile: in
+// the score phase each lane scores one key over the whole head, in the value
+// phase d/32 lanes share a key (32 dims each).  Each warp keeps one online
+// softmax state; warps are merged once per CTA and splits once per slot by
+// the last CTA to finish (atomic ticket), so one launch produces the final
+// fp16 output.
 //
 // Scores.  Sign agreement: d - 2*popc(q_sign ^ k_sign) over the head.  The
 // INT4 residual dot is exact integer arithmetic: each query element is
-// quantised once to 16 bits (q ~= Q16 * qmax/32767) split into hi/lo bytes,
-// nibbles are offset to unsigned (n+8) by one XOR and dotted with dp4a; the
-// offset is removed with a precomputed 8*sum(Q16).
+// quantised once to 16 bits (q ~= Q16 * qmax/32767) split into hi/lo bytes;
+// the plane stores codes offset-binary (u = n + 8), dotted with dp4a (odd
+// elements in place as 16u); the offset is removed with a precomputed
+// 8*sum(Q16).
 //
 // Values.  For key weight w: sign part 2*a*b - a with a = w*scale_v, residual
 // part c*(u - 8) with c = w*res_scale_v/7 and u = n+8.  Sign bits and nibbles
 // are masked in place and used directly as fp32 denormal operands
-// (pattern * 2^-149); packed fma.rn.f32x2 with power-of-two-rescaled
-// coefficients turns them into exact multiples of 2^-64, and the constant
-// parts sum_s (a_s + 8 c_s) are subtracted once at the end.
+// (pattern * 2^-149) of packed fma.rn.f32x2 with one coefficient per key;
+// each accumulator carries the fixed power-of-two scale of its bit position,
+// removed once per CTA together with the constant parts sum_s (a_s + 8 c_s).
 #include <mutex>
 
 #include "common.cuh"
@@ -39,20 +42,33 @@ namespace bc {
 
 __device__ unsigned int g_bc_device_error = 0;
 
-constexpr int kDecThreads = 256;
-constexpr int kStages = 4;
+// Tuning knobs (defaults are the measured best; see the design notes).
+#ifndef BC_DEC_STAGES
+#define BC_DEC_STAGES 2        // ring stages at head_dim <= 128 (2: 4 CTAs, 16 warps per SM)
+#endif
+#ifndef BC_DEC_QPACK_SMEM
+#define BC_DEC_QPACK_SMEM 1    // 1: the score phase reads the query packs from shared memory
+#endif
+#ifndef BC_DEC_V_HOIST
+#define BC_DEC_V_HOIST 0       // 1: the value phase loads all rounds' operands before computing
+#endif
+
+constexpr int kDecThreads = 128;  // 4 warps
+constexpr int kWarps = kDecThreads / 32;
+constexpr int kTile = 128;        // keys per tile: 32 per warp
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
-constexpr float kLazy = 8.0f;   // rescale only when the running max grows by > 2^8
-constexpr int kAccShift = 64;   // accumulators hold value * 2^-64
+constexpr float kLazy = 8.0f;     // rescale only when the running max grows by > 2^8
+constexpr int kAccShift = 64;     // accumulators hold value * 2^-64
 
 template <int D, int GC, bool COMP>
 struct DecCfg {
-    static constexpr int NWD = D / 32;            // sign words per key
-    static constexpr int QPK = NWD;               // threads per key (32 dims each)
-    static constexpr int KPAR = kDecThreads / QPK;
-    static constexpr int KPT = 2;                 // keys per group per tile
-    static constexpr int T = KPAR * KPT;          // keys per tile
+    static constexpr int NWD = D / 32;       // sign words (and 16-byte nibble chunks) per key
+    static constexpr int QPK = NWD;          // value-phase lanes per key (32 dims each)
+    static constexpr int KPW = 32 / QPK;     // value-phase keys in parallel per warp
+    static constexpr int NS = (D == 256) ? 2 : BC_DEC_STAGES;  // ring stages
+    static constexpr int LAG = 1;            // refill the stage consumed one tile ago
+    static constexpr int T = kTile;
     static constexpr int SIGN_B = T * D / 8;
     static constexpr int NIB_B = COMP ? T * D / 2 : 0;
     static constexpr int SC_B = T * 2;
@@ -65,18 +81,18 @@ struct DecCfg {
     static constexpr int OFF_VNIB = OFF_VBS + SC_B;
     static constexpr int OFF_VRS = OFF_VNIB + NIB_B;
     static constexpr int STAGE_B = OFF_VRS + (COMP ? SC_B : 0);
-    static constexpr int RING_B = kStages * STAGE_B;
-    // merge scratch (reuses the ring): [warps][GC][D+2] floats
-    static constexpr int MERGE_B = (kDecThreads / 32) * GC * (D + 2) * 4;
+    static constexpr int RING_B = NS * STAGE_B;
+    static constexpr int MERGE_B = kWarps * GC * (D + 2) * 4;  // reuses the ring after the main loop
     static constexpr int BODY_B = RING_B > MERGE_B ? RING_B : MERGE_B;
     static constexpr int QF_OFF = BODY_B;                       // float q[GC][D]
     static constexpr int Q16_OFF = QF_OFF + GC * D * 4;         // int Q16[GC][D]
     static constexpr int QSIGN_OFF = Q16_OFF + GC * D * 4;      // uint32 [GC][8]
-    static constexpr int QCONST_OFF = QSIGN_OFF + GC * 8 * 4;   // float bco, rco; int off8 -> [GC][4]
-    static constexpr int BAR_OFF = QCONST_OFF + GC * 4 * 4;
-    static constexpr int FLAG_OFF = BAR_OFF + kStages * 8;
-    static constexpr int SMEM_B = FLAG_OFF + 16 + 128;  // + slack for aligning the base to 128 B
-    static constexpr int MIN_BLOCKS = (GC == 1) ? 2 : 1;
+    static constexpr int QCONST_OFF = QSIGN_OFF + GC * 8 * 4;   // [GC][4]: bco, rco, off8
+    static constexpr int QPK_OFF = QCONST_OFF + GC * 4 * 4;     // uint32 [GC][D/8][4] query packs
+    static constexpr int FULL_OFF = QPK_OFF + (BC_DEC_QPACK_SMEM ? GC * (D / 8) * 16 : 0);  // mbarriers
+    static constexpr int EMPTY_OFF = FULL_OFF + NS * 8;         // mbarriers: all warps done with a stage
+    static constexpr int FLAG_OFF = EMPTY_OFF + NS * 8;         // abort flag
+    static constexpr int SMEM_B = FLAG_OFF + 16 + 128;          // + slack to align the base to 128 B
 };
 
 struct DecodeArgs {
@@ -91,27 +107,49 @@ struct DecodeArgs {
     int head_dim;
 };
 
-// Per-thread query state for GC heads.
-template <int GC>
+// Per-lane query state for GC heads.  The score phase handles whole keys, so
+// every lane holds the full query: sign words and, for the residual dot, q
+// quantised to 16 bits split into hi (signed) / lo (unsigned) bytes, packed
+// per nibble word as [even hi, even lo, odd hi, odd lo].
+template <int D, int GC>
 struct QState {
-    uint32_t sign[GC];
-    uint32_t pk[GC][4][4];  // [head][nibble word][even hi, even lo, odd hi, odd lo]
+    uint32_t sign[GC][D / 32];
+#if BC_DEC_QPACK_SMEM
+    const uint4* pk;  // shared memory, [GC][D/8]
+#else
+    uint32_t pk[GC][D / 8][4];
+#endif
     float bco[GC], rco[GC];
     int off8[GC];
 };
 
+// Value accumulators.  Pair p holds dims (p, p+16) of the lane's 32-dim
+// chunk.  Sign part: sum of 2a*b (a = w*scale_v) scaled by 2^(p-64), because
+// sign bit p enters as the denormal 2^(p-149) and the coefficient is the
+// same 2a*2^85 for every p.  Residual part: sum of c*u (c = w*res_scale_v/7,
+// u = code + 8) scaled by 2^(4(p%4)-64), the nibble's in-register position.
+// Keeping the two parts apart lets every FFMA2 of a key share one
+// coefficient; the fixed scales are removed once per CTA.
 template <int GC>
 struct SoftState {
-    float m[GC], l[GC], t[GC];
-    f2 acc[GC][4][4];  // [head][nibble word w][j] -> dims (8w+j, 8w+4+j) of the thread's 32
+    float m[GC];         // running max (log2 units), uniform across the warp
+    float l[GC], t[GC];  // per lane: sum of weights and sum of (a + 8c) of the lane's own keys
+    f2 acc_s[GC][16];
+    f2 acc_n[GC][16];
 };
+
+__device__ __forceinline__ uint8_t* aligned_smem(uint8_t* raw) {
+    return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(raw) + 127) & ~uintptr_t(127));
+}
 
 // ---------------------------------------------------------------------------
 // Query preparation (once per CTA).  scale_q is summed sequentially over the
-// head as in compensated_attention.cu:65-67.
+// head as in compensated_attention.cu:65-67.  The residual dot uses q
+// quantised against the head's max |q|: q_i ~= Q16_i * qmax / 32767.
 // ---------------------------------------------------------------------------
 template <int D, int GC, bool COMP, typename Cfg>
-__device__ __forceinline__ void prepare_query(const DecodeArgs& a, int slot, int hg, uint8_t* smem, QState<GC>& qs) {
+__device__ __forceinline__ void prepare_query(const DecodeArgs& a, int slot, int hg, uint8_t* smem,
+                                              QState<D, GC>& qs) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     float* qf = reinterpret_cast<float*>(smem + Cfg::QF_OFF);
     int* q16 = reinterpret_cast<int*>(smem + Cfg::Q16_OFF);
@@ -151,21 +189,38 @@ __device__ __forceinline__ void prepare_query(const DecodeArgs& a, int slot, int
         }
     }
     __syncthreads();
-    const int qt = tid % Cfg::QPK;
 #pragma unroll
     for (int g = 0; g < GC; ++g) {
-        qs.sign[g] = qsign[g * 8 + qt];
+#pragma unroll
+        for (int k = 0; k < D / 32; ++k) qs.sign[g][k] = qsign[g * 8 + k];
         qs.bco[g] = qc[g * 4 + 0];
         qs.rco[g] = qc[g * 4 + 1];
         qs.off8[g] = reinterpret_cast<const int*>(qc)[g * 4 + 2];
+#if BC_DEC_QPACK_SMEM
+        qs.pk = reinterpret_cast<const uint4*>(smem + Cfg::QPK_OFF);
         if (COMP) {
-#pragma unroll
-            for (int w = 0; w < 4; ++w) {
+            uint4* dst = reinterpret_cast<uint4*>(smem + Cfg::QPK_OFF);
+            for (int w = threadIdx.x; w < D / 8; w += kDecThreads) {
                 uint32_t eh = 0, el = 0, oh = 0, ol = 0;
 #pragma unroll
                 for (int b = 0; b < 4; ++b) {
-                    const int de = g * D + 32 * qt + 8 * w + 2 * b;
-                    const int ve = q16[de], vo = q16[de + 1];
+                    const int ve = q16[g * D + 8 * w + 2 * b], vo = q16[g * D + 8 * w + 2 * b + 1];
+                    eh |= ((uint32_t)(ve >> 8) & 0xFFu) << (8 * b);
+                    el |= ((uint32_t)ve & 0xFFu) << (8 * b);
+                    oh |= ((uint32_t)(vo >> 8) & 0xFFu) << (8 * b);
+                    ol |= ((uint32_t)vo & 0xFFu) << (8 * b);
+                }
+                dst[g * (D / 8) + w] = make_uint4(eh, el, oh, ol);
+            }
+        }
+#else
+        if (COMP) {
+#pragma unroll
+            for (int w = 0; w < D / 8; ++w) {
+                uint32_t eh = 0, el = 0, oh = 0, ol = 0;
+#pragma unroll
+                for (int b = 0; b < 4; ++b) {
+                    const int ve = q16[g * D + 8 * w + 2 * b], vo = q16[g * D + 8 * w + 2 * b + 1];
                     eh |= ((uint32_t)(ve >> 8) & 0xFFu) << (8 * b);
                     el |= ((uint32_t)ve & 0xFFu) << (8 * b);
                     oh |= ((uint32_t)(vo >> 8) & 0xFFu) << (8 * b);
@@ -177,170 +232,254 @@ __device__ __forceinline__ void prepare_query(const DecodeArgs& a, int slot, int
                 qs.pk[g][w][3] = ol;
             }
         }
+#endif
+    }
+#if BC_DEC_QPACK_SMEM
+    __syncthreads();
+#endif
+}
+
+template <int GC>
+__device__ __forceinline__ void init_soft(SoftState<GC>& st) {
+#pragma unroll
+    for (int g = 0; g < GC; ++g) {
+        st.m[g] = -INFINITY;
+        st.l[g] = 0.0f;
+        st.t[g] = 0.0f;
+#pragma unroll
+        for (int p = 0; p < 16; ++p) {
+            st.acc_s[g][p] = f2{0.0f, 0.0f};
+            st.acc_n[g][p] = f2{0.0f, 0.0f};
+        }
     }
 }
 
 // ---------------------------------------------------------------------------
-// One key: score for the GC heads (integer parts reduced across the QPK
-// threads of the group), online softmax update, V accumulation for 32 dims.
+// One warp consumes its 32 keys of a tile held in shared memory (canonical
+// layout: sign rows, bscale, interleaved offset-binary nibbles, rscale; K then V).
+//  1. score phase: lane `lane` scores key `kw + lane` for the GC heads;
+//  2. lazy rescale of the warp's running max (vote, then a warp max only when
+//     some score exceeds the max by more than 2^8);
+//  3. value phase: d/32 lanes per key accumulate 32 dims each (consecutive
+//     lanes take consecutive keys, so the interleaved nibble reads are
+//     bank-conflict free), receiving the key's weight coefficients from its
+//     score lane by shuffle.
+// Nibbles are stored offset-binary (u = code + 8), so no XOR is needed here.
 // ---------------------------------------------------------------------------
-template <int D, int GC, bool COMP>
-__device__ __forceinline__ void consume_key(const QState<GC>& qs, SoftState<GC>& st, bool valid, uint32_t ks, float kbs,
-                                            uint4 kn, float krs, uint32_t vs, float vbs, uint4 vn, float vrs) {
-    constexpr int QPK = D / 32;
-    float w_g[GC];
+template <int D, int GC, bool COMP, typename Cfg>
+__device__ __forceinline__ void consume_warp_tile(const QState<D, GC>& qs, SoftState<GC>& st, const uint8_t* sb,
+                                                  int kw, int nk) {
+    constexpr int NWD = Cfg::NWD, QPK = Cfg::QPK, KPW = Cfg::KPW;
+    const int lane = threadIdx.x & 31;
+    const int kk = kw + lane;
+    const bool valid = kk < nk;
+    // ---- score phase -------------------------------------------------------
+    uint32_t ks[NWD];
+    {
+        const uint32_t* row = reinterpret_cast<const uint32_t*>(sb + Cfg::OFF_KSIGN) + kk * NWD;
+        if constexpr (NWD % 4 == 0) {
 #pragma unroll
-    for (int g = 0; g < GC; ++g) {
-        int pop = __popc(qs.sign[g] ^ ks);
-        int dot = 0;
-        if (COMP) {
-            int hi = 0, lo = 0;
-            const uint32_t nk[4] = {kn.x, kn.y, kn.z, kn.w};
+            for (int c = 0; c < NWD / 4; ++c) {
+                const uint4 v = reinterpret_cast<const uint4*>(row)[c];
+                ks[4 * c] = v.x; ks[4 * c + 1] = v.y; ks[4 * c + 2] = v.z; ks[4 * c + 3] = v.w;
+            }
+        } else if constexpr (NWD == 2) {
+            const uint2 v = *reinterpret_cast<const uint2*>(row);
+            ks[0] = v.x; ks[1] = v.y;
+        } else {
+            ks[0] = row[0];
+        }
+    }
+    const float kbs = __half2float(reinterpret_cast<const __half*>(sb + Cfg::OFF_KBS)[kk]);
+    int dot[GC];
+    float krs = 0.0f;
+    if (COMP) {
+        krs = __half2float(reinterpret_cast<const __half*>(sb + Cfg::OFF_KRS)[kk]);
+        int eh[GC], el[GC], oh[GC], ol[GC];
+#pragma unroll
+        for (int g = 0; g < GC; ++g) eh[g] = el[g] = oh[g] = ol[g] = 0;
+#pragma unroll
+        for (int c = 0; c < NWD; ++c) {
+            const uint4 ch = *reinterpret_cast<const uint4*>(sb + Cfg::OFF_KNIB + nib_chunk_offset(kk, c, D));
+            const uint32_t wds[4] = {ch.x, ch.y, ch.z, ch.w};
 #pragma unroll
             for (int w = 0; w < 4; ++w) {
-                const uint32_t nx = nk[w] ^ 0x88888888u;
-                const uint32_t ue = nx & 0x0F0F0F0Fu;
-                const uint32_t uo = (nx >> 4) & 0x0F0F0F0Fu;
-                hi = dp4a_us(ue, qs.pk[g][w][0], hi);
-                lo = dp4a_uu(ue, qs.pk[g][w][1], lo);
-                hi = dp4a_us(uo, qs.pk[g][w][2], hi);
-                lo = dp4a_uu(uo, qs.pk[g][w][3], lo);
+                const uint32_t ue = wds[w] & 0x0F0F0F0Fu;    // even elements, u
+                const uint32_t uo16 = wds[w] & 0xF0F0F0F0u;  // odd elements, 16u
+#pragma unroll
+                for (int g = 0; g < GC; ++g) {
+#if BC_DEC_QPACK_SMEM
+                    const uint4 pv = qs.pk[g * (D / 8) + 4 * c + w];
+                    const uint32_t pk[4] = {pv.x, pv.y, pv.z, pv.w};
+#else
+                    const uint32_t* pk = qs.pk[g][4 * c + w];
+#endif
+                    eh[g] = dp4a_us(ue, pk[0], eh[g]);
+                    el[g] = dp4a_uu(ue, pk[1], el[g]);
+                    oh[g] = dp4a_us(uo16, pk[2], oh[g]);
+                    ol[g] = dp4a_uu(uo16, pk[3], ol[g]);
+                }
             }
-            dot = hi * 256 + lo;
         }
 #pragma unroll
-        for (int off = 1; off < QPK; off <<= 1) {
-            pop += __shfl_xor_sync(0xffffffffu, pop, off);
-            if (COMP) dot += __shfl_xor_sync(0xffffffffu, dot, off);
-        }
-        // Shuffles above run on every lane; everything below is per key group and
-        // skipped for keys past the end of the range.
-        float s2 = qs.bco[g] * kbs * (float)(D - 2 * pop);
-        if (COMP) s2 = fmaf(qs.rco[g] * krs, (float)(dot - qs.off8[g]), s2);
-        if (!valid) s2 = -INFINITY;
-        if (s2 > st.m[g] + kLazy) {
-            const float alpha = fast_exp2(st.m[g] - s2);
-            st.m[g] = s2;
+        for (int g = 0; g < GC; ++g) dot[g] = eh[g] * 256 + el[g] + ((oh[g] * 256 + ol[g]) >> 4);
+    }
+    float s2[GC];
+#pragma unroll
+    for (int g = 0; g < GC; ++g) {
+        int pop = 0;
+#pragma unroll
+        for (int k = 0; k < NWD; ++k) pop += __popc(qs.sign[g][k] ^ ks[k]);
+        float s = qs.bco[g] * kbs * (float)(D - 2 * pop);
+        if (COMP) s = fmaf(qs.rco[g] * krs, (float)(dot[g] - qs.off8[g]), s);
+        s2[g] = valid ? s : -INFINITY;
+    }
+    // ---- lazy rescale, weights -------------------------------------------------
+    const float vbs = valid ? __half2float(reinterpret_cast<const __half*>(sb + Cfg::OFF_VBS)[kk]) : 0.0f;
+    const float vrs = (COMP && valid) ? __half2float(reinterpret_cast<const __half*>(sb + Cfg::OFF_VRS)[kk]) : 0.0f;
+    float A0[GC], C0[GC];
+#pragma unroll
+    for (int g = 0; g < GC; ++g) {
+        if (__any_sync(0xffffffffu, s2[g] > st.m[g] + kLazy)) {  // warp-uniform, rare after the first tile
+            float M = s2[g];
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+            const float alpha = fast_exp2(st.m[g] - M);
+            st.m[g] = M;
             st.l[g] *= alpha;
             st.t[g] *= alpha;
             const f2 al = {alpha, alpha};
 #pragma unroll
-            for (int w = 0; w < 4; ++w)
-#pragma unroll
-                for (int j = 0; j < 4; ++j) fmul2(st.acc[g][w][j], al);
+            for (int p = 0; p < 16; ++p) {
+                fmul2(st.acc_s[g][p], al);
+                if (COMP) fmul2(st.acc_n[g][p], al);
+            }
         }
-        const float wt = valid ? fast_exp2(s2 - st.m[g]) : 0.0f;
+        const float wt = valid ? fast_exp2(s2[g] - st.m[g]) : 0.0f;
         st.l[g] += wt;
-        w_g[g] = wt;
-    }
-    if (!valid) return;
-    // V accumulation
-    const uint32_t nv[4] = {vn.x, vn.y, vn.z, vn.w};
-#pragma unroll
-    for (int g = 0; g < GC; ++g) {
-        const float av = w_g[g] * vbs;
-        const float A0 = 2.0f * av * exp2i(149 - kAccShift);
-        float C0 = 0.0f;
+        const float av = wt * vbs;
+        A0[g] = 2.0f * av * exp2i(149 - kAccShift);
         if (COMP) {
-            const float cv = w_g[g] * vrs * (1.0f / 7.0f);
-            C0 = cv * exp2i(149 - kAccShift);
+            const float cv = wt * vrs * (1.0f / 7.0f);
+            C0[g] = cv * exp2i(149 - kAccShift);
             st.t[g] += av + 8.0f * cv;
         } else {
+            C0[g] = 0.0f;
             st.t[g] += av;
         }
+    }
+    // ---- value phase -----------------------------------------------------------
+    const int grp = lane % KPW, qt = lane / KPW;
+#if BC_DEC_V_HOIST
+    uint32_t vs_all[QPK];
+    uint4 vn_all[QPK];
 #pragma unroll
-        for (int w = 0; w < 4; ++w) {
-            const uint32_t sw = vs >> (8 * w);
-            const uint32_t sw4 = vs >> (8 * w + 4);
+    for (int r = 0; r < QPK; ++r) {
+        const int kv = kw + grp + r * KPW;
+        vs_all[r] = reinterpret_cast<const uint32_t*>(sb + Cfg::OFF_VSIGN)[kv * NWD + qt];
+        vn_all[r] = COMP ? *reinterpret_cast<const uint4*>(sb + Cfg::OFF_VNIB + nib_chunk_offset(kv, qt, D))
+                         : make_uint4(0, 0, 0, 0);
+    }
+#endif
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const float Aj = A0 * exp2i(-j);
-                const f2 y = {bits_f(sw & (1u << j)), bits_f(sw4 & (1u << j))};
-                ffma2(st.acc[g][w][j], f2{Aj, Aj}, y);
-            }
-            if (COMP) {
-                const uint32_t nx = nv[w] ^ 0x88888888u;
-                const uint32_t nh = nx >> 16;
+    for (int r = 0; r < QPK; ++r) {
+        const int src = grp + r * KPW;
+#if BC_DEC_V_HOIST
+        const uint32_t vs = vs_all[r];
+#else
+        const int kv = kw + src;
+        const uint32_t vs = reinterpret_cast<const uint32_t*>(sb + Cfg::OFF_VSIGN)[kv * NWD + qt];
+#endif
+        const uint32_t vs_hi = vs >> 16;
+        uint32_t nw[4] = {0, 0, 0, 0}, nh[4] = {0, 0, 0, 0};
+        if (COMP) {
+#if BC_DEC_V_HOIST
+            const uint4 vn = vn_all[r];
+#else
+            const uint4 vn = *reinterpret_cast<const uint4*>(sb + Cfg::OFF_VNIB + nib_chunk_offset(kv, qt, D));
+#endif
+            nw[0] = vn.x; nw[1] = vn.y; nw[2] = vn.z; nw[3] = vn.w;
 #pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    const float Cj = C0 * exp2i(-4 * j);
-                    const f2 x = {bits_f(nx & (0xFu << (4 * j))), bits_f(nh & (0xFu << (4 * j)))};
-                    ffma2(st.acc[g][w][j], f2{Cj, Cj}, x);
+            for (int k = 0; k < 4; ++k) nh[k] = nw[k] >> 16;
+        }
+#pragma unroll
+        for (int g = 0; g < GC; ++g) {
+            const float a0 = __shfl_sync(0xffffffffu, A0[g], src);
+            const float c0 = COMP ? __shfl_sync(0xffffffffu, C0[g], src) : 0.0f;
+            const f2 a2 = {a0, a0}, c2 = {c0, c0};
+#pragma unroll
+            for (int p = 0; p < 16; ++p) {
+                // sign bits of dims p and p+16, each the exact denormal 2^(p-149)
+                const f2 y = {bits_f(vs & (1u << p)), bits_f(vs_hi & (1u << p))};
+                ffma2(st.acc_s[g][p], a2, y);
+                if (COMP) {
+                    // codes of dims p (word p/8) and p+16 (word 2 + p/8), nibble p%8:
+                    // nibbles 0-3 from the word, 4-7 from its upper half
+                    const int t = p & 7, kw0 = p >> 3;
+                    const uint32_t srca = (t < 4) ? nw[kw0] : nh[kw0];
+                    const uint32_t srcb = (t < 4) ? nw[2 + kw0] : nh[2 + kw0];
+                    const int sh = 4 * (t & 3);
+                    const f2 x = {bits_f(srca & (0xFu << sh)), bits_f(srcb & (0xFu << sh))};
+                    ffma2(st.acc_n[g][p], c2, x);
                 }
             }
         }
     }
 }
 
-// Convert accumulator pair (w, j) to true unnormalised value of dims (8w+j, 8w+4+j).
-__device__ __forceinline__ float acc_true(float acc_scaled, float t) { return acc_scaled * exp2i(kAccShift) - t; }
-
 // ---------------------------------------------------------------------------
-// Merge all key groups of the CTA, then (split-K) publish a partial and let the
-// last CTA of the slot combine and write the outputs.
+// End of a CTA: reduce each warp, merge the warps (log-sum-exp), then either
+// write the outputs (single split) or publish a partial and let the last CTA
+// of the (slot, head group) combine all splits.
 // ---------------------------------------------------------------------------
 template <int D, int GC, typename Cfg>
 __device__ __forceinline__ void finish_cta(const DecodeArgs& a, int slot, int hg, int split, uint8_t* smem,
                                            SoftState<GC>& st) {
-    constexpr int QPK = Cfg::QPK;
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, qt = tid % QPK;
-    // per-thread true values for its 32 dims, ordered by dim
-    float o[GC][32];
-#pragma unroll
-    for (int g = 0; g < GC; ++g)
-#pragma unroll
-        for (int w = 0; w < 4; ++w)
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                o[g][8 * w + j] = acc_true(st.acc[g][w][j].x, st.t[g]);
-                o[g][8 * w + 4 + j] = acc_true(st.acc[g][w][j].y, st.t[g]);
-            }
-    // warp-level merge across key groups (lanes differing in bits >= log2(QPK))
-#pragma unroll
-    for (int off = QPK; off < 32; off <<= 1) {
-#pragma unroll
-        for (int g = 0; g < GC; ++g) {
-            const float mp = __shfl_xor_sync(0xffffffffu, st.m[g], off);
-            const float lp = __shfl_xor_sync(0xffffffffu, st.l[g], off);
-            const float M = fmaxf(st.m[g], mp);
-            const float fa = (st.m[g] == -INFINITY) ? 0.0f : fast_exp2(st.m[g] - M);
-            const float fb = (mp == -INFINITY) ? 0.0f : fast_exp2(mp - M);
-            st.l[g] = st.l[g] * fa + lp * fb;
-            st.m[g] = M;
-#pragma unroll
-            for (int i = 0; i < 32; ++i) {
-                const float op = __shfl_xor_sync(0xffffffffu, o[g][i], off);
-                o[g][i] = o[g][i] * fa + op * fb;
-            }
-        }
-    }
+    constexpr int KPW = Cfg::KPW;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, qt = lane / KPW;
     __syncthreads();  // ring no longer in use
     float* mg = reinterpret_cast<float*>(smem);  // [warps][GC][D+2]
-    if (lane < QPK) {
 #pragma unroll
-        for (int g = 0; g < GC; ++g) {
-            float* rec = mg + ((size_t)warp * GC + g) * (D + 2);
-            if (lane == 0) {
-                rec[0] = st.m[g];
-                rec[1] = st.l[g];
-            }
+    for (int g = 0; g < GC; ++g) {
+        float l = st.l[g], t = st.t[g];
 #pragma unroll
-            for (int i = 0; i < 32; ++i) rec[2 + 32 * qt + i] = o[g][i];
+        for (int off = 16; off > 0; off >>= 1) {
+            l += __shfl_xor_sync(0xffffffffu, l, off);
+            t += __shfl_xor_sync(0xffffffffu, t, off);
+        }
+        float o[32];
+#pragma unroll
+        for (int p = 0; p < 16; ++p) {
+            const float fs = exp2i(kAccShift - p), fn = exp2i(kAccShift - 4 * (p & 3));
+            o[p] = st.acc_s[g][p].x * fs + st.acc_n[g][p].x * fn;
+            o[p + 16] = st.acc_s[g][p].y * fs + st.acc_n[g][p].y * fn;
+        }
+        // lanes holding the same chunk (same qt) differ in their low log2(KPW) bits
+#pragma unroll
+        for (int off = 1; off < KPW; off <<= 1)
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] += __shfl_xor_sync(0xffffffffu, o[i], off);
+        float* rec = mg + ((size_t)warp * GC + g) * (D + 2);
+        if (lane % KPW == 0) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) rec[2 + 32 * qt + i] = o[i] - t;
+        }
+        if (lane == 0) {
+            rec[0] = st.m[g];
+            rec[1] = l;
         }
     }
     __syncthreads();
-    constexpr int NWARP = kDecThreads / 32;
-    // cross-warp merge: thread handles (g, dim)
     const bool single = (a.n_splits == 1);
     const int64_t head0 = (int64_t)slot * a.group + (int64_t)hg * GC;
     for (int idx = tid; idx < GC * D; idx += kDecThreads) {
         const int g = idx / D, i = idx % D;
         float M = -INFINITY;
 #pragma unroll
-        for (int w = 0; w < NWARP; ++w) M = fmaxf(M, mg[((size_t)w * GC + g) * (D + 2)]);
+        for (int w = 0; w < kWarps; ++w) M = fmaxf(M, mg[((size_t)w * GC + g) * (D + 2)]);
         float L = 0.0f, O = 0.0f;
 #pragma unroll
-        for (int w = 0; w < NWARP; ++w) {
+        for (int w = 0; w < kWarps; ++w) {
             const float* rec = mg + ((size_t)w * GC + g) * (D + 2);
             const float f = (rec[0] == -INFINITY) ? 0.0f : fast_exp2(rec[0] - M);
             L += rec[1] * f;
@@ -367,7 +506,6 @@ __device__ __forceinline__ void finish_cta(const DecodeArgs& a, int slot, int hg
         }
     }
     if (single) return;
-    // ticket: the last CTA of this (slot, head group) combines the splits
     __shared__ unsigned s_last;
     __syncthreads();
     if (tid == 0) {
@@ -401,195 +539,183 @@ __device__ __forceinline__ void finish_cta(const DecodeArgs& a, int slot, int hg
             p[2 + i] = O;
         }
     }
-    if (tid == 0) a.ws_cnt[(int64_t)slot * a.n_hgroups + hg] = 0u;  // leave the workspace zeroed
+    if (tid == 0) a.ws_cnt[(int64_t)slot * a.n_hgroups + hg] = 0u;  // leave the counter zeroed
 }
 
-template <int GC>
-__device__ __forceinline__ void init_soft(SoftState<GC>& st) {
-#pragma unroll
-    for (int g = 0; g < GC; ++g) {
-        st.m[g] = -INFINITY;
-        st.l[g] = 0.0f;
-        st.t[g] = 0.0f;
-#pragma unroll
-        for (int w = 0; w < 4; ++w)
-#pragma unroll
-            for (int j = 0; j < 4; ++j) st.acc[g][w][j] = f2{0.0f, 0.0f};
-    }
+__device__ __forceinline__ void cta_coords(const DecodeArgs& a, int& slot, int& hg, int& split) {
+    const int cta = blockIdx.x;
+    split = cta % a.n_splits;
+    const int rest = cta / a.n_splits;
+    hg = rest % a.n_hgroups;
+    slot = rest / a.n_hgroups;
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
 // ---------------------------------------------------------------------------
-// Plane-layout kernel (TMA ring)
+// Plane-layout kernel.  Thread 0 keeps the ring full: at iteration `it` it
+// refills the stage consumed at iteration it-LAG once all four warps have
+// released it (per-stage "empty" mbarrier, one arrival per warp).  Warps
+// otherwise run free: no CTA-wide barrier per tile.
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ uint8_t* aligned_smem(uint8_t* raw) {
-    return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(raw) + 127) & ~uintptr_t(127));
-}
-
 template <int D, int GC, bool COMP>
-__global__ void __launch_bounds__(kDecThreads, DecCfg<D, GC, COMP>::MIN_BLOCKS)
-    k_decode_planes(const DecodeArgs a) {
+__global__ void __launch_bounds__(kDecThreads) k_decode_planes(const DecodeArgs a) {
     using Cfg = DecCfg<D, GC, COMP>;
+    constexpr int NS = Cfg::NS, LAG = Cfg::LAG, T = Cfg::T;
     extern __shared__ __align__(128) uint8_t smem_raw[];
     uint8_t* smem = aligned_smem(smem_raw);
-    const int tid = threadIdx.x;
-    const int cta = blockIdx.x;
-    const int split = cta % a.n_splits;
-    const int rest = cta / a.n_splits;
-    const int hg = rest % a.n_hgroups;
-    const int slot = rest / a.n_hgroups;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::BAR_OFF);
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    int slot, hg, split;
+    cta_coords(a, slot, hg, split);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + Cfg::FULL_OFF);
+    uint64_t* empty = reinterpret_cast<uint64_t*>(smem + Cfg::EMPTY_OFF);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + Cfg::FLAG_OFF);
 
     const int s_begin = split * a.keys_per_split;
     const int s_end = min(a.seq_len, s_begin + a.keys_per_split);
     const int n_keys = max(0, s_end - s_begin);
-    const int n_tiles = (n_keys + Cfg::T - 1) / Cfg::T;
+    const int n_tiles = (n_keys + T - 1) / T;
 
     if (tid == 0) {
-        for (int s = 0; s < kStages; ++s) mbar_init(&bars[s], 1);
+        for (int s = 0; s < NS; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kWarps);
+        }
+        *abort_flag = 0;
         fence_mbar_init();
     }
     __syncthreads();
 
     const int64_t row_base = (int64_t)slot * a.kv_stride + s_begin;
     auto issue = [&](int tile, int stage) {
-        const int k0 = tile * Cfg::T;
-        const int nk = min(Cfg::T, n_keys - k0);
+        const int k0 = tile * T;
+        const int nk = min(T, n_keys - k0);
         const int nk8 = (nk + 7) & ~7;
         const int64_t row = row_base + k0;
-        uint8_t* sb = smem + stage * Cfg::STAGE_B;
+        uint8_t* sbuf = smem + stage * Cfg::STAGE_B;
         const uint32_t sign_b = nk8 * (D / 8), sc_b = nk8 * 2, nib_b = nk8 * (D / 2);
         const uint32_t total = 2 * (sign_b + sc_b + (COMP ? nib_b + sc_b : 0));
-        mbar_arrive_expect_tx(&bars[stage], total);
-        bulk_g2s(sb + Cfg::OFF_KSIGN, (const uint8_t*)a.K.sign + row * (D / 8), sign_b, &bars[stage]);
-        bulk_g2s(sb + Cfg::OFF_KBS, (const uint8_t*)a.K.bscale + row * 2, sc_b, &bars[stage]);
-        bulk_g2s(sb + Cfg::OFF_VSIGN, (const uint8_t*)a.V.sign + row * (D / 8), sign_b, &bars[stage]);
-        bulk_g2s(sb + Cfg::OFF_VBS, (const uint8_t*)a.V.bscale + row * 2, sc_b, &bars[stage]);
+        mbar_arrive_expect_tx(&full[stage], total);
+        bulk_g2s(sbuf + Cfg::OFF_KSIGN, (const uint8_t*)a.K.sign + row * (D / 8), sign_b, &full[stage]);
+        bulk_g2s(sbuf + Cfg::OFF_KBS, (const uint8_t*)a.K.bscale + row * 2, sc_b, &full[stage]);
+        bulk_g2s(sbuf + Cfg::OFF_VSIGN, (const uint8_t*)a.V.sign + row * (D / 8), sign_b, &full[stage]);
+        bulk_g2s(sbuf + Cfg::OFF_VBS, (const uint8_t*)a.V.bscale + row * 2, sc_b, &full[stage]);
         if (COMP) {
-            bulk_g2s(sb + Cfg::OFF_KNIB, (const uint8_t*)a.K.nib + row * (D / 2), nib_b, &bars[stage]);
-            bulk_g2s(sb + Cfg::OFF_KRS, (const uint8_t*)a.K.rscale + row * 2, sc_b, &bars[stage]);
-            bulk_g2s(sb + Cfg::OFF_VNIB, (const uint8_t*)a.V.nib + row * (D / 2), nib_b, &bars[stage]);
-            bulk_g2s(sb + Cfg::OFF_VRS, (const uint8_t*)a.V.rscale + row * 2, sc_b, &bars[stage]);
+            bulk_g2s(sbuf + Cfg::OFF_KNIB, (const uint8_t*)a.K.nib + row * (D / 2), nib_b, &full[stage]);
+            bulk_g2s(sbuf + Cfg::OFF_KRS, (const uint8_t*)a.K.rscale + row * 2, sc_b, &full[stage]);
+            bulk_g2s(sbuf + Cfg::OFF_VNIB, (const uint8_t*)a.V.nib + row * (D / 2), nib_b, &full[stage]);
+            bulk_g2s(sbuf + Cfg::OFF_VRS, (const uint8_t*)a.V.rscale + row * 2, sc_b, &full[stage]);
         }
     };
-    if (tid == 0) {
-        const int pre = min(kStages - 1, n_tiles);
-        for (int t = 0; t < pre; ++t) issue(t, t);
-    }
+    if (tid == 0)
+        for (int t = 0; t < min(NS, n_tiles); ++t) issue(t, t);
 
-    QState<GC> qs;
+    QState<D, GC> qs;
     prepare_query<D, GC, COMP, Cfg>(a, slot, hg, smem, qs);
     SoftState<GC> st;
     init_soft<GC>(st);
 
-    const int grp = tid / Cfg::QPK, qt = tid % Cfg::QPK;
-    for (int it = 0; it < n_tiles; ++it) {
-        const int stage = it % kStages;
-        const uint32_t parity = (uint32_t)(it / kStages) & 1u;
-        if (tid == 0 && it + kStages - 1 < n_tiles) {
-            fence_proxy_async_smem();
-            issue(it + kStages - 1, (it + kStages - 1) % kStages);
-        }
-        const bool ok = mbar_wait_bounded(&bars[stage], parity);
-        if (ok) {
-            const uint8_t* sb = smem + stage * Cfg::STAGE_B;
-            const int nk = min(Cfg::T, n_keys - it * Cfg::T);
-#pragma unroll
-            for (int kk = 0; kk < Cfg::KPT; ++kk) {
-                const int key = grp + kk * Cfg::KPAR;
-                {
-                    const uint32_t ks = reinterpret_cast<const uint32_t*>(sb + Cfg::OFF_KSIGN)[key * Cfg::NWD + qt];
-                    const float kbs = __half2float(reinterpret_cast<const __half*>(sb + Cfg::OFF_KBS)[key]);
-                    const uint32_t vs = reinterpret_cast<const uint32_t*>(sb + Cfg::OFF_VSIGN)[key * Cfg::NWD + qt];
-                    const float vbs = __half2float(reinterpret_cast<const __half*>(sb + Cfg::OFF_VBS)[key]);
-                    uint4 kn = make_uint4(0, 0, 0, 0), vn = make_uint4(0, 0, 0, 0);
-                    float krs = 0.0f, vrs = 0.0f;
-                    if (COMP) {
-                        kn = reinterpret_cast<const uint4*>(sb + Cfg::OFF_KNIB)[key * Cfg::NWD + qt];
-                        krs = __half2float(reinterpret_cast<const __half*>(sb + Cfg::OFF_KRS)[key]);
-                        vn = reinterpret_cast<const uint4*>(sb + Cfg::OFF_VNIB)[key * Cfg::NWD + qt];
-                        vrs = __half2float(reinterpret_cast<const __half*>(sb + Cfg::OFF_VRS)[key]);
-                    }
-                    consume_key<D, GC, COMP>(qs, st, key < nk, ks, kbs, kn, krs, vs, vbs, vn, vrs);
-                }
+    int it = 0;
+    for (; it < n_tiles; ++it) {
+        const int stage = it % NS;
+        if (tid == 0 && it >= LAG && it - LAG + NS < n_tiles) {
+            const int old = it - LAG;
+            if (mbar_wait_bounded(&empty[old % NS], (uint32_t)(old / NS) & 1u)) {
+                fence_proxy_async_smem();
+                issue(old + NS, old % NS);
+            } else {
+                *abort_flag = 1;
             }
         }
-        if (__syncthreads_or(!ok)) {
-            // A copy never landed: report, drain what is still in flight (bounded), leave.
-            if (tid == 0) {
-                raise_device_error(&g_bc_device_error, BC_DEVERR_TIMEOUT);
-                for (int t = it; t < min(n_tiles, it + kStages); ++t)
-                    mbar_wait_bounded(&bars[t % kStages], (uint32_t)(t / kStages) & 1u);
-            }
-            return;
+        bool ok = mbar_wait_bounded(&full[stage], (uint32_t)(it / NS) & 1u);
+        if (!ok) *abort_flag = 1;
+        if (*abort_flag) break;
+        const int nk = min(T, n_keys - it * T);
+        consume_warp_tile<D, GC, COMP, Cfg>(qs, st, smem + stage * Cfg::STAGE_B, warp * 32, nk);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[stage]);
+    }
+    __syncthreads();
+    if (*abort_flag) {
+        // A copy never landed (or a stage was never released): report, drain
+        // what is still in flight (bounded), and leave.
+        if (tid == 0) {
+            raise_device_error(&g_bc_device_error, BC_DEVERR_TIMEOUT);
+            const int issued = min(n_tiles, NS + max(0, it - LAG + 1));
+            for (int t = max(0, it - NS); t < issued; ++t)
+                mbar_wait_bounded(&full[t % NS], (uint32_t)(t / NS) & 1u);
         }
+        return;
     }
     finish_cta<D, GC, Cfg>(a, slot, hg, split, smem, st);
 }
 
 // ---------------------------------------------------------------------------
-// Reference-record kernel: same math, fields read straight from BinaryVec
-// (36 B) / ResidualVec (130 B, 2-byte aligned) arrays.  K, V record bases are
-// passed in .sign (BinaryVec*) and .nib (ResidualVec*), kv_stride = seq_len.
+// Reference-record kernel: the same compute on tiles transcoded into the
+// canonical shared-memory layout from BinaryVec (36 B) / ResidualVec (130 B,
+// 2-byte aligned) arrays with plain loads.  K, V record bases are passed in
+// .sign (BinaryVec*) and .nib (ResidualVec*); kv_stride = seq_len.
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ uint4 load_res_nibbles16(const uint8_t* p) {
-    const uint16_t* h = reinterpret_cast<const uint16_t*>(p);
-    uint4 r;
-    r.x = (uint32_t)__ldg(h + 0) | ((uint32_t)__ldg(h + 1) << 16);
-    r.y = (uint32_t)__ldg(h + 2) | ((uint32_t)__ldg(h + 3) << 16);
-    r.z = (uint32_t)__ldg(h + 4) | ((uint32_t)__ldg(h + 5) << 16);
-    r.w = (uint32_t)__ldg(h + 6) | ((uint32_t)__ldg(h + 7) << 16);
-    return r;
+template <int D, bool COMP, typename Cfg>
+__device__ __forceinline__ void load_tile_records(const DecodeArgs& a, int64_t rec0, int nk, uint8_t* sb) {
+    constexpr int NWD = D / 32;
+    const int kk = threadIdx.x;  // one key per thread (T == kDecThreads)
+    if (kk >= nk) return;
+    const int64_t rec = rec0 + kk;
+#pragma unroll
+    for (int side = 0; side < 2; ++side) {
+        const uint8_t* bin = (const uint8_t*)(side ? a.V.sign : a.K.sign) + rec * kBinRecBytes;
+        uint32_t* srow = reinterpret_cast<uint32_t*>(sb + (side ? Cfg::OFF_VSIGN : Cfg::OFF_KSIGN)) + kk * NWD;
+#pragma unroll
+        for (int w = 0; w < NWD; ++w) srow[w] = __ldg(reinterpret_cast<const uint32_t*>(bin) + w);
+        reinterpret_cast<uint16_t*>(sb + (side ? Cfg::OFF_VBS : Cfg::OFF_KBS))[kk] =
+            __ldg(reinterpret_cast<const unsigned short*>(bin + kBinScaleOff));
+        if (COMP) {
+            const uint16_t* res = reinterpret_cast<const uint16_t*>((const uint8_t*)(side ? a.V.nib : a.K.nib) +
+                                                                    rec * kResRecBytes);
+            uint8_t* nb = sb + (side ? Cfg::OFF_VNIB : Cfg::OFF_KNIB);
+#pragma unroll
+            for (int c = 0; c < NWD; ++c) {
+                uint4 v;
+                // two's-complement codes -> offset-binary (u = code + 8 per nibble)
+                v.x = ((uint32_t)__ldg(res + 8 * c + 0) | ((uint32_t)__ldg(res + 8 * c + 1) << 16)) ^ 0x88888888u;
+                v.y = ((uint32_t)__ldg(res + 8 * c + 2) | ((uint32_t)__ldg(res + 8 * c + 3) << 16)) ^ 0x88888888u;
+                v.z = ((uint32_t)__ldg(res + 8 * c + 4) | ((uint32_t)__ldg(res + 8 * c + 5) << 16)) ^ 0x88888888u;
+                v.w = ((uint32_t)__ldg(res + 8 * c + 6) | ((uint32_t)__ldg(res + 8 * c + 7) << 16)) ^ 0x88888888u;
+                *reinterpret_cast<uint4*>(nb + nib_chunk_offset(kk, c, D)) = v;
+            }
+            reinterpret_cast<uint16_t*>(sb + (side ? Cfg::OFF_VRS : Cfg::OFF_KRS))[kk] = __ldg(res + 64);
+        }
+    }
 }
 
 template <int D, int GC, bool COMP>
-__global__ void __launch_bounds__(kDecThreads, DecCfg<D, GC, COMP>::MIN_BLOCKS)
-    k_decode_records(const DecodeArgs a) {
+__global__ void __launch_bounds__(kDecThreads) k_decode_records(const DecodeArgs a) {
     using Cfg = DecCfg<D, GC, COMP>;
+    constexpr int T = Cfg::T;
     extern __shared__ __align__(128) uint8_t smem_raw[];
     uint8_t* smem = aligned_smem(smem_raw);
-    const int tid = threadIdx.x;
-    const int cta = blockIdx.x;
-    const int split = cta % a.n_splits;
-    const int rest = cta / a.n_splits;
-    const int hg = rest % a.n_hgroups;
-    const int slot = rest / a.n_hgroups;
+    const int warp = threadIdx.x >> 5;
+    int slot, hg, split;
+    cta_coords(a, slot, hg, split);
     const int s_begin = split * a.keys_per_split;
     const int s_end = min(a.seq_len, s_begin + a.keys_per_split);
+    const int n_keys = max(0, s_end - s_begin);
+    const int n_tiles = (n_keys + T - 1) / T;
 
-    QState<GC> qs;
+    QState<D, GC> qs;
     prepare_query<D, GC, COMP, Cfg>(a, slot, hg, smem, qs);
     SoftState<GC> st;
     init_soft<GC>(st);
-
-    const int grp = tid / Cfg::QPK, qt = tid % Cfg::QPK;
-    const uint8_t* kb = (const uint8_t*)a.K.sign;
-    const uint8_t* kr = (const uint8_t*)a.K.nib;
-    const uint8_t* vb = (const uint8_t*)a.V.sign;
-    const uint8_t* vr = (const uint8_t*)a.V.nib;
-    const int64_t base = (int64_t)slot * a.kv_stride;
-    const int n_keys = max(0, s_end - s_begin);
-    const int trips = (n_keys + Cfg::KPAR - 1) / Cfg::KPAR;
-    for (int tr = 0; tr < trips; ++tr) {
-        const int s = s_begin + grp + tr * Cfg::KPAR;
-        const bool valid = s < s_end;
-        const int64_t rec = base + (valid ? s : s_begin);
-        const uint8_t* kbr = kb + rec * kBinRecBytes;
-        const uint8_t* vbr = vb + rec * kBinRecBytes;
-        const uint32_t ks = __ldg(reinterpret_cast<const uint32_t*>(kbr) + qt);
-        const float kbs = __half2float(__ldg(reinterpret_cast<const __half*>(kbr + kBinScaleOff)));
-        const uint32_t vs = __ldg(reinterpret_cast<const uint32_t*>(vbr) + qt);
-        const float vbs = __half2float(__ldg(reinterpret_cast<const __half*>(vbr + kBinScaleOff)));
-        uint4 kn = make_uint4(0, 0, 0, 0), vn = make_uint4(0, 0, 0, 0);
-        float krs = 0.0f, vrs = 0.0f;
-        if (COMP) {
-            const uint8_t* krr = kr + rec * kResRecBytes;
-            const uint8_t* vrr = vr + rec * kResRecBytes;
-            kn = load_res_nibbles16(krr + 16 * qt);
-            krs = __half2float(__ldg(reinterpret_cast<const __half*>(krr + kResScaleOff)));
-            vn = load_res_nibbles16(vrr + 16 * qt);
-            vrs = __half2float(__ldg(reinterpret_cast<const __half*>(vrr + kResScaleOff)));
-        }
-        consume_key<D, GC, COMP>(qs, st, valid, ks, kbs, kn, krs, vs, vbs, vn, vrs);
+    const int64_t rec_base = (int64_t)slot * a.kv_stride + s_begin;
+    for (int it = 0; it < n_tiles; ++it) {
+        const int nk = min(T, n_keys - it * T);
+        __syncthreads();
+        load_tile_records<D, COMP, Cfg>(a, rec_base + it * T, nk, smem);
+        __syncthreads();
+        consume_warp_tile<D, GC, COMP, Cfg>(qs, st, smem, warp * 32, nk);
     }
     finish_cta<D, GC, Cfg>(a, slot, hg, split, smem, st);
 }
@@ -654,15 +780,22 @@ struct Plan {
     int n_splits, keys_per_split, n_hgroups, gc, tile;
 };
 
-int tile_keys(int d) { return 2 * (kDecThreads / (d / 32)); }
+int tile_keys(int d) {
+    (void)d;
+    return kTile;
+}
 
-int heads_per_cta(int group) { return group >= 2 ? 2 : 1; }
+// Query heads handled per CTA: two for grouped-query caches where the two
+// queries fit a lane's registers (one KV read serves both); otherwise one,
+// and the CTAs of a slot's head groups, adjacent in the grid, share the KV
+// tiles through L2.
+int heads_per_cta(int group, int d, bool comp) { return (group >= 2 && (d <= 64 || !comp)) ? 2 : 1; }
 
 // Choose the split count so that all CTAs fit in one resident wave when the
 // slots alone cannot fill the GPU (avoids a ragged second wave).
-Plan make_plan(int n_slots, int group, int seq_len, int d, int capacity) {
+Plan make_plan(int n_slots, int group, int seq_len, int d, bool comp, int capacity) {
     Plan p;
-    p.gc = heads_per_cta(group);
+    p.gc = heads_per_cta(group, d, comp);
     p.n_hgroups = group / p.gc;
     p.tile = tile_keys(d);
     const int n_tiles = max(1, (seq_len + p.tile - 1) / p.tile);
@@ -682,8 +815,16 @@ size_t ws_bytes_for(int n_slots, int group, int n_splits, int d, int n_hgroups) 
     return ((part + 255) & ~(size_t)255) + ((cnt + 255) & ~(size_t)255);
 }
 
-int max_plan_splits(int n_slots, int group, int seq_len, int d) {
-    return make_plan(n_slots, group, seq_len, d, kMaxCtasPlan).n_splits;
+// Workspace bound over both modes: the counter region is sized for one head
+// per CTA (the most counters), the partial region for the most splits.
+size_t ws_bound(int n_slots, int group, int seq_len, int d) {
+    size_t best = 0;
+    for (int comp = 0; comp < 2; ++comp) {
+        const Plan p = make_plan(n_slots, group, seq_len, d, comp != 0, kMaxCtasPlan);
+        const size_t b = ws_bytes_for(n_slots, group, p.n_splits, d, group);
+        best = b > best ? b : best;
+    }
+    return best;
 }
 
 template <int D, int GC, bool COMP>
@@ -728,7 +869,7 @@ int capacity_of(bool records) {
 template <int D, int GC, bool COMP>
 int run_decode_t(DecodeArgs a, bool records, void* ws, size_t ws_bytes, cudaStream_t st) {
     const int cap = min(capacity_of<D, GC, COMP>(records), kMaxCtasPlan);
-    Plan p = make_plan(a.n_slots, a.group, a.seq_len, D, cap);
+    Plan p = make_plan(a.n_slots, a.group, a.seq_len, D, COMP, cap);
     a.n_splits = p.n_splits;
     a.keys_per_split = p.keys_per_split;
     a.n_hgroups = p.n_hgroups;
@@ -750,9 +891,14 @@ int run_decode_t(DecodeArgs a, bool records, void* ws, size_t ws_bytes, cudaStre
 
 template <int D>
 int run_decode_d(const DecodeArgs& a, bool comp, bool records, void* ws, size_t wsb, cudaStream_t st) {
-    const int gc = heads_per_cta(a.group);
-    if (gc == 1) return comp ? run_decode_t<D, 1, true>(a, records, ws, wsb, st) : run_decode_t<D, 1, false>(a, records, ws, wsb, st);
-    return comp ? run_decode_t<D, 2, true>(a, records, ws, wsb, st) : run_decode_t<D, 2, false>(a, records, ws, wsb, st);
+    const bool two = heads_per_cta(a.group, D, comp) == 2;
+    if (comp) {
+        if constexpr (D <= 64) {
+            if (two) return run_decode_t<D, 2, true>(a, records, ws, wsb, st);
+        }
+        return run_decode_t<D, 1, true>(a, records, ws, wsb, st);
+    }
+    return two ? run_decode_t<D, 2, false>(a, records, ws, wsb, st) : run_decode_t<D, 1, false>(a, records, ws, wsb, st);
 }
 
 int run_decode(const DecodeArgs& a, bool comp, bool records, void* ws, size_t wsb, cudaStream_t st) {
@@ -784,9 +930,7 @@ unsigned int bc_get_device_error(int clear) {
 
 size_t bc_decode_workspace_bytes(int n_slots, int group, int seq_len, int head_dim) {
     if (n_slots <= 0 || !valid_group(group) || seq_len < 0 || !bc_valid_head_dim(head_dim)) return 0;
-    const int gc = heads_per_cta(group);
-    const int s = max_plan_splits(n_slots, group, seq_len, head_dim);
-    return ws_bytes_for(n_slots, group, s, head_dim, group / gc);
+    return ws_bound(n_slots, group, seq_len, head_dim);
 }
 
 int bc_decode_attention(const void* q, bc_kv_planes K, bc_kv_planes V, void* out, float* partial, int n_slots,
@@ -954,7 +1098,7 @@ int bc_decode_attention_noalloc(const void* q, bc_kv_planes K, bc_kv_planes V, v
     // The ticket counters must start at zero.  The array keeps the previous
     // call's contents, and a previous call of another shape may have written
     // partial results over this shape's counters, so they are cleared here.
-    const size_t counter_bytes = (size_t)n_slots * (group / heads_per_cta(group)) * sizeof(unsigned);
+    const size_t counter_bytes = (size_t)n_slots * group * sizeof(unsigned);  // counters of any mode
     cudaError_t e = cudaMemsetAsync(scratch, 0, counter_bytes, (cudaStream_t)stream);
     if (e != cudaSuccess) return BC_ERR_CUDA_BASE + (int)e;
     return bc_decode_attention(q, K, V, out, partial, n_slots, group, seq_len, kv_stride, head_dim, mode, scratch,

@@ -125,11 +125,15 @@ __device__ __forceinline__ void store_sign_row(uint32_t* row, const uint32_t (&w
         if (lane == k) row[k] = w[k];
 }
 
+// Nibble word 4k+m of plane row `row` (chunk k, word m), interleaved layout,
+// stored offset-binary (each nibble holds code + 8).
 template <int NW>
-__device__ __forceinline__ void store_nib_row(uint32_t* row, const uint32_t (&nw)[NW], int lane) {
+__device__ __forceinline__ void store_nib_row(uint8_t* plane, int64_t row, const uint32_t (&nw)[NW], int lane) {
 #pragma unroll
     for (int k = 0; k < NW; ++k)
-        if ((lane & 7) == 0 && lane < 32) row[4 * k + (lane >> 3)] = nw[k];
+        if ((lane & 7) == 0)
+            *reinterpret_cast<uint32_t*>(plane + nib_chunk_offset(row, k, 32 * NW) + 4 * (lane >> 3)) =
+                nw[k] ^ 0x88888888u;  // offset-binary: code + 8
 }
 
 // ---------------------------------------------------------------------------
@@ -209,7 +213,7 @@ __device__ __forceinline__ void encode_row_planes(const float (&x)[NW], int lane
         const float s = (RES == BC_RES_FP16_SCALE) ? __half2float(__ushort_as_half(sb)) : mean_abs;
         uint32_t nw[NW], nh[NW];
         const float absmax = quantise_residual<NW>(x, w, s, lane, nw, nh);
-        store_nib_row<NW>(reinterpret_cast<uint32_t*>(P.nib) + row * (4 * NW), nw, lane);
+        store_nib_row<NW>(reinterpret_cast<uint8_t*>(P.nib), row, nw, lane);
         if (lane == 0) reinterpret_cast<uint16_t*>(P.rscale)[row] = f2h_bits(absmax);
     }
 }
@@ -259,8 +263,10 @@ __global__ void __launch_bounds__(kEncWarps * 32) k_records_to_planes(const uint
         reinterpret_cast<uint16_t*>(P.bscale)[v] = *reinterpret_cast<const uint16_t*>(b + kBinScaleOff);
     if (res != nullptr && P.nib != nullptr) {
         const uint16_t* r = reinterpret_cast<const uint16_t*>(res + v * kResRecBytes);
-        uint16_t* dst = reinterpret_cast<uint16_t*>(P.nib) + v * (8 * NW);
-        for (int i = lane; i < 8 * NW; i += 32) dst[i] = r[i];
+        uint8_t* nib = reinterpret_cast<uint8_t*>(P.nib);
+        for (int i = lane; i < 8 * NW; i += 32)
+            *reinterpret_cast<uint16_t*>(nib + nib_chunk_offset(v, i >> 3, 32 * NW) + 2 * (i & 7)) =
+                (uint16_t)(r[i] ^ 0x8888u);
         if (lane == 0) reinterpret_cast<uint16_t*>(P.rscale)[v] = r[64];
     }
 }
@@ -276,8 +282,11 @@ __global__ void __launch_bounds__(kEncWarps * 32) k_planes_to_records(bc_kv_plan
     if (lane == 8) b[8] = (uint32_t)reinterpret_cast<const uint16_t*>(P.bscale)[v];
     if (res != nullptr && P.nib != nullptr) {
         uint16_t* r = reinterpret_cast<uint16_t*>(res + v * kResRecBytes);
-        const uint16_t* src = reinterpret_cast<const uint16_t*>(P.nib) + v * (8 * NW);
-        for (int i = lane; i < 64; i += 32) r[i] = (i < 8 * NW) ? src[i] : (uint16_t)0;
+        const uint8_t* nib = reinterpret_cast<const uint8_t*>(P.nib);
+        for (int i = lane; i < 64; i += 32)
+            r[i] = (i < 8 * NW) ? (uint16_t)(*reinterpret_cast<const uint16_t*>(nib + nib_chunk_offset(v, i >> 3, 32 * NW) +
+                                                                              2 * (i & 7)) ^ 0x8888u)
+                                : (uint16_t)0;
         if (lane == 0) r[64] = reinterpret_cast<const uint16_t*>(P.rscale)[v];
     }
 }

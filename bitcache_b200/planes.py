@@ -2,7 +2,9 @@
 
 Layout (per K or V cache; include/bitcache_b200.h):
     sign   uint32 [slots, kv_stride, head_dim/32]
-    nib    uint8  [slots, kv_stride, head_dim/2]    (compensated caches only)
+    nib    uint8  [slots, kv_stride, head_dim/2] bytes, interleaved in blocks of 8
+           positions (16-byte chunk c of position p at (p/8)*4d + 128c + 16(p%8));
+           nib_rows() gives the per-position view    (compensated caches only)
     bscale fp16   [slots, kv_stride]
     rscale fp16   [slots, kv_stride]                (compensated caches only)
 kv_stride is the position capacity rounded up to a multiple of 8 so every
@@ -48,7 +50,9 @@ class Planes:
         bscale = mk((n_slots, kv_stride), dtype=torch.float16, device=device)
         nib = rscale = None
         if compensated:
-            nib = mk((n_slots, kv_stride, head_dim // 2), dtype=torch.uint8, device=device)
+            # zero codes are 0x88 bytes in the offset-binary nibble plane
+            nib = (torch.full if zero else torch.empty)(
+                (n_slots, kv_stride, head_dim // 2), *((0x88,) if zero else ()), dtype=torch.uint8, device=device)
             rscale = mk((n_slots, kv_stride), dtype=torch.float16, device=device)
         return Planes(sign, bscale, nib, rscale, head_dim)
 
@@ -67,14 +71,38 @@ class Planes:
     def c(self) -> _lib.KVPlanes:
         return _lib.KVPlanes(_lib.ptr(self.sign), _lib.ptr(self.nib), _lib.ptr(self.bscale), _lib.ptr(self.rscale))
 
+    def nib_rows(self) -> torch.Tensor:
+        """The INT4 codes per position, uint8 [slots, kv_stride, head_dim/2] (a copy)."""
+        return nib_rows(self.nib, self.head_dim)
+
     def nbytes(self) -> int:
         return sum(t.numel() * t.element_size() for t in (self.sign, self.bscale, self.nib, self.rscale)
                    if t is not None)
 
     def zero_(self) -> None:
-        for t in (self.sign, self.bscale, self.nib, self.rscale):
+        """Reset to all-zero fields (nibble bytes 0x88 = codes 0)."""
+        for t in (self.sign, self.bscale, self.rscale):
             if t is not None:
                 t.zero_()
+        if self.nib is not None:
+            self.nib.fill_(0x88)
+
+
+def nib_rows(nib: torch.Tensor, head_dim: int) -> torch.Tensor:
+    """De-interleave a nibble plane [slots, kv_stride, head_dim/2] into per-position rows of
+    the reference's byte format (two's-complement codes, element 2i in the low nibble)."""
+    slots, stride = nib.shape[0], nib.shape[1]
+    rows = (nib.reshape(slots, stride // 8, head_dim // 32, 8, 16).permute(0, 1, 3, 2, 4)
+            .reshape(slots, stride, head_dim // 2))
+    return torch.bitwise_xor(rows, 0x88).contiguous()
+
+
+def nib_interleave(rows: torch.Tensor, head_dim: int) -> torch.Tensor:
+    """Inverse of nib_rows: reference-format rows [slots, kv_stride, head_dim/2] -> plane bytes."""
+    slots, stride = rows.shape[0], rows.shape[1]
+    x = torch.bitwise_xor(rows, 0x88)
+    return (x.reshape(slots, stride // 8, 8, head_dim // 32, 16).permute(0, 1, 3, 2, 4)
+            .reshape(slots, stride, head_dim // 2).contiguous())
 
 
 def _stream(t: torch.Tensor) -> int:

@@ -23,7 +23,11 @@
  *  - planes (native): per K or V cache, four 16-byte-aligned arrays indexed
  *    [slot][position] with a row stride kv_stride (positions per slot):
  *        sign   uint32 [slots][kv_stride][head_dim/32]   bit i%32 of word i/32 = (x_i >= 0)
- *        nib    uint8  [slots][kv_stride][head_dim/2]    INT4 residual, element 2i low nibble
+ *        nib    uint8  [slots][kv_stride][head_dim/2]    INT4 residual codes stored offset-binary
+ *               (each nibble holds code + 8, i.e. the reference's byte XOR 0x88), interleaved in blocks
+ *               of 8 positions: the 16-byte chunk c (dims 32c..32c+31, element 2i in the low
+ *               nibble of byte i) of plane row r = slot*kv_stride + pos starts at byte
+ *               (r/8)*(4*head_dim) + c*128 + (r%8)*16
  *        bscale fp16   [slots][kv_stride]                mean |x| (binary scale)
  *        rscale fp16   [slots][kv_stride]                residual absmax
  *    5*head_dim/8 + 4 bytes per vector (84 B at head_dim 128).  The field
@@ -118,7 +122,7 @@ int bc_adaptive_select(const float* entropy, uint8_t* modes, int batch, int n_he
 
 typedef struct bc_kv_planes {
     void* sign;   /* uint32 [slots][kv_stride][head_dim/32] */
-    void* nib;    /* uint8  [slots][kv_stride][head_dim/2]  (NULL for binary-only caches) */
+    void* nib;    /* uint8, interleaved as above             (NULL for binary-only caches) */
     void* bscale; /* fp16   [slots][kv_stride] */
     void* rscale; /* fp16   [slots][kv_stride]              (NULL for binary-only caches) */
 } bc_kv_planes;

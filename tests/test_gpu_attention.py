@@ -102,7 +102,7 @@ def test_gqa_vs_oracle(cuda, group, d):
 
     def host(X):
         return {"words": X.sign.cpu().numpy().view(np.uint32), "bscale": X.bscale.cpu().numpy().view(np.uint16),
-                "nib": X.nib.cpu().numpy(), "rscale": X.rscale.cpu().numpy().view(np.uint16)}
+                "nib": X.nib_rows().cpu().numpy(), "rscale": X.rscale.cpu().numpy().view(np.uint16)}
 
     want = O.attention(q.numpy(), host(K), host(V), group, S, stride, True).view(np.float16).astype(np.float32)
     close(mine, want, f"gqa g={group} d={d}")
@@ -290,6 +290,6 @@ def test_workspace_counters_left_zero_and_no_device_error(cuda, slots, group):
         assert torch.equal(planes.decode_attention(q, K, V, S), first)
     torch.cuda.synchronize()
     key = (cuda.index or 0, _lib.stream_of(cuda), "decode", slots, group)
-    n_cnt = slots * (1 if group == 1 else group // 2)
+    n_cnt = slots * group  # upper bound of the counter region (one head per CTA)
     assert not _lib._ws[key][: 4 * n_cnt].any(), "split-K ticket counters not returned to zero"
     assert _lib.device_error() == 0

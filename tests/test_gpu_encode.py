@@ -97,7 +97,7 @@ def test_plane_encode_bit_exact(cuda, d, mode):
     if mode != planes.RES_NONE:
         rr = refgpu.residual_encode(x, rb)
         nr, rsr = fields_res(rr, d)
-        assert np.array_equal(P.nib[:, :seq].cpu().numpy().reshape(-1, d // 2), nr)
+        assert np.array_equal(P.nib_rows()[:, :seq].cpu().numpy().reshape(-1, d // 2), nr)
         assert np.array_equal(P.rscale[:, :seq].cpu().numpy().view(np.uint16).reshape(-1), rsr)
 
 
@@ -150,7 +150,7 @@ def test_append_kv_matches_online_records(cuda, d):
         torch.cuda.synchronize()
         assert np.array_equal(X.sign.cpu().numpy().view(np.uint32).reshape(-1, d // 32), w)
         assert np.array_equal(X.bscale.cpu().numpy().view(np.uint16).reshape(-1), s)
-        assert np.array_equal(X.nib.cpu().numpy().reshape(-1, d // 2), nib)
+        assert np.array_equal(X.nib_rows().cpu().numpy().reshape(-1, d // 2), nib)
         assert np.array_equal(X.rscale.cpu().numpy().view(np.uint16).reshape(-1), rs)
 
 
