@@ -98,6 +98,15 @@ class BitCache:
         out = _planes.decode_attention(Q.view(-1, self.head_dim), self._K, self._V, self._filled, mode)
         return out.view(self.batch, self.n_heads, self.head_dim)
 
+    def keep_residuals(self, fraction: float = 0.25) -> None:
+        """Per-vector adaptive precision: keep the INT4 residual only for the given fraction
+        of cached vectors (per K/V, per slot) with the largest residual energy; the rest
+        become binary-only.  Applies to the positions cached so far."""
+        assert self.compensated, "keep_residuals needs a compensated cache"
+        n_keep = _planes.keep_count(self._filled, fraction)
+        for P in (self._K, self._V):
+            _planes.select_residual_topk(P, self._filled, n_keep, apply=True)
+
     def reset(self) -> None:
         """Clear the cache and the ring pointers."""
         self._K.zero_()

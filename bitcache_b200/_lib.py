@@ -62,6 +62,9 @@ _SIGS = {
     "bc_decode_noalloc_max_scratch_bytes": (c_size_t, []),
     "bc_decode_attention_noalloc": (c_int, [c_void_p, KVPlanes, KVPlanes, c_void_p, c_void_p, c_int, c_int, c_int,
                                             c_int64, c_int, c_int, c_void_p]),
+    "bc_select_workspace_bytes": (c_size_t, [c_int, c_int64]),
+    "bc_select_residual_topk": (c_int, [KVPlanes, c_int, c_int, c_int64, c_int, c_int, c_void_p, c_int, c_void_p,
+                                        c_size_t, c_void_p]),
     "bc_lse_merge": (c_int, [c_void_p, c_int, c_int64, c_int, c_void_p, c_void_p]),
     "bc_xnor_popcount": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int64, c_int, c_void_p]),
     "bc_records_to_planes": (c_int, [c_void_p, c_void_p, KVPlanes, c_int64, c_int, c_void_p]),
@@ -89,7 +92,10 @@ def load() -> ctypes.CDLL:
                 "`python -m bitcache_b200.build`")
         lib = ctypes.CDLL(LIB_PATH)
         for name, (res, args) in _SIGS.items():
-            fn = getattr(lib, name)
+            try:
+                fn = getattr(lib, name)
+            except AttributeError as e:
+                raise RuntimeError(f"{LIB_PATH} lacks {name}; rebuild with `python -m bitcache_b200.build`") from e
             fn.restype = res
             fn.argtypes = args
         _lib = lib

@@ -167,6 +167,29 @@ def decode_attention(q: torch.Tensor, K: Planes, V: Planes, seq_len: int, mode: 
     return out
 
 
+def keep_count(seq_len: int, fraction: float) -> int:
+    """Number of residuals kept per slot for a keep fraction (rounded to nearest, ties up)."""
+    return int(seq_len * fraction + 0.5)
+
+
+def select_residual_topk(P: Planes, seq_len: int, n_keep: int, apply: bool = True,
+                         want_mask: bool = False) -> torch.Tensor | None:
+    """Per-vector adaptive precision on one plane cache: keep the residuals of the n_keep
+    vectors per slot with the largest residual energy (see bc_select_residual_topk);
+    with apply, zero the others in place.  Returns the uint8 keep mask when asked."""
+    if not P.compensated:
+        raise RuntimeError("select_residual_topk needs a compensated (residual) cache")
+    lib = _lib.load()
+    st = _lib.stream_of(P.sign.device)
+    keep = torch.zeros((P.n_slots, P.kv_stride), dtype=torch.uint8, device=P.sign.device) if want_mask else None
+    wsb = lib.bc_select_workspace_bytes(P.n_slots, P.kv_stride)
+    ws = torch.empty(max(wsb, 16), dtype=torch.uint8, device=P.sign.device)
+    _lib.check(lib.bc_select_residual_topk(P.c(), P.n_slots, seq_len, P.kv_stride, P.head_dim, n_keep,
+                                           _lib.ptr(keep), 1 if apply else 0, ws.data_ptr(), ws.numel(), st),
+               "select_residual_topk")
+    return keep
+
+
 def lse_merge(parts: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
     """Merge partial triples float32 [n_parts, n_heads, head_dim + 2] -> fp16 [n_heads, head_dim]."""
     n_parts, n_heads, dp2 = parts.shape

@@ -171,6 +171,17 @@ int bc_decode_attention_noalloc(const void* q, bc_kv_planes K, bc_kv_planes V, v
                                 int n_slots, int group, int seq_len, int64_t kv_stride, int head_dim, int mode,
                                 void* stream);
 
+/* Per-vector adaptive precision (no reference kernel; the reference adapts per head):
+ * within each slot keep the INT4 residual of the n_keep vectors (of positions
+ * [0, seq_len)) with the largest key fp32(rs*rs) * (float)sum_i code_i^2, ties
+ * to the lower position.  keep (uint8 [slots][kv_stride], may be NULL when
+ * apply != 0) receives 1 for kept vectors.  apply != 0 zeroes the residual
+ * scale and codes of the others in place, which makes them contribute
+ * exactly nothing to compensated attention.  Workspace: the per-vector keys. */
+size_t bc_select_workspace_bytes(int n_slots, int64_t kv_stride);
+int bc_select_residual_topk(bc_kv_planes P, int n_slots, int seq_len, int64_t kv_stride, int head_dim, int n_keep,
+                            uint8_t* keep, int apply, void* workspace, size_t workspace_bytes, void* stream);
+
 /* Log-sum-exp merge of n_parts partial triples per head (the cross-GPU sequence split):
  * parts[(p*n_heads + h)*(head_dim+2) + ...] as written by bc_decode_attention;
  * out fp16 [n_heads][head_dim]. */

@@ -135,3 +135,26 @@ def test_seq_split_gloo_world2():
         assert p.exitcode == 0
     for r in range(2):
         np.testing.assert_allclose(res[r], want, rtol=1e-4, atol=1e-5)
+
+
+def test_oracle_topk_selection_matches_numpy():
+    """The oracle's per-vector selection equals a stable numpy sort on the same keys."""
+    rng = np.random.default_rng(3)
+    slots, S, d = 2, 200, 64
+    nib = rng.integers(0, 256, (slots, S, d // 2), dtype=np.uint8)
+    nib[:, 50:60] = nib[:, 5:6]  # ties
+    rs = (rng.random((slots, S)) * 0.5).astype(np.float16)
+    rs[:, 50:60] = rs[:, 5:6]
+    keep = O.select_residual_topk(nib, rs.view(np.uint16), S, 37)
+    lo = (nib & 0x0F).astype(np.int64)
+    hi = (nib >> 4).astype(np.int64)
+    lo = np.where(lo >= 8, lo - 16, lo)
+    hi = np.where(hi >= 8, hi - 16, hi)
+    ss = (lo * lo + hi * hi).sum(-1)
+    rr = rs.astype(np.float32) * rs.astype(np.float32)
+    key = (rr * ss.astype(np.float32)).astype(np.float32)
+    for j in range(slots):
+        order = sorted(range(S), key=lambda s: (-key[j, s], s))
+        want = np.zeros(S, np.uint8)
+        want[order[:37]] = 1
+        assert np.array_equal(keep[j], want)
