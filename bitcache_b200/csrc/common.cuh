@@ -100,6 +100,11 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
         : "memory");
 }
 
+// Bulk prefetch of a global range into L2 (no shared memory involved).
+__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
 // ---------------------------------------------------------------------------
 // Packed fp32x2 arithmetic (sm_100).  Written without .ftz so that denormal
 // operands are honoured: the V accumulation feeds sign bits and INT4 codes in

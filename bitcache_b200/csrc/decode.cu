@@ -49,6 +49,9 @@ __device__ unsigned int g_bc_device_error = 0;
 #ifndef BC_DEC_QPACK_SMEM
 #define BC_DEC_QPACK_SMEM 1    // 1: the score phase reads the query packs from shared memory
 #endif
+#ifndef BC_DEC_L2_PREFETCH
+#define BC_DEC_L2_PREFETCH 0   // tiles ahead of the ring to prefetch into L2 (0: off)
+#endif
 #ifndef BC_DEC_V_HOIST
 #define BC_DEC_V_HOIST 0       // 1: the value phase loads all rounds' operands before computing
 #endif
@@ -130,12 +133,17 @@ struct QState {
 // u = code + 8) scaled by 2^(4(p%4)-64), the nibble's in-register position.
 // Keeping the two parts apart lets every FFMA2 of a key share one
 // coefficient; the fixed scales are removed once per CTA.
+// With several query heads per CTA (grouped-query caches) each head keeps one
+// combined accumulator instead (value * 2^-64), and every FFMA2 carries its
+// dim pair's power-of-two factor in the coefficient: that halves the
+// accumulator registers so up to four heads share one extraction of each key.
 template <int GC>
 struct SoftState {
+    static constexpr bool kSplit = (GC == 1);
     float m[GC];         // running max (log2 units), uniform across the warp
     float l[GC], t[GC];  // per lane: sum of weights and sum of (a + 8c) of the lane's own keys
-    f2 acc_s[GC][16];
-    f2 acc_n[GC][16];
+    f2 acc_s[GC][16];                   // split: sign part; combined: whole value
+    f2 acc_n[kSplit ? GC : 1][16];      // split only: residual part
 };
 
 __device__ __forceinline__ uint8_t* aligned_smem(uint8_t* raw) {
@@ -249,7 +257,7 @@ __device__ __forceinline__ void init_soft(SoftState<GC>& st) {
 #pragma unroll
         for (int p = 0; p < 16; ++p) {
             st.acc_s[g][p] = f2{0.0f, 0.0f};
-            st.acc_n[g][p] = f2{0.0f, 0.0f};
+            if constexpr (SoftState<GC>::kSplit) st.acc_n[g][p] = f2{0.0f, 0.0f};
         }
     }
 }
@@ -352,7 +360,7 @@ __device__ __forceinline__ void consume_warp_tile(const QState<D, GC>& qs, SoftS
 #pragma unroll
             for (int p = 0; p < 16; ++p) {
                 fmul2(st.acc_s[g][p], al);
-                if (COMP) fmul2(st.acc_n[g][p], al);
+                if constexpr (COMP && SoftState<GC>::kSplit) fmul2(st.acc_n[g][p], al);
             }
         }
         const float wt = valid ? fast_exp2(s2[g] - st.m[g]) : 0.0f;
@@ -411,7 +419,12 @@ __device__ __forceinline__ void consume_warp_tile(const QState<D, GC>& qs, SoftS
             for (int p = 0; p < 16; ++p) {
                 // sign bits of dims p and p+16, each the exact denormal 2^(p-149)
                 const f2 y = {bits_f(vs & (1u << p)), bits_f(vs_hi & (1u << p))};
-                ffma2(st.acc_s[g][p], a2, y);
+                if constexpr (SoftState<GC>::kSplit) {
+                    ffma2(st.acc_s[g][p], a2, y);
+                } else {
+                    const float ap = a0 * exp2i(-p);
+                    ffma2(st.acc_s[g][p], f2{ap, ap}, y);
+                }
                 if (COMP) {
                     // codes of dims p (word p/8) and p+16 (word 2 + p/8), nibble p%8:
                     // nibbles 0-3 from the word, 4-7 from its upper half
@@ -420,7 +433,12 @@ __device__ __forceinline__ void consume_warp_tile(const QState<D, GC>& qs, SoftS
                     const uint32_t srcb = (t < 4) ? nw[2 + kw0] : nh[2 + kw0];
                     const int sh = 4 * (t & 3);
                     const f2 x = {bits_f(srca & (0xFu << sh)), bits_f(srcb & (0xFu << sh))};
-                    ffma2(st.acc_n[g][p], c2, x);
+                    if constexpr (SoftState<GC>::kSplit) {
+                        ffma2(st.acc_n[g][p], c2, x);
+                    } else {
+                        const float cp = c0 * exp2i(-sh);
+                        ffma2(st.acc_s[g][p], f2{cp, cp}, x);
+                    }
                 }
             }
         }
@@ -450,9 +468,14 @@ __device__ __forceinline__ void finish_cta(const DecodeArgs& a, int slot, int hg
         float o[32];
 #pragma unroll
         for (int p = 0; p < 16; ++p) {
-            const float fs = exp2i(kAccShift - p), fn = exp2i(kAccShift - 4 * (p & 3));
-            o[p] = st.acc_s[g][p].x * fs + st.acc_n[g][p].x * fn;
-            o[p + 16] = st.acc_s[g][p].y * fs + st.acc_n[g][p].y * fn;
+            if constexpr (SoftState<GC>::kSplit) {
+                const float fs = exp2i(kAccShift - p), fn = exp2i(kAccShift - 4 * (p & 3));
+                o[p] = st.acc_s[g][p].x * fs + st.acc_n[g][p].x * fn;
+                o[p + 16] = st.acc_s[g][p].y * fs + st.acc_n[g][p].y * fn;
+            } else {
+                o[p] = st.acc_s[g][p].x * exp2i(kAccShift);
+                o[p + 16] = st.acc_s[g][p].y * exp2i(kAccShift);
+            }
         }
         // lanes holding the same chunk (same qt) differ in their low log2(KPW) bits
 #pragma unroll
@@ -608,6 +631,26 @@ __global__ void __launch_bounds__(kDecThreads) k_decode_planes(const DecodeArgs 
             bulk_g2s(sbuf + Cfg::OFF_VNIB, (const uint8_t*)a.V.nib + row * (D / 2), nib_b, &full[stage]);
             bulk_g2s(sbuf + Cfg::OFF_VRS, (const uint8_t*)a.V.rscale + row * 2, sc_b, &full[stage]);
         }
+#if BC_DEC_L2_PREFETCH > 0
+        // Start the HBM reads of a later tile now, into L2, so its ring copy
+        // later finds the data close by without holding shared memory.
+        const int pt = tile + BC_DEC_L2_PREFETCH;
+        if (pt < n_tiles) {
+            const int pk0 = pt * T;
+            const int pn8 = (min(T, n_keys - pk0) + 7) & ~7;
+            const int64_t prow = row_base + pk0;
+            bulk_prefetch_l2((const uint8_t*)a.K.sign + prow * (D / 8), pn8 * (D / 8));
+            bulk_prefetch_l2((const uint8_t*)a.V.sign + prow * (D / 8), pn8 * (D / 8));
+            bulk_prefetch_l2((const uint8_t*)a.K.bscale + prow * 2, pn8 * 2);
+            bulk_prefetch_l2((const uint8_t*)a.V.bscale + prow * 2, pn8 * 2);
+            if (COMP) {
+                bulk_prefetch_l2((const uint8_t*)a.K.nib + prow * (D / 2), pn8 * (D / 2));
+                bulk_prefetch_l2((const uint8_t*)a.V.nib + prow * (D / 2), pn8 * (D / 2));
+                bulk_prefetch_l2((const uint8_t*)a.K.rscale + prow * 2, pn8 * 2);
+                bulk_prefetch_l2((const uint8_t*)a.V.rscale + prow * 2, pn8 * 2);
+            }
+        }
+#endif
     };
     if (tid == 0)
         for (int t = 0; t < min(NS, n_tiles); ++t) issue(t, t);
@@ -785,11 +828,14 @@ int tile_keys(int d) {
     return kTile;
 }
 
-// Query heads handled per CTA: two for grouped-query caches where the two
-// queries fit a lane's registers (one KV read serves both); otherwise one,
-// and the CTAs of a slot's head groups, adjacent in the grid, share the KV
-// tiles through L2.
-int heads_per_cta(int group, int d, bool comp) { return (group >= 2 && (d <= 64 || !comp)) ? 2 : 1; }
+// Query heads handled per CTA: up to two (compensated) or four (binary) of a
+// slot's group, so one read and one bit extraction of every KV key serve
+// them all; the CTAs of a slot's remaining head groups, adjacent in the
+// grid, share the KV tiles through L2.
+int heads_per_cta(int group, int d, bool comp) {
+    const int cap = (comp || d > 128) ? 2 : 4;  // register budget without spills
+    return group < cap ? group : cap;
+}
 
 // Choose the split count so that all CTAs fit in one resident wave when the
 // slots alone cannot fill the GPU (avoids a ragged second wave).
@@ -832,10 +878,14 @@ int launch_decode(const DecodeArgs& a, bool records, cudaStream_t st) {
     using Cfg = DecCfg<D, GC, COMP>;
     const unsigned grid = (unsigned)((int64_t)a.n_slots * a.n_hgroups * a.n_splits);
     if (grid == 0) return BC_OK;
-    if (records)
-        k_decode_records<D, GC, COMP><<<grid, kDecThreads, Cfg::SMEM_B, st>>>(a);
-    else
-        k_decode_planes<D, GC, COMP><<<grid, kDecThreads, Cfg::SMEM_B, st>>>(a);
+    if constexpr (GC == 1) {
+        if (records) {
+            k_decode_records<D, GC, COMP><<<grid, kDecThreads, Cfg::SMEM_B, st>>>(a);
+            BC_LAUNCH_CHECK();
+            return BC_OK;
+        }
+    }
+    k_decode_planes<D, GC, COMP><<<grid, kDecThreads, Cfg::SMEM_B, st>>>(a);
     BC_LAUNCH_CHECK();
     return BC_OK;
 }
@@ -852,11 +902,17 @@ int capacity_of(bool records) {
     if (dev >= 0 && dev < kMaxDev && cap[records][dev] > 0) return cap[records][dev];
     int sms = 148, per_sm = 1;
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    if (records) {
-        cudaFuncSetAttribute(k_decode_records<D, GC, COMP>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_B);
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_decode_records<D, GC, COMP>, kDecThreads,
-                                                      Cfg::SMEM_B);
-    } else {
+    bool done = false;
+    if constexpr (GC == 1) {
+        if (records) {
+            cudaFuncSetAttribute(k_decode_records<D, GC, COMP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 Cfg::SMEM_B);
+            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_decode_records<D, GC, COMP>, kDecThreads,
+                                                          Cfg::SMEM_B);
+            done = true;
+        }
+    }
+    if (!done) {
         cudaFuncSetAttribute(k_decode_planes<D, GC, COMP>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_B);
         cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_decode_planes<D, GC, COMP>, kDecThreads,
                                                       Cfg::SMEM_B);
@@ -891,14 +947,15 @@ int run_decode_t(DecodeArgs a, bool records, void* ws, size_t ws_bytes, cudaStre
 
 template <int D>
 int run_decode_d(const DecodeArgs& a, bool comp, bool records, void* ws, size_t wsb, cudaStream_t st) {
-    const bool two = heads_per_cta(a.group, D, comp) == 2;
-    if (comp) {
-        if constexpr (D <= 64) {
-            if (two) return run_decode_t<D, 2, true>(a, records, ws, wsb, st);
-        }
-        return run_decode_t<D, 1, true>(a, records, ws, wsb, st);
+    switch (heads_per_cta(a.group, D, comp)) {
+        case 1:
+            return comp ? run_decode_t<D, 1, true>(a, records, ws, wsb, st) : run_decode_t<D, 1, false>(a, records, ws, wsb, st);
+        case 2:
+            return comp ? run_decode_t<D, 2, true>(a, records, ws, wsb, st) : run_decode_t<D, 2, false>(a, records, ws, wsb, st);
+        default:
+            if constexpr (D <= 128) return run_decode_t<D, 4, false>(a, records, ws, wsb, st);
+            return BC_ERR_UNSUPPORTED;
     }
-    return two ? run_decode_t<D, 2, false>(a, records, ws, wsb, st) : run_decode_t<D, 1, false>(a, records, ws, wsb, st);
 }
 
 int run_decode(const DecodeArgs& a, bool comp, bool records, void* ws, size_t wsb, cudaStream_t st) {
