@@ -353,20 +353,20 @@ def main():
                          device=str(dev), compensated=comp, n_kv_heads=my_slots if world > 1 else w.n_kv_heads)
         cache.prefill(k_all.view(cache.batch, cache.n_kv_heads, my_S, d), v_all.view(cache.batch, cache.n_kv_heads, my_S, d))
         del k_all, v_all
-        qh = q_all.view(cache.batch, cache.n_heads, d).cpu().pin_memory()
-        kh = (torch.randn(cache.batch, cache.n_kv_heads, d) / math.sqrt(d)).half().pin_memory()
-        vh = (torch.randn(cache.batch, cache.n_kv_heads, d) / math.sqrt(d)).half().pin_memory()
+        # One pinned host staging buffer [q | k | v] per step, one copy in, one copy out.
+        nq, nkv = cache.batch * cache.n_heads * d, cache.batch * cache.n_kv_heads * d
+        host_in = torch.empty(nq + 2 * nkv, dtype=torch.float16).pin_memory()
+        host_in[:nq] = q_all.reshape(-1).cpu()
+        host_in[nq:] = (torch.randn(2 * nkv) / math.sqrt(d)).half()
         oh = torch.empty((cache.batch, cache.n_heads, d), dtype=torch.float16).pin_memory()
-        qd = torch.empty_like(qh, device=dev)
-        kd = torch.empty_like(kh, device=dev)
-        vd = torch.empty_like(vh, device=dev)
+        dev_in = torch.empty_like(host_in, device=dev)
+        qd = dev_in[:nq].view(cache.batch, cache.n_heads, d)
+        kd = dev_in[nq:nq + nkv].view(cache.batch, cache.n_kv_heads, d)
+        vd = dev_in[nq + nkv:].view(cache.batch, cache.n_kv_heads, d)
 
         def e2e_step():
-            qd.copy_(qh, non_blocking=True)
-            kd.copy_(kh, non_blocking=True)
-            vd.copy_(vh, non_blocking=True)
-            cache.append(kd, vd)
-            o = cache.attend(qd)
+            dev_in.copy_(host_in, non_blocking=True)
+            o = cache.step(qd, kd, vd)  # append + attend, one launch
             oh.copy_(o, non_blocking=True)
 
         for _ in range(max(3, args.warmup)):
@@ -385,13 +385,34 @@ def main():
             t = torch.tensor([e2e_ms], device=dev, dtype=torch.float64)
             pg.all_reduce(t, op=pg.ReduceOp.MAX)
             e2e_ms = float(t[0])
-        h2d = (qh.numel() + kh.numel() + vh.numel()) * 2 * world
+        h2d = host_in.numel() * 2 * world
         d2h = oh.numel() * 2 * world
         # the cache in the e2e leg is one copy: its reads may partly hit L2 when it is small
         e2e = {"value": bytes_total / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s", "ms_per_step": e2e_ms,
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-               "path": "BitCache.append + BitCache.attend, pinned host Q/K/V in, output out",
-               "gpu_launches_per_step": 2}
+               "path": "BitCache.step (fused append + attend), pinned host Q/K/V in, output out",
+               "gpu_launches_per_step": 1}
+
+    # ---- prefill encode throughput (fused binary + INT4 residual into planes) ----
+    prefill = None
+    if rank == 0:
+        Kp = planes.Planes.empty(my_slots, stride, d, comp, dev, zero=False)
+        src = w.k.reshape(n_slots, S, d)[a:b, s_a:s_b].contiguous()
+        for _ in range(3):
+            planes.encode_planes(src, Kp, res_mode)
+        p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        n_enc = 10
+        p0.record(stream)
+        for _ in range(n_enc):
+            planes.encode_planes(src, Kp, res_mode)
+        p1.record(stream)
+        torch.cuda.synchronize()
+        enc_ms = p0.elapsed_time(p1) / n_enc
+        enc_bytes = src.numel() * 2 + my_slots * my_S * planes.vector_bytes(d, comp)
+        prefill = {"value": enc_bytes / (enc_ms * 1e-3) / 1e9, "unit": "GB/s", "ms": enc_ms,
+                   "vectors": my_slots * my_S, "bytes": enc_bytes, "kernel": "k_encode_planes",
+                   "frac": enc_bytes / (enc_ms * 1e-3) / 1e9 / peaks()[0]}
+        del Kp, src
 
     hbm, peak_kind = peaks()
     achieved = bytes_rank / (kern_ms * 1e-3) / 1e9
@@ -418,6 +439,7 @@ def main():
         "clocks": clocks,
         "gpu_launches": args.steps * (2 if seq_split else 1),
         "e2e": e2e,
+        "prefill_encode": prefill,
     }
 
     if rank == 0 and world == 1 and not args.no_ref_gpu:

@@ -98,6 +98,23 @@ class BitCache:
         out = _planes.decode_attention(Q.view(-1, self.head_dim), self._K, self._V, self._filled, mode)
         return out.view(self.batch, self.n_heads, self.head_dim)
 
+    def step(self, Q: Tensor, K: Tensor, V: Tensor) -> Tensor:
+        """One decode step in one launch: ``append(K, V)`` followed by ``attend(Q)``
+        (reference bitcache/__init__.py:95-148), with identical results and cache
+        contents.  The new token is encoded inside the attention kernel and
+        attended from the encoder's output."""
+        self._validate_kv(K, V)
+        assert Q.shape == (self.batch, self.n_heads, self.head_dim), "Q shape mismatch"
+        assert Q.dtype == torch.float16 and Q.is_cuda and Q.is_contiguous(), "Q must be contiguous fp16 CUDA"
+        pos = self._write_pos
+        filled = min(self._filled + 1, self.max_seq)
+        mode = _planes.MODE_COMPENSATED if self.compensated else _planes.MODE_BINARY
+        out = _planes.decode_step(Q.view(-1, self.head_dim), K.view(-1, self.head_dim), V.view(-1, self.head_dim),
+                                  self._K, self._V, filled, pos, mode, self._res_mode)
+        self._write_pos = (pos + 1) % self.max_seq
+        self._filled = filled
+        return out.view(self.batch, self.n_heads, self.head_dim)
+
     def keep_residuals(self, fraction: float = 0.25) -> None:
         """Per-vector adaptive precision: keep the INT4 residual only for the given fraction
         of cached vectors (per K/V, per slot) with the largest residual energy; the rest

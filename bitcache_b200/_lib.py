@@ -59,6 +59,8 @@ _SIGS = {
     "bc_decode_workspace_bytes": (c_size_t, [c_int, c_int, c_int, c_int]),
     "bc_decode_attention": (c_int, [c_void_p, KVPlanes, KVPlanes, c_void_p, c_void_p, c_int, c_int, c_int, c_int64,
                                     c_int, c_int, c_void_p, c_size_t, c_void_p]),
+    "bc_decode_step": (c_int, [c_void_p, c_void_p, c_void_p, KVPlanes, KVPlanes, c_void_p, c_void_p, c_int, c_int,
+                               c_int, c_int64, c_int, c_int, c_int, c_int, c_void_p, c_size_t, c_void_p]),
     "bc_decode_noalloc_max_scratch_bytes": (c_size_t, []),
     "bc_decode_attention_noalloc": (c_int, [c_void_p, KVPlanes, KVPlanes, c_void_p, c_void_p, c_int, c_int, c_int,
                                             c_int64, c_int, c_int, c_void_p]),

@@ -36,7 +36,7 @@
 // removed once per CTA together with the constant parts sum_s (a_s + 8 c_s).
 #include <mutex>
 
-#include "common.cuh"
+#include "encode_core.cuh"
 
 namespace bc {
 
@@ -95,7 +95,15 @@ struct DecCfg {
     static constexpr int FULL_OFF = QPK_OFF + (BC_DEC_QPACK_SMEM ? GC * (D / 8) * 16 : 0);  // mbarriers
     static constexpr int EMPTY_OFF = FULL_OFF + NS * 8;         // mbarriers: all warps done with a stage
     static constexpr int FLAG_OFF = EMPTY_OFF + NS * 8;         // abort flag
-    static constexpr int SMEM_B = FLAG_OFF + 16 + 128;          // + slack to align the base to 128 B
+    // Fused decode step: the appended K and V rows, staged once per CTA in
+    // plane format (sign words, 16-byte nibble chunks in natural order, scales).
+    static constexpr int NEWSIGN_B = (D / 8 + 15) & ~15;
+    static constexpr int NEWROW_B = NEWSIGN_B + D / 2 + 16;
+    static constexpr int NEW_OFF = FLAG_OFF + 16;               // [2][NEWROW_B]: K row, V row
+    static constexpr int SMEM_B = NEW_OFF + 2 * NEWROW_B + 128; // + slack to align the base to 128 B
+    // Resident CTAs per SM the plain kernel reaches at head_dim <= 128 with one
+    // head per CTA; the fused-step variant is held to the same register budget.
+    static constexpr int STEP_MIN_CTAS = (GC == 1 && D <= 128) ? (COMP ? 4 : 8) : 0;
 };
 
 struct DecodeArgs {
@@ -108,6 +116,11 @@ struct DecodeArgs {
     int n_slots, group, seq_len, n_splits, keys_per_split, n_hgroups;
     int64_t kv_stride;
     int head_dim;
+    // fused decode step only: one new K and V row per slot, written at plane
+    // position append_pos of every slot before that position is attended
+    const __half* new_k;
+    const __half* new_v;
+    int append_pos, append_res;
 };
 
 // Per-lane query state for GC heads.  The score phase handles whole keys, so
@@ -578,13 +591,98 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
 }
 
 // ---------------------------------------------------------------------------
+// Fused decode step helpers.  The CTAs whose key range holds the append
+// position encode the new K (warp 0) and V (warp 1) row with the shared
+// warp encoders (bit-identical to bc_append_kv), stage it in shared memory,
+// and, in head group 0 only, store it to the planes.  When the tile holding
+// that position lands, its owning warp overwrites the stale row in the stage
+// before scoring, so the tile is attended exactly as if the append had run
+// first, whatever the ring copy read from global memory.
+// ---------------------------------------------------------------------------
+template <int NW>
+struct StagedRowSink {
+    PlaneRowSink<NW> g;  // global row (written when `store`)
+    uint8_t* srow;       // shared-memory row: sign words, nibble chunks, scales
+    int nib_off;
+    bool store;
+    __device__ __forceinline__ void sign(const uint32_t (&w)[NW], int lane) {
+        if (store) g.sign(w, lane);
+#pragma unroll
+        for (int k = 0; k < NW; ++k)
+            if (lane == k) reinterpret_cast<uint32_t*>(srow)[k] = w[k];
+    }
+    __device__ __forceinline__ void bscale(uint16_t b) {
+        if (store) g.bscale(b);
+        reinterpret_cast<uint16_t*>(srow + nib_off + 16 * NW)[0] = b;
+    }
+    __device__ __forceinline__ void nib(const uint32_t (&nw)[NW], int lane) {
+        if (store) g.nib(nw, lane);
+#pragma unroll
+        for (int k = 0; k < NW; ++k)
+            if ((lane & 7) == 0)
+                reinterpret_cast<uint32_t*>(srow + nib_off + 16 * k)[lane >> 3] = nw[k] ^ 0x88888888u;
+    }
+    __device__ __forceinline__ void rscale(uint16_t b) {
+        if (store) g.rscale(b);
+        reinterpret_cast<uint16_t*>(srow + nib_off + 16 * NW)[1] = b;
+    }
+};
+
+template <int D, typename Cfg>
+__device__ __noinline__ void encode_append_row(const DecodeArgs& a, int slot, bool store, uint8_t* smem) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;  // warp 0: K, warp 1: V
+    uint8_t* srow = smem + Cfg::NEW_OFF + warp * Cfg::NEWROW_B;
+    if (a.append_res == BC_RES_NONE) {
+        // binary append: the staged residual is code 0 (offset-binary 0x8) with scale 0
+        if (lane < D / 8) reinterpret_cast<uint32_t*>(srow + Cfg::NEWSIGN_B)[lane] = 0x88888888u;
+        if (lane == 0) reinterpret_cast<uint16_t*>(srow + Cfg::NEWSIGN_B + D / 2)[1] = 0;
+    }
+    float x[D / 32];
+    load_vec<D / 32>((warp == 0 ? a.new_k : a.new_v) + (int64_t)slot * D, lane, x);
+    StagedRowSink<D / 32> sink{{warp == 0 ? a.K : a.V, (int64_t)slot * a.kv_stride + a.append_pos}, srow,
+                               Cfg::NEWSIGN_B, store};
+    switch (a.append_res) {
+        case BC_RES_NONE: encode_row<D / 32, BC_RES_NONE>(x, lane, a.head_dim, sink); break;
+        case BC_RES_FP16_SCALE: encode_row<D / 32, BC_RES_FP16_SCALE>(x, lane, a.head_dim, sink); break;
+        default: encode_row<D / 32, BC_RES_FP32_SCALE>(x, lane, a.head_dim, sink); break;
+    }
+}
+
+// Overwrite key kk of a landed stage with the staged rows (one warp).
+template <int D, bool COMP, typename Cfg>
+__device__ __noinline__ void patch_stage_row(uint8_t* sb, int kk, const uint8_t* smem) {
+    constexpr int NWD = D / 32;
+    const int lane = threadIdx.x & 31;
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+        const uint8_t* srow = smem + Cfg::NEW_OFF + j * Cfg::NEWROW_B;
+        const uint16_t* sc = reinterpret_cast<const uint16_t*>(srow + Cfg::NEWSIGN_B + D / 2);
+        const int off_sign = j ? Cfg::OFF_VSIGN : Cfg::OFF_KSIGN, off_bs = j ? Cfg::OFF_VBS : Cfg::OFF_KBS;
+        if (lane < NWD)
+            reinterpret_cast<uint32_t*>(sb + off_sign)[kk * NWD + lane] = reinterpret_cast<const uint32_t*>(srow)[lane];
+        if (lane == 0) reinterpret_cast<uint16_t*>(sb + off_bs)[kk] = sc[0];
+        if (COMP) {
+            const int off_nib = j ? Cfg::OFF_VNIB : Cfg::OFF_KNIB, off_rs = j ? Cfg::OFF_VRS : Cfg::OFF_KRS;
+            if (lane < NWD)
+                *reinterpret_cast<uint4*>(sb + off_nib + nib_chunk_offset(kk, lane, D)) =
+                    reinterpret_cast<const uint4*>(srow + Cfg::NEWSIGN_B)[lane];
+            if (lane == 0) reinterpret_cast<uint16_t*>(sb + off_rs)[kk] = sc[1];
+        }
+    }
+    // the stage is refilled by the async proxy later: order these writes first
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    __syncwarp();
+}
+
+// ---------------------------------------------------------------------------
 // Plane-layout kernel.  Thread 0 keeps the ring full: at iteration `it` it
 // refills the stage consumed at iteration it-LAG once all four warps have
 // released it (per-stage "empty" mbarrier, one arrival per warp).  Warps
 // otherwise run free: no CTA-wide barrier per tile.
 // ---------------------------------------------------------------------------
-template <int D, int GC, bool COMP>
-__global__ void __launch_bounds__(kDecThreads) k_decode_planes(const DecodeArgs a) {
+template <int D, int GC, bool COMP, bool STEP = false>
+__global__ void __launch_bounds__(kDecThreads, STEP ? DecCfg<D, GC, COMP>::STEP_MIN_CTAS : 0)
+    k_decode_planes(const DecodeArgs a) {
     using Cfg = DecCfg<D, GC, COMP>;
     constexpr int NS = Cfg::NS, LAG = Cfg::LAG, T = Cfg::T;
     extern __shared__ __align__(128) uint8_t smem_raw[];
@@ -655,6 +753,19 @@ __global__ void __launch_bounds__(kDecThreads) k_decode_planes(const DecodeArgs 
     if (tid == 0)
         for (int t = 0; t < min(NS, n_tiles); ++t) issue(t, t);
 
+    // fused step: does this CTA's key range hold the append position?
+    // The owning warp patches tile patch_it at key patch_kk (patch_it = -1: not this warp).
+    int patch_it = -1, patch_kk = 0;
+    if constexpr (STEP) {
+        const bool appends = a.append_pos >= s_begin && a.append_pos < s_end;
+        if (appends && warp < 2) encode_append_row<D, Cfg>(a, slot, hg == 0, smem);  // staged before the barriers below
+        const int rel = a.append_pos - s_begin;
+        if (appends && (rel % T) / 32 == warp) {
+            patch_it = rel / T;
+            patch_kk = rel % T;
+        }
+    }
+
     QState<D, GC> qs;
     prepare_query<D, GC, COMP, Cfg>(a, slot, hg, smem, qs);
     SoftState<GC> st;
@@ -676,6 +787,9 @@ __global__ void __launch_bounds__(kDecThreads) k_decode_planes(const DecodeArgs 
         if (!ok) *abort_flag = 1;
         if (*abort_flag) break;
         const int nk = min(T, n_keys - it * T);
+        if constexpr (STEP) {
+            if (it == patch_it) patch_stage_row<D, COMP, Cfg>(smem + stage * Cfg::STAGE_B, patch_kk, smem);
+        }
         consume_warp_tile<D, GC, COMP, Cfg>(qs, st, smem + stage * Cfg::STAGE_B, warp * 32, nk);
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[stage]);
@@ -873,58 +987,66 @@ size_t ws_bound(int n_slots, int group, int seq_len, int d) {
     return best;
 }
 
+enum Variant { kVarPlanes = 0, kVarRecords = 1, kVarStep = 2 };
+
 template <int D, int GC, bool COMP>
-int launch_decode(const DecodeArgs& a, bool records, cudaStream_t st) {
+int launch_decode(const DecodeArgs& a, int var, cudaStream_t st) {
     using Cfg = DecCfg<D, GC, COMP>;
     const unsigned grid = (unsigned)((int64_t)a.n_slots * a.n_hgroups * a.n_splits);
     if (grid == 0) return BC_OK;
     if constexpr (GC == 1) {
-        if (records) {
+        if (var == kVarRecords) {
             k_decode_records<D, GC, COMP><<<grid, kDecThreads, Cfg::SMEM_B, st>>>(a);
             BC_LAUNCH_CHECK();
             return BC_OK;
         }
     }
-    k_decode_planes<D, GC, COMP><<<grid, kDecThreads, Cfg::SMEM_B, st>>>(a);
+    if (var == kVarStep)
+        k_decode_planes<D, GC, COMP, true><<<grid, kDecThreads, Cfg::SMEM_B, st>>>(a);
+    else
+        k_decode_planes<D, GC, COMP, false><<<grid, kDecThreads, Cfg::SMEM_B, st>>>(a);
     BC_LAUNCH_CHECK();
     return BC_OK;
 }
 
-// Sets the dynamic shared-memory limit of both kernel variants on the current
+template <typename K>
+int set_smem_and_occupancy(K kernel, int smem) {
+    int per_sm = 1;
+    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kDecThreads, smem);
+    return per_sm;
+}
+
+// Sets the dynamic shared-memory limit of the kernel variant on the current
 // device (once per device) and returns the resident-CTA capacity of the GPU.
 template <int D, int GC, bool COMP>
-int capacity_of(bool records) {
+int capacity_of(int var) {
     using Cfg = DecCfg<D, GC, COMP>;
     constexpr int kMaxDev = 64;
-    static int cap[2][kMaxDev] = {};
+    static int cap[3][kMaxDev] = {};
     int dev = 0;
     cudaGetDevice(&dev);
-    if (dev >= 0 && dev < kMaxDev && cap[records][dev] > 0) return cap[records][dev];
+    if (dev >= 0 && dev < kMaxDev && cap[var][dev] > 0) return cap[var][dev];
     int sms = 148, per_sm = 1;
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     bool done = false;
     if constexpr (GC == 1) {
-        if (records) {
-            cudaFuncSetAttribute(k_decode_records<D, GC, COMP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 Cfg::SMEM_B);
-            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_decode_records<D, GC, COMP>, kDecThreads,
-                                                          Cfg::SMEM_B);
+        if (var == kVarRecords) {
+            per_sm = set_smem_and_occupancy(k_decode_records<D, GC, COMP>, Cfg::SMEM_B);
             done = true;
         }
     }
-    if (!done) {
-        cudaFuncSetAttribute(k_decode_planes<D, GC, COMP>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_B);
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_decode_planes<D, GC, COMP>, kDecThreads,
-                                                      Cfg::SMEM_B);
-    }
+    if (!done)
+        per_sm = (var == kVarStep) ? set_smem_and_occupancy(k_decode_planes<D, GC, COMP, true>, Cfg::SMEM_B)
+                                   : set_smem_and_occupancy(k_decode_planes<D, GC, COMP, false>, Cfg::SMEM_B);
     const int c = sms * max(1, per_sm);
-    if (dev >= 0 && dev < kMaxDev) cap[records][dev] = c;
+    if (dev >= 0 && dev < kMaxDev) cap[var][dev] = c;
     return c;
 }
 
 template <int D, int GC, bool COMP>
-int run_decode_t(DecodeArgs a, bool records, void* ws, size_t ws_bytes, cudaStream_t st) {
-    const int cap = min(capacity_of<D, GC, COMP>(records), kMaxCtasPlan);
+int run_decode_t(DecodeArgs a, int var, void* ws, size_t ws_bytes, cudaStream_t st) {
+    const int cap = min(capacity_of<D, GC, COMP>(var), kMaxCtasPlan);
     Plan p = make_plan(a.n_slots, a.group, a.seq_len, D, COMP, cap);
     a.n_splits = p.n_splits;
     a.keys_per_split = p.keys_per_split;
@@ -942,28 +1064,28 @@ int run_decode_t(DecodeArgs a, bool records, void* ws, size_t ws_bytes, cudaStre
         a.ws_part = nullptr;
         a.ws_cnt = nullptr;
     }
-    return launch_decode<D, GC, COMP>(a, records, st);
+    return launch_decode<D, GC, COMP>(a, var, st);
 }
 
 template <int D>
-int run_decode_d(const DecodeArgs& a, bool comp, bool records, void* ws, size_t wsb, cudaStream_t st) {
+int run_decode_d(const DecodeArgs& a, bool comp, int var, void* ws, size_t wsb, cudaStream_t st) {
     switch (heads_per_cta(a.group, D, comp)) {
         case 1:
-            return comp ? run_decode_t<D, 1, true>(a, records, ws, wsb, st) : run_decode_t<D, 1, false>(a, records, ws, wsb, st);
+            return comp ? run_decode_t<D, 1, true>(a, var, ws, wsb, st) : run_decode_t<D, 1, false>(a, var, ws, wsb, st);
         case 2:
-            return comp ? run_decode_t<D, 2, true>(a, records, ws, wsb, st) : run_decode_t<D, 2, false>(a, records, ws, wsb, st);
+            return comp ? run_decode_t<D, 2, true>(a, var, ws, wsb, st) : run_decode_t<D, 2, false>(a, var, ws, wsb, st);
         default:
-            if constexpr (D <= 128) return run_decode_t<D, 4, false>(a, records, ws, wsb, st);
+            if constexpr (D <= 128) return run_decode_t<D, 4, false>(a, var, ws, wsb, st);
             return BC_ERR_UNSUPPORTED;
     }
 }
 
-int run_decode(const DecodeArgs& a, bool comp, bool records, void* ws, size_t wsb, cudaStream_t st) {
+int run_decode(const DecodeArgs& a, bool comp, int var, void* ws, size_t wsb, cudaStream_t st) {
     switch (a.head_dim) {
-        case 32: return run_decode_d<32>(a, comp, records, ws, wsb, st);
-        case 64: return run_decode_d<64>(a, comp, records, ws, wsb, st);
-        case 128: return run_decode_d<128>(a, comp, records, ws, wsb, st);
-        case 256: return run_decode_d<256>(a, comp, records, ws, wsb, st);
+        case 32: return run_decode_d<32>(a, comp, var, ws, wsb, st);
+        case 64: return run_decode_d<64>(a, comp, var, ws, wsb, st);
+        case 128: return run_decode_d<128>(a, comp, var, ws, wsb, st);
+        case 256: return run_decode_d<256>(a, comp, var, ws, wsb, st);
         default: return BC_ERR_UNSUPPORTED;
     }
 }
@@ -990,9 +1112,9 @@ size_t bc_decode_workspace_bytes(int n_slots, int group, int seq_len, int head_d
     return ws_bound(n_slots, group, seq_len, head_dim);
 }
 
-int bc_decode_attention(const void* q, bc_kv_planes K, bc_kv_planes V, void* out, float* partial, int n_slots,
-                        int group, int seq_len, int64_t kv_stride, int head_dim, int mode, void* workspace,
-                        size_t workspace_bytes, void* stream) {
+static int check_decode_args(const void* q, const bc_kv_planes& K, const bc_kv_planes& V, const void* out,
+                             const float* partial, int n_slots, int group, int seq_len, int64_t kv_stride,
+                             int head_dim, int mode) {
     if (!bc_valid_head_dim(head_dim)) return BC_ERR_HEAD_DIM;
     if (head_dim != 32 && head_dim != 64 && head_dim != 128 && head_dim != 256) return BC_ERR_UNSUPPORTED;
     if (!valid_group(group)) return BC_ERR_UNSUPPORTED;
@@ -1008,6 +1130,11 @@ int bc_decode_attention(const void* q, bc_kv_planes K, bc_kv_planes V, void* out
     for (int i = 0; i < (comp ? 8 : 4); ++i)
         if (!bc_aligned(ptrs[i], 16)) return BC_ERR_ALIGN;
     if (!bc_aligned(q, 2) || (out && !bc_aligned(out, 2)) || (partial && !bc_aligned(partial, 4))) return BC_ERR_ALIGN;
+    return BC_OK;
+}
+
+static DecodeArgs decode_args(const void* q, bc_kv_planes K, bc_kv_planes V, void* out, float* partial, int n_slots,
+                              int group, int seq_len, int64_t kv_stride, int head_dim) {
     DecodeArgs a{};
     a.q = (const __half*)q;
     a.K = K;
@@ -1019,7 +1146,41 @@ int bc_decode_attention(const void* q, bc_kv_planes K, bc_kv_planes V, void* out
     a.seq_len = seq_len;
     a.kv_stride = kv_stride;
     a.head_dim = head_dim;
-    return run_decode(a, comp, false, workspace, workspace_bytes, (cudaStream_t)stream);
+    a.append_pos = -1;
+    return a;
+}
+
+int bc_decode_attention(const void* q, bc_kv_planes K, bc_kv_planes V, void* out, float* partial, int n_slots,
+                        int group, int seq_len, int64_t kv_stride, int head_dim, int mode, void* workspace,
+                        size_t workspace_bytes, void* stream) {
+    const int rc = check_decode_args(q, K, V, out, partial, n_slots, group, seq_len, kv_stride, head_dim, mode);
+    if (rc != BC_OK || n_slots == 0) return rc;
+    const DecodeArgs a = decode_args(q, K, V, out, partial, n_slots, group, seq_len, kv_stride, head_dim);
+    return run_decode(a, mode == BC_MODE_COMPENSATED, kVarPlanes, workspace, workspace_bytes, (cudaStream_t)stream);
+}
+
+int bc_decode_step(const void* q, const void* new_k, const void* new_v, bc_kv_planes K, bc_kv_planes V, void* out,
+                   float* partial, int n_slots, int group, int seq_len, int64_t kv_stride, int head_dim, int mode,
+                   int append_pos, int append_res, void* workspace, size_t workspace_bytes, void* stream) {
+    const int rc = check_decode_args(q, K, V, out, partial, n_slots, group, seq_len, kv_stride, head_dim, mode);
+    if (rc != BC_OK || n_slots == 0) return rc;
+    if (append_pos < -1 || append_pos >= seq_len) return BC_ERR_ARG;
+    DecodeArgs a = decode_args(q, K, V, out, partial, n_slots, group, seq_len, kv_stride, head_dim);
+    if (append_pos >= 0) {
+        if (append_res != BC_RES_NONE && append_res != BC_RES_FP16_SCALE && append_res != BC_RES_FP32_SCALE)
+            return BC_ERR_ARG;
+        // compensated attention reads the residual of the appended row
+        if (mode == BC_MODE_COMPENSATED && append_res == BC_RES_NONE) return BC_ERR_ARG;
+        if (!new_k || !new_v) return BC_ERR_ARG;
+        if (append_res != BC_RES_NONE && (!K.nib || !K.rscale || !V.nib || !V.rscale)) return BC_ERR_ARG;
+        if (append_res != BC_RES_NONE && (!bc_aligned(K.nib, 16) || !bc_aligned(V.nib, 16))) return BC_ERR_ALIGN;
+        if (!bc_aligned(new_k, 2) || !bc_aligned(new_v, 2)) return BC_ERR_ALIGN;
+        a.new_k = (const __half*)new_k;
+        a.new_v = (const __half*)new_v;
+        a.append_pos = append_pos;
+        a.append_res = append_res;
+    }
+    return run_decode(a, mode == BC_MODE_COMPENSATED, kVarStep, workspace, workspace_bytes, (cudaStream_t)stream);
 }
 
 size_t bc_attention_workspace_bytes(int batch, int n_heads, int seq_len, int head_dim) {
@@ -1051,7 +1212,7 @@ static int record_attention(const void* q, const void* kb, const void* kr, const
     a.seq_len = seq_len;
     a.kv_stride = seq_len;
     a.head_dim = head_dim;
-    return run_decode(a, comp, true, ws, wsb, (cudaStream_t)stream);
+    return run_decode(a, comp, kVarRecords, ws, wsb, (cudaStream_t)stream);
 }
 
 int bc_binary_attention(const void* q, const void* k_bin, const void* v_bin, void* out, int batch, int n_heads,

@@ -1,92 +1,11 @@
 // Encoders: sign-bit packing + mean|x| scale, INT4 residual, online (decode
 // step) append, and record <-> plane converters.  sm_100a.
 //
-// One warp encodes one vector.  Lane l holds elements l + 32k (k < head_dim/32),
-// so __ballot_sync(x >= 0) yields sign word k directly (bit i%32 of word i/32,
-// reference binary_encode.cu:36-39), and the mean-|x| reduction is evaluated in
-// exactly the reference's order: per-thread strided sums over a 128-thread
-// block followed by the stride-halving tree (binary_encode.cu:32-50).  Both
-// divisions (sum / head_dim and 7 / absmax) are written as in the reference
-// with runtime operands and the library is compiled with --use_fast_math like
-// the reference, so they lower to the same instruction and the encodings are
-// bit-identical.
-#include "common.cuh"
+// The warp-level encoders themselves live in encode_core.cuh (one warp per
+// vector, reference summation order, bit-identical to the reference kernels).
+#include "encode_core.cuh"
 
 namespace bc {
-
-template <int NW>
-struct WarpVec {
-    float x[NW];
-};
-
-template <int NW>
-__device__ __forceinline__ void load_vec(const __half* __restrict__ v, int lane, float (&x)[NW]) {
-#pragma unroll
-    for (int k = 0; k < NW; ++k) x[k] = __half2float(v[32 * k + lane]);
-}
-
-template <int NW>
-__device__ __forceinline__ void sign_words(const float (&x)[NW], uint32_t (&w)[NW]) {
-#pragma unroll
-    for (int k = 0; k < NW; ++k) w[k] = __ballot_sync(0xffffffffu, x[k] >= 0.0f);
-}
-
-// Sum of |x_i| in the reference block order (see file comment).  Thread t of
-// the reference's 128-thread block owns t and t + 128; here t = lane + 32k.
-template <int NW>
-__device__ __forceinline__ float tree_abs_sum(const float (&x)[NW]) {
-    float p7[4];
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-        float s = 0.0f;
-        if (k < NW) s += fabsf(x[k]);
-        if (k + 4 < NW) s += fabsf(x[k + 4]);
-        p7[k] = s;
-    }
-    const float p6a = p7[0] + p7[2];  // stride 64
-    const float p6b = p7[1] + p7[3];
-    float v = p6a + p6b;              // stride 32
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);  // strides 16..1
-    return v;
-}
-
-// INT4 residual of x against sign bits w and binary scale s (residual.cu:30-77,
-// online_encode.cu:85-119).  On return lanes 8m (m < 4) hold nibble word 4k+m
-// in nw[k] (8 codes, element 8j low nibble first) and lanes 4m (m < 8) hold the
-// 16-bit pair of bytes 16k+2m, 16k+2m+1 in nh[k].
-template <int NW>
-__device__ __forceinline__ float quantise_residual(const float (&x)[NW], const uint32_t (&w)[NW], float s, int lane,
-                                                   uint32_t (&nw)[NW], uint32_t (&nh)[NW]) {
-    float r[NW];
-    float lm = 0.0f;
-#pragma unroll
-    for (int k = 0; k < NW; ++k) {
-        const uint32_t bit = (w[k] >> lane) & 1u;
-        const float rec = bit ? s : -s;
-        r[k] = x[k] - rec;
-        lm = fmaxf(lm, fabsf(r[k]));
-    }
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) lm = fmaxf(lm, __shfl_xor_sync(0xffffffffu, lm, off));
-    const float absmax = lm;
-    const float inv_absmax = (absmax > 0.0f) ? (7.0f / absmax) : 0.0f;
-#pragma unroll
-    for (int k = 0; k < NW; ++k) {
-        int q = __float2int_rn(r[k] * inv_absmax);
-        q = max(-7, min(7, q));
-        const uint32_t nb = (uint32_t)q & 0xFu;
-        const uint32_t hi = __shfl_down_sync(0xffffffffu, nb, 1);
-        const uint32_t byte = nb | (hi << 4);
-        const uint32_t t1 = byte | (__shfl_down_sync(0xffffffffu, byte, 2) << 8);
-        const uint32_t t2 = t1 | (__shfl_down_sync(0xffffffffu, t1, 4) << 16);
-        nh[k] = t1;
-        nw[k] = t2;
-    }
-    return absmax;
-}
-
-__device__ __forceinline__ uint16_t f2h_bits(float f) { return __half_as_ushort(__float2half(f)); }
 
 // ---------------------------------------------------------------------------
 // Reference-record writers
@@ -113,27 +32,6 @@ __device__ __forceinline__ void store_resvec(uint8_t* rec, const uint32_t (&nh)[
         if ((lane & 3) == 0) rh[8 * k + (lane >> 2)] = (uint16_t)nh[k];
     for (int i = 8 * NW + lane; i < 64; i += 32) rh[i] = 0;  // unused nibbles zeroed
     if (lane == 0) rh[64] = scale;
-}
-
-// ---------------------------------------------------------------------------
-// Plane writers
-// ---------------------------------------------------------------------------
-template <int NW>
-__device__ __forceinline__ void store_sign_row(uint32_t* row, const uint32_t (&w)[NW], int lane) {
-#pragma unroll
-    for (int k = 0; k < NW; ++k)
-        if (lane == k) row[k] = w[k];
-}
-
-// Nibble word 4k+m of plane row `row` (chunk k, word m), interleaved layout,
-// stored offset-binary (each nibble holds code + 8).
-template <int NW>
-__device__ __forceinline__ void store_nib_row(uint8_t* plane, int64_t row, const uint32_t (&nw)[NW], int lane) {
-#pragma unroll
-    for (int k = 0; k < NW; ++k)
-        if ((lane & 7) == 0)
-            *reinterpret_cast<uint32_t*>(plane + nib_chunk_offset(row, k, 32 * NW) + 4 * (lane >> 3)) =
-                nw[k] ^ 0x88888888u;  // offset-binary: code + 8
 }
 
 // ---------------------------------------------------------------------------
@@ -199,25 +97,6 @@ __global__ void __launch_bounds__(kEncWarps * 32) k_online_encode_rec(const __ha
     }
 }
 
-// Encode one vector into plane row `row`.
-template <int NW, int RES>
-__device__ __forceinline__ void encode_row_planes(const float (&x)[NW], int lane, int head_dim, bc_kv_planes P,
-                                                  int64_t row) {
-    uint32_t w[NW];
-    sign_words<NW>(x, w);
-    const float mean_abs = tree_abs_sum<NW>(x) / (float)head_dim;
-    const uint16_t sb = f2h_bits(mean_abs);
-    store_sign_row<NW>(reinterpret_cast<uint32_t*>(P.sign) + row * NW, w, lane);
-    if (lane == 0) reinterpret_cast<uint16_t*>(P.bscale)[row] = sb;
-    if (RES != BC_RES_NONE) {
-        const float s = (RES == BC_RES_FP16_SCALE) ? __half2float(__ushort_as_half(sb)) : mean_abs;
-        uint32_t nw[NW], nh[NW];
-        const float absmax = quantise_residual<NW>(x, w, s, lane, nw, nh);
-        store_nib_row<NW>(reinterpret_cast<uint8_t*>(P.nib), row, nw, lane);
-        if (lane == 0) reinterpret_cast<uint16_t*>(P.rscale)[row] = f2h_bits(absmax);
-    }
-}
-
 template <int NW, int RES>
 __global__ void __launch_bounds__(kEncWarps * 32) k_encode_planes(const __half* __restrict__ src, bc_kv_planes P,
                                                                   int n_slots, int seq_len, int64_t kv_stride,
@@ -225,11 +104,19 @@ __global__ void __launch_bounds__(kEncWarps * 32) k_encode_planes(const __half* 
     const int lane = threadIdx.x & 31;
     const int64_t n = (int64_t)n_slots * seq_len;
     const int64_t nwarps = (int64_t)gridDim.x * kEncWarps;
-    for (int64_t v = (int64_t)blockIdx.x * kEncWarps + (threadIdx.x >> 5); v < n; v += nwarps) {
-        float x[NW];
-        load_vec<NW>(src + v * head_dim, lane, x);
-        const int64_t slot = v / seq_len, s = v - slot * seq_len;
-        encode_row_planes<NW, RES>(x, lane, head_dim, P, slot * kv_stride + s);
+    for (int64_t v0 = ((int64_t)blockIdx.x * kEncWarps + (threadIdx.x >> 5)) * kVecsPerWarp; v0 < n;
+         v0 += nwarps * kVecsPerWarp) {
+        float x[kVecsPerWarp][NW];
+#pragma unroll
+        for (int j = 0; j < kVecsPerWarp; ++j)
+            if (v0 + j < n) load_vec<NW>(src + (v0 + j) * head_dim, lane, x[j]);
+#pragma unroll
+        for (int j = 0; j < kVecsPerWarp; ++j) {
+            const int64_t v = v0 + j;
+            if (v >= n) break;  // warp-uniform
+            const int64_t slot = v / seq_len, s = v - slot * seq_len;
+            encode_row_planes<NW, RES>(x[j], lane, head_dim, P, slot * kv_stride + s);
+        }
     }
 }
 
@@ -399,7 +286,8 @@ int bc_encode_planes(const void* src, bc_kv_planes out, int n_slots, int seq_len
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     const int64_t max_blocks = (int64_t)sms * 8;
-    const unsigned blocks = (unsigned)(enc_blocks(n) < max_blocks ? enc_blocks(n) : max_blocks);
+    const int64_t want = (n + (int64_t)kEncWarps * kVecsPerWarp - 1) / ((int64_t)kEncWarps * kVecsPerWarp);
+    const unsigned blocks = (unsigned)(want < max_blocks ? want : max_blocks);
     cudaStream_t st = (cudaStream_t)stream;
     switch (residual_mode) {
         case BC_RES_NONE:

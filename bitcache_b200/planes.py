@@ -167,6 +167,40 @@ def decode_attention(q: torch.Tensor, K: Planes, V: Planes, seq_len: int, mode: 
     return out
 
 
+def decode_step(q: torch.Tensor, k: torch.Tensor | None, v: torch.Tensor | None, K: Planes, V: Planes,
+                seq_len: int, append_pos: int, mode: int = MODE_COMPENSATED, residual_mode: int = RES_FP32_SCALE,
+                out: torch.Tensor | None = None, partial: torch.Tensor | None = None,
+                want_out: bool = True) -> torch.Tensor | None:
+    """Fused decode step: append k, v ([n_slots, head_dim]) at append_pos with residual_mode
+    arithmetic, then attend q over keys [0, seq_len), in one launch (bc_decode_step).
+    append_pos = -1 (k, v None) attends only.  Results equal append_kv + decode_attention."""
+    _check_half(q, "Q")
+    if append_pos >= 0:
+        _check_half(k, "K")
+        _check_half(v, "V")
+    d = q.shape[-1]
+    n_heads = q.numel() // d
+    n_slots = K.n_slots
+    group = n_heads // n_slots
+    if group * n_slots != n_heads:
+        raise RuntimeError("number of query heads must be a multiple of the number of KV slots")
+    if append_pos >= 0 and (k.numel() != n_slots * d or v.numel() != n_slots * d):
+        raise RuntimeError("k and v must hold one head_dim row per KV slot")
+    if want_out and out is None:
+        out = torch.empty((n_heads, d), dtype=torch.float16, device=q.device)
+    lib = _lib.load()
+    st = _stream(q)
+    wsb = lib.bc_decode_workspace_bytes(n_slots, group, seq_len, d)
+    ws = _lib.workspace(q.device, st, wsb, ("decode", n_slots, group))
+    _lib.check(lib.bc_decode_step(q.data_ptr(), _lib.ptr(k) if append_pos >= 0 else None,
+                                  _lib.ptr(v) if append_pos >= 0 else None, K.c(), V.c(),
+                                  _lib.ptr(out) if want_out else None, _lib.ptr(partial), n_slots, group, seq_len,
+                                  K.kv_stride, d, mode, append_pos, residual_mode, _lib.ptr(ws),
+                                  ws.numel() if ws is not None else 0, st),
+               "decode_step")
+    return out
+
+
 def keep_count(seq_len: int, fraction: float) -> int:
     """Number of residuals kept per slot for a keep fraction (rounded to nearest, ties up)."""
     return int(seq_len * fraction + 0.5)

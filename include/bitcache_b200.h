@@ -153,6 +153,19 @@ int bc_decode_attention(const void* q, bc_kv_planes K, bc_kv_planes V, void* out
                         int group, int seq_len, int64_t kv_stride, int head_dim, int mode, void* workspace,
                         size_t workspace_bytes, void* stream);
 
+/* Fused decode step: bc_append_kv of new_k / new_v (fp16 [n_slots][head_dim]) at plane
+ * position append_pos with append_res arithmetic, then bc_decode_attention over keys
+ * [0, seq_len), in ONE launch.  Replaces the reference's BitCache.append followed by
+ * BitCache.attend (bitcache/__init__.py:95-148: two online_encode_token launches and one
+ * attention launch).  Results are identical to bc_append_kv + bc_decode_attention: the
+ * planes receive the same bytes, and the appended row is attended from the encoder's
+ * output, not re-read.  append_pos = -1 appends nothing (plain decode); otherwise
+ * 0 <= append_pos < seq_len, and compensated attention needs append_res != BC_RES_NONE.
+ * Workspace as bc_decode_workspace_bytes. */
+int bc_decode_step(const void* q, const void* new_k, const void* new_v, bc_kv_planes K, bc_kv_planes V, void* out,
+                   float* partial, int n_slots, int group, int seq_len, int64_t kv_stride, int head_dim, int mode,
+                   int append_pos, int append_res, void* workspace, size_t workspace_bytes, void* stream);
+
 /* Allocation-free bc_decode_attention, for callers that cannot allocate
  * device memory where they run attention (an engine that reserves all of its
  * GPU memory at start-up and forbids allocation in the decode loop, or a

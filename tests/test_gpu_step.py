@@ -1,0 +1,180 @@
+"""GPU: the fused decode step (bc_decode_step: append + attend in one launch)
+against the two-launch path it replaces (bc_append_kv + bc_decode_attention)
+and against the C oracle.  The planes must receive identical bytes; the
+outputs must agree within the north-star tolerance (the step kernel may plan a
+different split count, which only reorders the fp32 split-K sums)."""
+import numpy as np
+import pytest
+import torch
+
+from bitcache_b200 import BitCache, planes
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+MAX_ABS = 2e-3
+MIN_COS = 0.9999
+
+
+def close(got, want, label=""):
+    g = got.float().cpu().numpy().astype(np.float64).ravel()
+    w = want.float().cpu().numpy().astype(np.float64).ravel() if torch.is_tensor(want) else want.astype(np.float64).ravel()
+    err = float(np.max(np.abs(g - w))) if g.size else 0.0
+    cos = float(g @ w / (np.linalg.norm(g) * np.linalg.norm(w) + 1e-30)) if g.size else 1.0
+    assert err <= MAX_ABS, f"{label}: max-abs {err:.3g}"
+    if np.linalg.norm(w) > 1e-6:
+        assert cos >= MIN_COS, f"{label}: cosine {cos:.6f}"
+
+
+def planes_equal(A, B, seq_len, comp):
+    assert torch.equal(A.sign[:, :seq_len], B.sign[:, :seq_len])
+    assert torch.equal(A.bscale[:, :seq_len], B.bscale[:, :seq_len])
+    if comp:
+        assert torch.equal(A.nib_rows()[:, :seq_len], B.nib_rows()[:, :seq_len])
+        assert torch.equal(A.rscale[:, :seq_len], B.rscale[:, :seq_len])
+
+
+def filled_pair(slots, stride, d, comp, S0, cuda, seed):
+    g = torch.Generator().manual_seed(seed)
+    x = [(torch.randn(slots, S0, d, generator=g) * 0.5).half().to(cuda) for _ in range(2)]
+    out = []
+    for _ in range(2):
+        K = planes.Planes.empty(slots, stride, d, comp, cuda)
+        V = planes.Planes.empty(slots, stride, d, comp, cuda)
+        if S0:
+            rm = planes.RES_FP32_SCALE if comp else planes.RES_NONE
+            planes.encode_planes(x[0], K, rm)
+            planes.encode_planes(x[1], V, rm)
+        out.append((K, V))
+    return out
+
+
+# (slots, group, d, comp, S0 already cached, max_seq): the step appends at S0 (growing)
+# or, with a full ring, at a position inside the range.
+CASES = [
+    (4, 1, 128, True, 1000, 4096),    # append at the end, several splits
+    (4, 1, 128, True, 0, 64),         # first token: seq_len 1
+    (2, 1, 64, True, 127, 512),       # append lands on a tile's last key
+    (2, 1, 64, True, 128, 512),       # ... and on a tile's first key
+    (3, 4, 128, True, 777, 1024),     # grouped-query: head groups 1.. patch without storing
+    (2, 8, 128, False, 2047, 4096),   # binary, four heads per CTA
+    (2, 2, 256, True, 300, 512),
+    (5, 1, 32, True, 4095, 8192),
+    (1, 1, 128, False, 65, 128),
+]
+
+
+@pytest.mark.parametrize("slots,group,d,comp,S0,max_seq", CASES)
+def test_step_equals_append_then_attend(cuda, slots, group, d, comp, S0, max_seq):
+    stride = planes.round_stride(max_seq)
+    (K1, V1), (K2, V2) = filled_pair(slots, stride, d, comp, S0, cuda, seed=S0 + d)
+    g = torch.Generator().manual_seed(99 + S0)
+    q = (torch.randn(slots * group, d, generator=g) * 0.5).half().to(cuda)
+    k = (torch.randn(slots, d, generator=g) * 0.5).half().to(cuda)
+    v = (torch.randn(slots, d, generator=g) * 0.5).half().to(cuda)
+    mode = planes.MODE_COMPENSATED if comp else planes.MODE_BINARY
+    rm = planes.RES_FP32_SCALE if comp else planes.RES_NONE
+    S = S0 + 1
+    got = planes.decode_step(q, k, v, K1, V1, S, S0, mode, rm)
+    planes.append_kv(k, v, K2, V2, S0, rm)
+    want = planes.decode_attention(q, K2, V2, S, mode)
+    torch.cuda.synchronize()
+    planes_equal(K1, K2, S, comp)
+    planes_equal(V1, V2, S, comp)
+    close(got, want, f"step slots{slots} g{group} d{d} comp={comp} S0={S0}")
+
+
+@pytest.mark.parametrize("pos", [0, 5, 128, 999, 1023])
+@pytest.mark.parametrize("group", [1, 4])
+def test_step_full_ring_overwrites_inside_range(cuda, pos, group):
+    """Full ring: the appended row replaces a cached one; every other CTA must
+    keep reading the old rows, the owner of pos must attend the new one."""
+    slots, d, S = 3, 128, 1024
+    (K1, V1), (K2, V2) = filled_pair(slots, S, d, True, S, cuda, seed=pos)
+    g = torch.Generator().manual_seed(pos + 7)
+    q = (torch.randn(slots * group, d, generator=g) * 0.5).half().to(cuda)
+    k = (torch.randn(slots, d, generator=g) * 2.0).half().to(cuda)  # a large row: its effect is visible
+    v = (torch.randn(slots, d, generator=g) * 2.0).half().to(cuda)
+    got = planes.decode_step(q, k, v, K1, V1, S, pos)
+    before = planes.decode_attention(q, K2, V2, S)
+    planes.append_kv(k, v, K2, V2, pos)
+    want = planes.decode_attention(q, K2, V2, S)
+    torch.cuda.synchronize()
+    planes_equal(K1, K2, S, True)
+    planes_equal(V1, V2, S, True)
+    close(got, want, f"ring pos={pos} group={group}")
+    assert (got.float() - before.float()).abs().max() > 1e-3  # the new row did change the answer
+
+
+def test_step_res_fp16_scale_and_no_append(cuda):
+    slots, d, S0 = 4, 64, 300
+    (K1, V1), (K2, V2) = filled_pair(slots, 512, d, True, S0, cuda, seed=3)
+    g = torch.Generator().manual_seed(4)
+    q = (torch.randn(slots, d, generator=g) * 0.5).half().to(cuda)
+    k = (torch.randn(slots, d, generator=g) * 0.5).half().to(cuda)
+    v = (torch.randn(slots, d, generator=g) * 0.5).half().to(cuda)
+    got = planes.decode_step(q, k, v, K1, V1, S0 + 1, S0, residual_mode=planes.RES_FP16_SCALE)
+    planes.append_kv(k, v, K2, V2, S0, planes.RES_FP16_SCALE)
+    want = planes.decode_attention(q, K2, V2, S0 + 1)
+    torch.cuda.synchronize()
+    planes_equal(K1, K2, S0 + 1, True)
+    close(got, want, "fp16-scale append")
+    # append_pos = -1: plain attention, planes untouched
+    snap = K1.sign.clone()
+    plain = planes.decode_step(q, None, None, K1, V1, S0 + 1, -1)
+    torch.cuda.synchronize()
+    assert torch.equal(K1.sign, snap)
+    close(plain, want, "no append")
+
+
+def test_step_rejects_bad_arguments(cuda):
+    K = planes.Planes.empty(1, 64, 128, True, cuda)
+    V = planes.Planes.empty(1, 64, 128, True, cuda)
+    q = torch.zeros(1, 128, dtype=torch.float16, device=cuda)
+    k = torch.zeros(1, 128, dtype=torch.float16, device=cuda)
+    with pytest.raises(RuntimeError):
+        planes.decode_step(q, k, k, K, V, 10, 10)  # pos outside [0, seq_len)
+    with pytest.raises(RuntimeError):  # compensated attention needs the appended residual
+        planes.decode_step(q, k, k, K, V, 10, 3, residual_mode=planes.RES_NONE)
+
+
+def test_bitcache_step_matches_append_attend_and_oracle(cuda):
+    """BitCache.step over a ring that wraps, against append+attend on a twin
+    cache (bit-identical planes) and the oracle on the final contents."""
+    B, H, Hkv, d, max_seq, steps = 2, 8, 2, 128, 200, 230
+    g = torch.Generator().manual_seed(17)
+    ks = (torch.randn(steps, B, Hkv, d, generator=g) * 0.5).half()
+    vs = (torch.randn(steps, B, Hkv, d, generator=g) * 0.5).half()
+    qs = (torch.randn(steps, B, H, d, generator=g) * 0.5).half()
+    a = BitCache(B, H, d, max_seq=max_seq, n_kv_heads=Hkv)
+    b = BitCache(B, H, d, max_seq=max_seq, n_kv_heads=Hkv)
+    for t in range(steps):
+        kt, vt, qt = ks[t].to(cuda), vs[t].to(cuda), qs[t].to(cuda)
+        got = a.step(qt, kt, vt)
+        b.append(kt, vt)
+        want = b.attend(qt)
+        if t in (0, 1, 150, max_seq - 1, max_seq, steps - 1):
+            close(got.view(-1, d), want.view(-1, d), f"t={t}")
+    torch.cuda.synchronize()
+    assert a.seq_len == b.seq_len == max_seq
+    for X, Y in zip(a.planes, b.planes):
+        planes_equal(X, Y, max_seq, True)
+    # oracle on the final ring contents: positions hold tokens t with t % max_seq == pos
+    order = [(steps - max_seq + i) for i in range(max_seq)]
+    pos = [t % max_seq for t in order]
+    kk = torch.empty(max_seq, B, Hkv, d, dtype=torch.float16)
+    vv = torch.empty_like(kk)
+    for t, p in zip(order, pos):
+        kk[p] = ks[t]
+        vv[p] = vs[t]
+    n = B * Hkv
+    kf = kk.permute(1, 2, 0, 3).reshape(-1, d).numpy()
+    vf = vv.permute(1, 2, 0, 3).reshape(-1, d).numpy()
+    ow, obs, onb, ors, _ = O.online_encode(kf)
+    vw, vbs, vnb, vrs, _ = O.online_encode(vf)
+    Kp = {"words": ow.reshape(n, max_seq, -1), "bscale": obs.reshape(n, max_seq),
+          "nib": onb.reshape(n, max_seq, -1), "rscale": ors.reshape(n, max_seq)}
+    Vp = {"words": vw.reshape(n, max_seq, -1), "bscale": vbs.reshape(n, max_seq),
+          "nib": vnb.reshape(n, max_seq, -1), "rscale": vrs.reshape(n, max_seq)}
+    want = O.attention(qs[-1].reshape(-1, d).numpy(), Kp, Vp, H // Hkv, max_seq, max_seq, True)
+    close(got.view(-1, d), want.view(np.float16).astype(np.float32), "BitCache.step vs oracle")
