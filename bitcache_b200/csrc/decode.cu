@@ -52,6 +52,9 @@ __device__ unsigned int g_bc_device_error = 0;
 #ifndef BC_DEC_L2_PREFETCH
 #define BC_DEC_L2_PREFETCH 0   // tiles ahead of the ring to prefetch into L2 (0: off)
 #endif
+#ifndef BC_DEC_WAVES
+#define BC_DEC_WAVES 1         // resident waves of CTAs the split plan aims for
+#endif
 #ifndef BC_DEC_V_HOIST
 #define BC_DEC_V_HOIST 0       // 1: the value phase loads all rounds' operands before computing
 #endif
@@ -100,10 +103,11 @@ struct DecCfg {
     static constexpr int NEWSIGN_B = (D / 8 + 15) & ~15;
     static constexpr int NEWROW_B = NEWSIGN_B + D / 2 + 16;
     static constexpr int NEW_OFF = FLAG_OFF + 16;               // [2][NEWROW_B]: K row, V row
-    static constexpr int SMEM_B = NEW_OFF + 2 * NEWROW_B + 128; // + slack to align the base to 128 B
-    // Resident CTAs per SM the plain kernel reaches at head_dim <= 128 with one
-    // head per CTA; the fused-step variant is held to the same register budget.
-    static constexpr int STEP_MIN_CTAS = (GC == 1 && D <= 128) ? (COMP ? 4 : 8) : 0;
+    static constexpr int NEWRAW_OFF = NEW_OFF + 2 * NEWROW_B;   // fp16 [2][D]: the new K, V rows as given
+    static constexpr int SMEM_B = NEWRAW_OFF + 4 * D + 128;     // + slack to align the base to 128 B
+    // Resident CTAs per SM that shared memory allows at head_dim <= 128 with one
+    // head per CTA; the register budget is held to it (0: no bound).
+    static constexpr int MIN_CTAS = (GC == 1 && D <= 128) ? (COMP ? 4 : 8) : 0;
 };
 
 struct DecodeArgs {
@@ -168,16 +172,41 @@ __device__ __forceinline__ uint8_t* aligned_smem(uint8_t* raw) {
 // head as in compensated_attention.cu:65-67.  The residual dot uses q
 // quantised against the head's max |q|: q_i ~= Q16_i * qmax / 32767.
 // ---------------------------------------------------------------------------
+// 16-byte asynchronous global->shared copies (cp.async, no register staging).
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+
+// Start the copy of the CTA's query rows (fp16) into the Q16 area before the
+// ring's first bulk copies are issued, so the few hundred bytes of q are not
+// queued behind them.  Returns false (nothing issued) when the rows are not
+// 16-byte aligned; prepare_query then loads them directly.
+template <int D, int GC, typename Cfg>
+__device__ __forceinline__ bool prefetch_query(const DecodeArgs& a, int slot, int hg, uint8_t* smem) {
+    const __half* src = a.q + ((int64_t)slot * a.group + (int64_t)hg * GC) * D;
+    if ((reinterpret_cast<uintptr_t>(src) & 15) != 0) return false;
+    for (int c = threadIdx.x; c < GC * D / 8; c += kDecThreads) cp_async16(smem + Cfg::Q16_OFF + 16 * c, src + 8 * c);
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    return true;
+}
+
 template <int D, int GC, bool COMP, typename Cfg>
 __device__ __forceinline__ void prepare_query(const DecodeArgs& a, int slot, int hg, uint8_t* smem,
-                                              QState<D, GC>& qs) {
+                                              QState<D, GC>& qs, bool staged = false) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     float* qf = reinterpret_cast<float*>(smem + Cfg::QF_OFF);
     int* q16 = reinterpret_cast<int*>(smem + Cfg::Q16_OFF);
     uint32_t* qsign = reinterpret_cast<uint32_t*>(smem + Cfg::QSIGN_OFF);
     float* qc = reinterpret_cast<float*>(smem + Cfg::QCONST_OFF);
     const int64_t qbase = ((int64_t)slot * a.group + (int64_t)hg * GC) * D;
-    for (int i = tid; i < GC * D; i += kDecThreads) qf[i] = __half2float(a.q[qbase + i]);
+    if (staged) {
+        asm volatile("cp.async.wait_all;" ::: "memory");
+        __syncthreads();
+        const __half* st = reinterpret_cast<const __half*>(smem + Cfg::Q16_OFF);
+        for (int i = tid; i < GC * D; i += kDecThreads) qf[i] = __half2float(st[i]);
+    } else {
+        for (int i = tid; i < GC * D; i += kDecThreads) qf[i] = __half2float(a.q[qbase + i]);
+    }
     __syncthreads();
     const float inv_sqrt_d = 1.0f / sqrtf((float)D);
     if (warp < GC) {
@@ -200,9 +229,16 @@ __device__ __forceinline__ void prepare_query(const DecodeArgs& a, int slot, int
         }
 #pragma unroll
         for (int off = 16; off > 0; off >>= 1) sum16 += __shfl_xor_sync(0xffffffffu, sum16, off);
+        // scale_q: a sequential sum in element order; the elements come from
+        // the lanes by shuffle so their loads do not sit on the add chain
+        float sq = 0.0f;
+#pragma unroll 1
+        for (int k = 0; k < D / 32; ++k) {
+            const float v = fabsf(qf[g * D + 32 * k + lane]);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) sq += __shfl_sync(0xffffffffu, v, j);
+        }
         if (lane == 0) {
-            float sq = 0.0f;
-            for (int i = 0; i < D; ++i) sq += fabsf(qf[g * D + i]);
             sq /= (float)D;
             qc[g * 4 + 0] = sq * inv_sqrt_d * kLog2e;
             qc[g * 4 + 1] = (mx / 32767.0f) * (1.0f / 7.0f) * inv_sqrt_d * kLog2e;
@@ -552,18 +588,39 @@ __device__ __forceinline__ void finish_cta(const DecodeArgs& a, int slot, int hg
     __syncthreads();
     if (!s_last) return;
     __threadfence();
+    // Splits are combined in chunks of kComb: the chunk's loads are all in
+    // flight together (one L2 round trip per chunk instead of two per split),
+    // then merged into a running (M, L, O).  With n_splits <= kComb this is
+    // the plain max-then-sum in split order.
+    constexpr int kComb = 16;
     for (int idx = tid; idx < GC * D; idx += kDecThreads) {
         const int g = idx / D, i = idx % D;
         const int64_t h = head0 + g;
         const float* base = a.ws_part + h * a.n_splits * (D + 2);
-        float M = -INFINITY;
-        for (int j = 0; j < a.n_splits; ++j) M = fmaxf(M, __ldcg(base + (size_t)j * (D + 2)));
-        float L = 0.0f, O = 0.0f;
-        for (int j = 0; j < a.n_splits; ++j) {
-            const float mj = __ldcg(base + (size_t)j * (D + 2));
-            const float f = (mj == -INFINITY) ? 0.0f : fast_exp2(mj - M);
-            L += __ldcg(base + (size_t)j * (D + 2) + 1) * f;
-            O += __ldcg(base + (size_t)j * (D + 2) + 2 + i) * f;
+        float M = -INFINITY, L = 0.0f, O = 0.0f;
+        for (int j0 = 0; j0 < a.n_splits; j0 += kComb) {
+            float mj[kComb], lj[kComb], oj[kComb];
+#pragma unroll
+            for (int k = 0; k < kComb; ++k) {
+                const bool in = j0 + k < a.n_splits;
+                const float* r = base + (size_t)(j0 + k) * (D + 2);
+                mj[k] = in ? __ldcg(r) : -INFINITY;
+                lj[k] = in ? __ldcg(r + 1) : 0.0f;
+                oj[k] = in ? __ldcg(r + 2 + i) : 0.0f;
+            }
+            float Mn = M;
+#pragma unroll
+            for (int k = 0; k < kComb; ++k) Mn = fmaxf(Mn, mj[k]);
+            const float fo = (M == -INFINITY) ? 0.0f : fast_exp2(M - Mn);
+            L *= fo;
+            O *= fo;
+#pragma unroll
+            for (int k = 0; k < kComb; ++k) {
+                const float f = (mj[k] == -INFINITY) ? 0.0f : fast_exp2(mj[k] - Mn);
+                L += lj[k] * f;
+                O += oj[k] * f;
+            }
+            M = Mn;
         }
         if (a.out) a.out[h * D + i] = __float2half((L > 0.0f) ? O * (1.0f / L) : 0.0f);
         if (a.partial) {
@@ -629,7 +686,8 @@ struct StagedRowSink {
 };
 
 template <int D, typename Cfg>
-__device__ __noinline__ void encode_append_row(const DecodeArgs& a, int slot, bool store, uint8_t* smem) {
+__device__ __noinline__ void encode_append_row(const DecodeArgs& a, int slot, bool store, uint8_t* smem,
+                                               const __half* src) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;  // warp 0: K, warp 1: V
     uint8_t* srow = smem + Cfg::NEW_OFF + warp * Cfg::NEWROW_B;
     if (a.append_res == BC_RES_NONE) {
@@ -638,7 +696,7 @@ __device__ __noinline__ void encode_append_row(const DecodeArgs& a, int slot, bo
         if (lane == 0) reinterpret_cast<uint16_t*>(srow + Cfg::NEWSIGN_B + D / 2)[1] = 0;
     }
     float x[D / 32];
-    load_vec<D / 32>((warp == 0 ? a.new_k : a.new_v) + (int64_t)slot * D, lane, x);
+    load_vec<D / 32>(src, lane, x);
     StagedRowSink<D / 32> sink{{warp == 0 ? a.K : a.V, (int64_t)slot * a.kv_stride + a.append_pos}, srow,
                                Cfg::NEWSIGN_B, store};
     switch (a.append_res) {
@@ -681,7 +739,7 @@ __device__ __noinline__ void patch_stage_row(uint8_t* sb, int kk, const uint8_t*
 // otherwise run free: no CTA-wide barrier per tile.
 // ---------------------------------------------------------------------------
 template <int D, int GC, bool COMP, bool STEP = false>
-__global__ void __launch_bounds__(kDecThreads, STEP ? DecCfg<D, GC, COMP>::STEP_MIN_CTAS : 0)
+__global__ void __launch_bounds__(kDecThreads, DecCfg<D, GC, COMP>::MIN_CTAS)
     k_decode_planes(const DecodeArgs a) {
     using Cfg = DecCfg<D, GC, COMP>;
     constexpr int NS = Cfg::NS, LAG = Cfg::LAG, T = Cfg::T;
@@ -698,6 +756,25 @@ __global__ void __launch_bounds__(kDecThreads, STEP ? DecCfg<D, GC, COMP>::STEP_
     const int s_end = min(a.seq_len, s_begin + a.keys_per_split);
     const int n_keys = max(0, s_end - s_begin);
     const int n_tiles = (n_keys + T - 1) / T;
+
+    // Small inputs first: their copies start before the ring's bulk copies.
+    const bool staged = prefetch_query<D, GC, Cfg>(a, slot, hg, smem);
+    // fused step: does this CTA's key range hold the append position?
+    const bool appends = STEP && a.append_pos >= s_begin && a.append_pos < s_end;
+    const __half* new_src[2] = {nullptr, nullptr};
+    if constexpr (STEP) {
+        if (appends) {
+            const __half* g[2] = {a.new_k + (int64_t)slot * D, a.new_v + (int64_t)slot * D};
+            const bool aligned = ((reinterpret_cast<uintptr_t>(g[0]) | reinterpret_cast<uintptr_t>(g[1])) & 15) == 0;
+            __half* raw = reinterpret_cast<__half*>(smem + Cfg::NEWRAW_OFF);
+            for (int j = 0; j < 2; ++j) {
+                new_src[j] = aligned ? raw + j * D : g[j];
+                if (aligned)
+                    for (int c = tid; c < D / 8; c += kDecThreads) cp_async16(raw + j * D + 8 * c, g[j] + 8 * c);
+            }
+            asm volatile("cp.async.commit_group;" ::: "memory");
+        }
+    }
 
     if (tid == 0) {
         for (int s = 0; s < NS; ++s) {
@@ -753,21 +830,25 @@ __global__ void __launch_bounds__(kDecThreads, STEP ? DecCfg<D, GC, COMP>::STEP_
     if (tid == 0)
         for (int t = 0; t < min(NS, n_tiles); ++t) issue(t, t);
 
-    // fused step: does this CTA's key range hold the append position?
-    // The owning warp patches tile patch_it at key patch_kk (patch_it = -1: not this warp).
+    QState<D, GC> qs;
+    prepare_query<D, GC, COMP, Cfg>(a, slot, hg, smem, qs, staged);
+
+    // Fused step: warps 0 and 1 encode the new K and V row; the owning warp
+    // patches tile patch_it at key patch_kk (patch_it = -1: not this warp).
     int patch_it = -1, patch_kk = 0;
     if constexpr (STEP) {
-        const bool appends = a.append_pos >= s_begin && a.append_pos < s_end;
-        if (appends && warp < 2) encode_append_row<D, Cfg>(a, slot, hg == 0, smem);  // staged before the barriers below
-        const int rel = a.append_pos - s_begin;
-        if (appends && (rel % T) / 32 == warp) {
-            patch_it = rel / T;
-            patch_kk = rel % T;
+        if (appends) {
+            asm volatile("cp.async.wait_all;" ::: "memory");
+            __syncthreads();
+            if (warp < 2) encode_append_row<D, Cfg>(a, slot, hg == 0, smem, new_src[warp]);
+            __syncthreads();
+            const int rel = a.append_pos - s_begin;
+            if ((rel % T) / 32 == warp) {
+                patch_it = rel / T;
+                patch_kk = rel % T;
+            }
         }
     }
-
-    QState<D, GC> qs;
-    prepare_query<D, GC, COMP, Cfg>(a, slot, hg, smem, qs);
     SoftState<GC> st;
     init_soft<GC>(st);
 
@@ -961,7 +1042,7 @@ Plan make_plan(int n_slots, int group, int seq_len, int d, bool comp, int capaci
     const int n_tiles = max(1, (seq_len + p.tile - 1) / p.tile);
     const int64_t units = (int64_t)n_slots * p.n_hgroups;
     int splits = 1;
-    if (units < capacity) splits = (int)(capacity / units);
+    if (units < capacity) splits = (int)((int64_t)capacity * BC_DEC_WAVES / units);
     splits = max(1, min(splits, n_tiles));
     const int tiles_per_split = (n_tiles + splits - 1) / splits;
     p.keys_per_split = tiles_per_split * p.tile;
