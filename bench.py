@@ -54,6 +54,8 @@ def parse():
     ap.add_argument("--cpu-sample-s", type=float, default=12.0)
     ap.add_argument("--profile", action="store_true",
                     help="small profiling run: one cache copy, only the decode kernel, warmup+steps launches")
+    ap.add_argument("--profile-seq", type=int, default=0,
+                    help="with --profile: override the config's sequence length (a smaller capture)")
     return ap.parse_args()
 
 
@@ -199,7 +201,7 @@ def run_profile(args):
 
     dev = torch.device("cuda", 0)
     comp = not args.binary
-    w = workloads.make(args.config, device=dev)
+    w = workloads.make(args.config, device=dev, **({"seq_len": args.profile_seq} if args.profile_seq else {}))
     S, d, n = w.seq_len, w.head_dim, w.n_slots
     K = planes.Planes.empty(n, planes.round_stride(S), d, comp, dev, zero=False)
     V = planes.Planes.empty(n, planes.round_stride(S), d, comp, dev, zero=False)

@@ -55,9 +55,6 @@ __device__ unsigned int g_bc_device_error = 0;
 #ifndef BC_DEC_WAVES
 #define BC_DEC_WAVES 1         // resident waves of CTAs the split plan aims for
 #endif
-#ifndef BC_DEC_V_HOIST
-#define BC_DEC_V_HOIST 0       // 1: the value phase loads all rounds' operands before computing
-#endif
 
 constexpr int kDecThreads = 128;  // 4 warps
 constexpr int kWarps = kDecThreads / 32;
@@ -70,7 +67,11 @@ constexpr int kAccShift = 64;     // accumulators hold value * 2^-64
 template <int D, int GC, bool COMP>
 struct DecCfg {
     static constexpr int NWD = D / 32;       // sign words (and 16-byte nibble chunks) per key
-    static constexpr int QPK = NWD;          // value-phase lanes per key (32 dims each)
+    // Value phase: each lane accumulates DL dims of a key, 32 with one head per
+    // CTA, 16 with several (so GC heads' accumulators fit the register budget).
+    static constexpr int DL = (GC == 1) ? 32 : 16;
+    static constexpr int NP = DL / 2;        // f32x2 accumulator pairs per lane and head part
+    static constexpr int QPK = D / DL;       // value-phase lanes per key
     static constexpr int KPW = 32 / QPK;     // value-phase keys in parallel per warp
     static constexpr int NS = (D == 256) ? 2 : BC_DEC_STAGES;  // ring stages
     static constexpr int LAG = 1;            // refill the stage consumed one tile ago
@@ -107,7 +108,7 @@ struct DecCfg {
     static constexpr int SMEM_B = NEWRAW_OFF + 4 * D + 128;     // + slack to align the base to 128 B
     // Resident CTAs per SM that shared memory allows at head_dim <= 128 with one
     // head per CTA; the register budget is held to it (0: no bound).
-    static constexpr int MIN_CTAS = (GC == 1 && D <= 128) ? (COMP ? 4 : 8) : 0;
+    static constexpr int MIN_CTAS = (D > 128) ? 0 : (GC == 1 && !COMP) ? 8 : 4;
 };
 
 struct DecodeArgs {
@@ -143,24 +144,21 @@ struct QState {
     int off8[GC];
 };
 
-// Value accumulators.  Pair p holds dims (p, p+16) of the lane's 32-dim
+// Value accumulators.  Pair p holds dims (p, p + NP) of the lane's DL-dim
 // chunk.  Sign part: sum of 2a*b (a = w*scale_v) scaled by 2^(p-64), because
 // sign bit p enters as the denormal 2^(p-149) and the coefficient is the
 // same 2a*2^85 for every p.  Residual part: sum of c*u (c = w*res_scale_v/7,
-// u = code + 8) scaled by 2^(4(p%4)-64), the nibble's in-register position.
-// Keeping the two parts apart lets every FFMA2 of a key share one
-// coefficient; the fixed scales are removed once per CTA.
-// With several query heads per CTA (grouped-query caches) each head keeps one
-// combined accumulator instead (value * 2^-64), and every FFMA2 carries its
-// dim pair's power-of-two factor in the coefficient: that halves the
-// accumulator registers so up to four heads share one extraction of each key.
-template <int GC>
+// u = code + 8) scaled by 2^(4(p%4) - 64), the nibble's in-register position
+// (nibbles 4-7 of a word are taken from its upper half, which keeps every
+// masked field below bit 23, the linear denormal range).  Keeping the two
+// parts apart lets every FFMA2 of a key share one coefficient; the fixed
+// scales are removed once per CTA.
+template <int GC, int NP>
 struct SoftState {
-    static constexpr bool kSplit = (GC == 1);
     float m[GC];         // running max (log2 units), uniform across the warp
     float l[GC], t[GC];  // per lane: sum of weights and sum of (a + 8c) of the lane's own keys
-    f2 acc_s[GC][16];                   // split: sign part; combined: whole value
-    f2 acc_n[kSplit ? GC : 1][16];      // split only: residual part
+    f2 acc_s[GC][NP];    // sign part
+    f2 acc_n[GC][NP];    // residual part
 };
 
 __device__ __forceinline__ uint8_t* aligned_smem(uint8_t* raw) {
@@ -296,17 +294,17 @@ __device__ __forceinline__ void prepare_query(const DecodeArgs& a, int slot, int
 #endif
 }
 
-template <int GC>
-__device__ __forceinline__ void init_soft(SoftState<GC>& st) {
+template <int GC, int NP>
+__device__ __forceinline__ void init_soft(SoftState<GC, NP>& st) {
 #pragma unroll
     for (int g = 0; g < GC; ++g) {
         st.m[g] = -INFINITY;
         st.l[g] = 0.0f;
         st.t[g] = 0.0f;
 #pragma unroll
-        for (int p = 0; p < 16; ++p) {
+        for (int p = 0; p < NP; ++p) {
             st.acc_s[g][p] = f2{0.0f, 0.0f};
-            if constexpr (SoftState<GC>::kSplit) st.acc_n[g][p] = f2{0.0f, 0.0f};
+            st.acc_n[g][p] = f2{0.0f, 0.0f};
         }
     }
 }
@@ -324,9 +322,9 @@ __device__ __forceinline__ void init_soft(SoftState<GC>& st) {
 // Nibbles are stored offset-binary (u = code + 8), so no XOR is needed here.
 // ---------------------------------------------------------------------------
 template <int D, int GC, bool COMP, typename Cfg>
-__device__ __forceinline__ void consume_warp_tile(const QState<D, GC>& qs, SoftState<GC>& st, const uint8_t* sb,
-                                                  int kw, int nk) {
-    constexpr int NWD = Cfg::NWD, QPK = Cfg::QPK, KPW = Cfg::KPW;
+__device__ __forceinline__ void consume_warp_tile(const QState<D, GC>& qs, SoftState<GC, Cfg::NP>& st,
+                                                  const uint8_t* sb, int kw, int nk) {
+    constexpr int NWD = Cfg::NWD, QPK = Cfg::QPK, KPW = Cfg::KPW, NP = Cfg::NP;
     const int lane = threadIdx.x & 31;
     const int kk = kw + lane;
     const bool valid = kk < nk;
@@ -407,9 +405,9 @@ __device__ __forceinline__ void consume_warp_tile(const QState<D, GC>& qs, SoftS
             st.t[g] *= alpha;
             const f2 al = {alpha, alpha};
 #pragma unroll
-            for (int p = 0; p < 16; ++p) {
+            for (int p = 0; p < NP; ++p) {
                 fmul2(st.acc_s[g][p], al);
-                if constexpr (COMP && SoftState<GC>::kSplit) fmul2(st.acc_n[g][p], al);
+                if constexpr (COMP) fmul2(st.acc_n[g][p], al);
             }
         }
         const float wt = valid ? fast_exp2(s2[g] - st.m[g]) : 0.0f;
@@ -427,66 +425,79 @@ __device__ __forceinline__ void consume_warp_tile(const QState<D, GC>& qs, SoftS
     }
     // ---- value phase -----------------------------------------------------------
     const int grp = lane % KPW, qt = lane / KPW;
-#if BC_DEC_V_HOIST
-    uint32_t vs_all[QPK];
-    uint4 vn_all[QPK];
+    if constexpr (Cfg::DL == 32) {
 #pragma unroll
-    for (int r = 0; r < QPK; ++r) {
-        const int kv = kw + grp + r * KPW;
-        vs_all[r] = reinterpret_cast<const uint32_t*>(sb + Cfg::OFF_VSIGN)[kv * NWD + qt];
-        vn_all[r] = COMP ? *reinterpret_cast<const uint4*>(sb + Cfg::OFF_VNIB + nib_chunk_offset(kv, qt, D))
-                         : make_uint4(0, 0, 0, 0);
-    }
-#endif
+        for (int r = 0; r < QPK; ++r) {
+            const int src = grp + r * KPW;
+            const int kv = kw + src;
+            const uint32_t vs = reinterpret_cast<const uint32_t*>(sb + Cfg::OFF_VSIGN)[kv * NWD + qt];
+            const uint32_t vs_hi = vs >> 16;
+            uint32_t nw[4] = {0, 0, 0, 0}, nh[4] = {0, 0, 0, 0};
+            if (COMP) {
+                const uint4 vn = *reinterpret_cast<const uint4*>(sb + Cfg::OFF_VNIB + nib_chunk_offset(kv, qt, D));
+                nw[0] = vn.x; nw[1] = vn.y; nw[2] = vn.z; nw[3] = vn.w;
 #pragma unroll
-    for (int r = 0; r < QPK; ++r) {
-        const int src = grp + r * KPW;
-#if BC_DEC_V_HOIST
-        const uint32_t vs = vs_all[r];
-#else
-        const int kv = kw + src;
-        const uint32_t vs = reinterpret_cast<const uint32_t*>(sb + Cfg::OFF_VSIGN)[kv * NWD + qt];
-#endif
-        const uint32_t vs_hi = vs >> 16;
-        uint32_t nw[4] = {0, 0, 0, 0}, nh[4] = {0, 0, 0, 0};
-        if (COMP) {
-#if BC_DEC_V_HOIST
-            const uint4 vn = vn_all[r];
-#else
-            const uint4 vn = *reinterpret_cast<const uint4*>(sb + Cfg::OFF_VNIB + nib_chunk_offset(kv, qt, D));
-#endif
-            nw[0] = vn.x; nw[1] = vn.y; nw[2] = vn.z; nw[3] = vn.w;
+                for (int k = 0; k < 4; ++k) nh[k] = nw[k] >> 16;
+            }
 #pragma unroll
-            for (int k = 0; k < 4; ++k) nh[k] = nw[k] >> 16;
-        }
+            for (int g = 0; g < GC; ++g) {
+                const float a0 = __shfl_sync(0xffffffffu, A0[g], src);
+                const float c0 = COMP ? __shfl_sync(0xffffffffu, C0[g], src) : 0.0f;
+                const f2 a2 = {a0, a0}, c2 = {c0, c0};
 #pragma unroll
-        for (int g = 0; g < GC; ++g) {
-            const float a0 = __shfl_sync(0xffffffffu, A0[g], src);
-            const float c0 = COMP ? __shfl_sync(0xffffffffu, C0[g], src) : 0.0f;
-            const f2 a2 = {a0, a0}, c2 = {c0, c0};
-#pragma unroll
-            for (int p = 0; p < 16; ++p) {
-                // sign bits of dims p and p+16, each the exact denormal 2^(p-149)
-                const f2 y = {bits_f(vs & (1u << p)), bits_f(vs_hi & (1u << p))};
-                if constexpr (SoftState<GC>::kSplit) {
+                for (int p = 0; p < 16; ++p) {
+                    // sign bits of dims p and p+16, each the exact denormal 2^(p-149)
+                    const f2 y = {bits_f(vs & (1u << p)), bits_f(vs_hi & (1u << p))};
                     ffma2(st.acc_s[g][p], a2, y);
-                } else {
-                    const float ap = a0 * exp2i(-p);
-                    ffma2(st.acc_s[g][p], f2{ap, ap}, y);
-                }
-                if (COMP) {
-                    // codes of dims p (word p/8) and p+16 (word 2 + p/8), nibble p%8:
-                    // nibbles 0-3 from the word, 4-7 from its upper half
-                    const int t = p & 7, kw0 = p >> 3;
-                    const uint32_t srca = (t < 4) ? nw[kw0] : nh[kw0];
-                    const uint32_t srcb = (t < 4) ? nw[2 + kw0] : nh[2 + kw0];
-                    const int sh = 4 * (t & 3);
-                    const f2 x = {bits_f(srca & (0xFu << sh)), bits_f(srcb & (0xFu << sh))};
-                    if constexpr (SoftState<GC>::kSplit) {
+                    if (COMP) {
+                        // codes of dims p (word p/8) and p+16 (word 2 + p/8), nibble p%8:
+                        // nibbles 0-3 from the word, 4-7 from its upper half
+                        const int t = p & 7, kw0 = p >> 3;
+                        const uint32_t srca = (t < 4) ? nw[kw0] : nh[kw0];
+                        const uint32_t srcb = (t < 4) ? nw[2 + kw0] : nh[2 + kw0];
+                        const int sh = 4 * (t & 3);
+                        const f2 x = {bits_f(srca & (0xFu << sh)), bits_f(srcb & (0xFu << sh))};
                         ffma2(st.acc_n[g][p], c2, x);
-                    } else {
-                        const float cp = c0 * exp2i(-sh);
-                        ffma2(st.acc_s[g][p], f2{cp, cp}, x);
+                    }
+                }
+            }
+        }
+    } else {
+        // 16-dim lanes: lane (grp, qt) takes half qt%2 of chunk qt/2.  Within
+        // each 8-key block the chunks alternate between the block's key groups
+        // round by round, so one round's 8-byte nibble loads cover all banks.
+        constexpr int G = KPW < 8 ? 8 / KPW : 1;  // key groups per 8-key block
+        const int c = qt >> 1, h = qt & 1;
+#pragma unroll
+        for (int r = 0; r < QPK; ++r) {
+            const int src = (G > 1) ? 8 * (r / G) + KPW * ((r + c) % G) + grp : grp + r * KPW;
+            const int kv = kw + src;
+            const uint32_t vs = reinterpret_cast<const uint32_t*>(sb + Cfg::OFF_VSIGN)[kv * NWD + c] >> (16 * h);
+            const uint32_t vs_hi = vs >> 8;
+            uint32_t n0 = 0, n1 = 0, nh0 = 0, nh1 = 0;
+            if (COMP) {
+                const uint2 vn = *reinterpret_cast<const uint2*>(sb + Cfg::OFF_VNIB + nib_chunk_offset(kv, c, D) + 8 * h);
+                n0 = vn.x;
+                n1 = vn.y;
+                nh0 = n0 >> 16;
+                nh1 = n1 >> 16;
+            }
+#pragma unroll
+            for (int g = 0; g < GC; ++g) {
+                const float a0 = __shfl_sync(0xffffffffu, A0[g], src);
+                const float c0 = COMP ? __shfl_sync(0xffffffffu, C0[g], src) : 0.0f;
+                const f2 a2 = {a0, a0}, c2 = {c0, c0};
+#pragma unroll
+                for (int p = 0; p < 8; ++p) {
+                    // sign bits of dims p and p+8; codes of dims p (word 0) and p+8
+                    // (word 1), nibble p: nibbles 4-7 from the words' upper halves, so
+                    // every masked field stays in the fp32 denormal range (bits < 23)
+                    const f2 y = {bits_f(vs & (1u << p)), bits_f(vs_hi & (1u << p))};
+                    ffma2(st.acc_s[g][p], a2, y);
+                    if (COMP) {
+                        const int sh = 4 * (p & 3);
+                        const f2 x = {bits_f((p < 4 ? n0 : nh0) & (0xFu << sh)), bits_f((p < 4 ? n1 : nh1) & (0xFu << sh))};
+                        ffma2(st.acc_n[g][p], c2, x);
                     }
                 }
             }
@@ -501,8 +512,8 @@ __device__ __forceinline__ void consume_warp_tile(const QState<D, GC>& qs, SoftS
 // ---------------------------------------------------------------------------
 template <int D, int GC, typename Cfg>
 __device__ __forceinline__ void finish_cta(const DecodeArgs& a, int slot, int hg, int split, uint8_t* smem,
-                                           SoftState<GC>& st) {
-    constexpr int KPW = Cfg::KPW;
+                                           SoftState<GC, Cfg::NP>& st) {
+    constexpr int KPW = Cfg::KPW, DL = Cfg::DL, NP = Cfg::NP;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, qt = lane / KPW;
     __syncthreads();  // ring no longer in use
     float* mg = reinterpret_cast<float*>(smem);  // [warps][GC][D+2]
@@ -514,27 +525,23 @@ __device__ __forceinline__ void finish_cta(const DecodeArgs& a, int slot, int hg
             l += __shfl_xor_sync(0xffffffffu, l, off);
             t += __shfl_xor_sync(0xffffffffu, t, off);
         }
-        float o[32];
+        float o[DL];
 #pragma unroll
-        for (int p = 0; p < 16; ++p) {
-            if constexpr (SoftState<GC>::kSplit) {
-                const float fs = exp2i(kAccShift - p), fn = exp2i(kAccShift - 4 * (p & 3));
-                o[p] = st.acc_s[g][p].x * fs + st.acc_n[g][p].x * fn;
-                o[p + 16] = st.acc_s[g][p].y * fs + st.acc_n[g][p].y * fn;
-            } else {
-                o[p] = st.acc_s[g][p].x * exp2i(kAccShift);
-                o[p + 16] = st.acc_s[g][p].y * exp2i(kAccShift);
-            }
+        for (int p = 0; p < NP; ++p) {
+            const float fs = exp2i(kAccShift - p);
+            const float fn = exp2i(kAccShift - 4 * (p & 3));
+            o[p] = st.acc_s[g][p].x * fs + st.acc_n[g][p].x * fn;
+            o[p + NP] = st.acc_s[g][p].y * fs + st.acc_n[g][p].y * fn;
         }
         // lanes holding the same chunk (same qt) differ in their low log2(KPW) bits
 #pragma unroll
         for (int off = 1; off < KPW; off <<= 1)
 #pragma unroll
-            for (int i = 0; i < 32; ++i) o[i] += __shfl_xor_sync(0xffffffffu, o[i], off);
+            for (int i = 0; i < DL; ++i) o[i] += __shfl_xor_sync(0xffffffffu, o[i], off);
         float* rec = mg + ((size_t)warp * GC + g) * (D + 2);
         if (lane % KPW == 0) {
 #pragma unroll
-            for (int i = 0; i < 32; ++i) rec[2 + 32 * qt + i] = o[i] - t;
+            for (int i = 0; i < DL; ++i) rec[2 + DL * qt + i] = o[i] - t;
         }
         if (lane == 0) {
             rec[0] = st.m[g];
@@ -849,8 +856,8 @@ __global__ void __launch_bounds__(kDecThreads, DecCfg<D, GC, COMP>::MIN_CTAS)
             }
         }
     }
-    SoftState<GC> st;
-    init_soft<GC>(st);
+    SoftState<GC, Cfg::NP> st;
+    init_soft(st);
 
     int it = 0;
     for (; it < n_tiles; ++it) {
@@ -945,8 +952,8 @@ __global__ void __launch_bounds__(kDecThreads) k_decode_records(const DecodeArgs
 
     QState<D, GC> qs;
     prepare_query<D, GC, COMP, Cfg>(a, slot, hg, smem, qs);
-    SoftState<GC> st;
-    init_soft<GC>(st);
+    SoftState<GC, Cfg::NP> st;
+    init_soft(st);
     const int64_t rec_base = (int64_t)slot * a.kv_stride + s_begin;
     for (int it = 0; it < n_tiles; ++it) {
         const int nk = min(T, n_keys - it * T);
@@ -1028,7 +1035,8 @@ int tile_keys(int d) {
 // them all; the CTAs of a slot's remaining head groups, adjacent in the
 // grid, share the KV tiles through L2.
 int heads_per_cta(int group, int d, bool comp) {
-    const int cap = (comp || d > 128) ? 2 : 4;  // register budget without spills
+    (void)d;
+    const int cap = comp ? 2 : 4;  // accumulator registers: 32 per head (compensated), 16 (binary)
     return group < cap ? group : cap;
 }
 
@@ -1156,8 +1164,7 @@ int run_decode_d(const DecodeArgs& a, bool comp, int var, void* ws, size_t wsb, 
         case 2:
             return comp ? run_decode_t<D, 2, true>(a, var, ws, wsb, st) : run_decode_t<D, 2, false>(a, var, ws, wsb, st);
         default:
-            if constexpr (D <= 128) return run_decode_t<D, 4, false>(a, var, ws, wsb, st);
-            return BC_ERR_UNSUPPORTED;
+            return run_decode_t<D, 4, false>(a, var, ws, wsb, st);
     }
 }
 

@@ -86,8 +86,10 @@ def test_c1_golden_vs_kernels(cuda):
 
 
 @pytest.mark.parametrize("group", [2, 4, 8])
-@pytest.mark.parametrize("d", [64, 128])
-def test_gqa_vs_oracle(cuda, group, d):
+@pytest.mark.parametrize("d", [32, 64, 128, 256])
+@pytest.mark.parametrize("comp", [True, False])
+def test_gqa_vs_oracle(cuda, group, d, comp):
+    """Grouped-query heads: 2 (compensated) or 4 (binary) heads per CTA on 16-dim value lanes."""
     slots, S = 3, 700
     g = torch.Generator().manual_seed(group * 10 + d)
     q = (torch.randn(slots * group, d, generator=g) * 0.5).half()
@@ -98,14 +100,15 @@ def test_gqa_vs_oracle(cuda, group, d):
     V = planes.Planes.empty(slots, stride, d, True, cuda)
     planes.encode_planes(k.to(cuda), K, planes.RES_FP16_SCALE)
     planes.encode_planes(v.to(cuda), V, planes.RES_FP16_SCALE)
-    mine = planes.decode_attention(q.to(cuda), K, V, S)
+    mode = planes.MODE_COMPENSATED if comp else planes.MODE_BINARY
+    mine = planes.decode_attention(q.to(cuda), K, V, S, mode)
 
     def host(X):
         return {"words": X.sign.cpu().numpy().view(np.uint32), "bscale": X.bscale.cpu().numpy().view(np.uint16),
                 "nib": X.nib_rows().cpu().numpy(), "rscale": X.rscale.cpu().numpy().view(np.uint16)}
 
-    want = O.attention(q.numpy(), host(K), host(V), group, S, stride, True).view(np.float16).astype(np.float32)
-    close(mine, want, f"gqa g={group} d={d}")
+    want = O.attention(q.numpy(), host(K), host(V), group, S, stride, comp).view(np.float16).astype(np.float32)
+    close(mine, want, f"gqa g={group} d={d} comp={comp}")
 
 
 @pytest.mark.parametrize("S", [0, 1, 7, 8, 9, 129, 1000])
