@@ -21,6 +21,7 @@ BC_ERR_WORKSPACE = 4
 BC_RES_NONE, BC_RES_FP16_SCALE, BC_RES_FP32_SCALE = 0, 1, 2
 BC_MODE_BINARY, BC_MODE_COMPENSATED = 0, 1
 BC_DEVERR_TIMEOUT = 1
+BC_DEVERR_PAGE = 2
 
 c_void_p = ctypes.c_void_p
 c_int = ctypes.c_int
@@ -33,6 +34,13 @@ class KVPlanes(ctypes.Structure):
     """bc_kv_planes: sign, nib, bscale, rscale device pointers."""
 
     _fields_ = [("sign", c_void_p), ("nib", c_void_p), ("bscale", c_void_p), ("rscale", c_void_p)]
+
+
+class PageTable(ctypes.Structure):
+    """bc_page_table: block table pointer and paging geometry."""
+
+    _fields_ = [("pages", c_void_p), ("max_pages", ctypes.c_int32), ("page_size", ctypes.c_int32),
+                ("n_pages", ctypes.c_int32)]
 
 
 _SIGS = {
@@ -61,6 +69,10 @@ _SIGS = {
                                     c_int, c_int, c_void_p, c_size_t, c_void_p]),
     "bc_decode_step": (c_int, [c_void_p, c_void_p, c_void_p, KVPlanes, KVPlanes, c_void_p, c_void_p, c_int, c_int,
                                c_int, c_int64, c_int, c_int, c_int, c_int, c_void_p, c_size_t, c_void_p]),
+    "bc_decode_step_paged": (c_int, [c_void_p, c_void_p, c_void_p, KVPlanes, KVPlanes, c_void_p, c_void_p, PageTable,
+                                     c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_void_p, c_size_t, c_void_p]),
+    "bc_append_kv_paged": (c_int, [c_void_p, c_void_p, KVPlanes, KVPlanes, PageTable, c_int, c_int, c_int64, c_int,
+                                   c_void_p]),
     "bc_decode_noalloc_max_scratch_bytes": (c_size_t, []),
     "bc_decode_attention_noalloc": (c_int, [c_void_p, KVPlanes, KVPlanes, c_void_p, c_void_p, c_int, c_int, c_int,
                                             c_int64, c_int, c_int, c_void_p]),

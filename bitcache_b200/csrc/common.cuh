@@ -165,6 +165,10 @@ __device__ __forceinline__ uint4 ldg_nc_v4(const void* p) {
 
 }  // namespace bc
 
+// Device address of the library's error word on the current device (defined
+// in decode.cu), for kernels of other translation units.
+unsigned int* bc_device_error_ptr();
+
 // ---------------------------------------------------------------------------
 // Host-side helpers shared by the entry points.
 // ---------------------------------------------------------------------------

@@ -49,9 +49,6 @@ __device__ unsigned int g_bc_device_error = 0;
 #ifndef BC_DEC_QPACK_SMEM
 #define BC_DEC_QPACK_SMEM 1    // 1: the score phase reads the query packs from shared memory
 #endif
-#ifndef BC_DEC_L2_PREFETCH
-#define BC_DEC_L2_PREFETCH 0   // tiles ahead of the ring to prefetch into L2 (0: off)
-#endif
 #ifndef BC_DEC_WAVES
 #define BC_DEC_WAVES 1         // resident waves of CTAs the split plan aims for
 #endif
@@ -126,7 +123,19 @@ struct DecodeArgs {
     const __half* new_k;
     const __half* new_v;
     int append_pos, append_res;
+    // paged caches (pages != null): logical position s of slot j lives in plane
+    // row pages[j * max_pages + s / page_size] * page_size + s % page_size
+    const int* pages;
+    int max_pages, page_size, n_pages;
 };
+
+// Plane row of logical position `pos` of `slot`, or -1 for a page id outside
+// the pool (the caller reports BC_DEVERR_PAGE instead of touching memory).
+__device__ __forceinline__ int64_t plane_row(const DecodeArgs& a, int slot, int pos) {
+    if (!a.pages) return (int64_t)slot * a.kv_stride + pos;
+    const int pg = __ldg(a.pages + (int64_t)slot * a.max_pages + pos / a.page_size);
+    return (pg >= 0 && pg < a.n_pages) ? (int64_t)pg * a.page_size + pos % a.page_size : -1;
+}
 
 // Per-lane query state for GC heads.  The score phase handles whole keys, so
 // every lane holds the full query: sign words and, for the residual dot, q
@@ -704,8 +713,12 @@ __device__ __noinline__ void encode_append_row(const DecodeArgs& a, int slot, bo
     }
     float x[D / 32];
     load_vec<D / 32>(src, lane, x);
-    StagedRowSink<D / 32> sink{{warp == 0 ? a.K : a.V, (int64_t)slot * a.kv_stride + a.append_pos}, srow,
-                               Cfg::NEWSIGN_B, store};
+    const int64_t row = plane_row(a, slot, a.append_pos);
+    if (row < 0) {
+        if (store && lane == 0) raise_device_error(&g_bc_device_error, BC_DEVERR_PAGE);
+        store = false;  // attend the staged row, store nothing
+    }
+    StagedRowSink<D / 32> sink{{warp == 0 ? a.K : a.V, row}, srow, Cfg::NEWSIGN_B, store};
     switch (a.append_res) {
         case BC_RES_NONE: encode_row<D / 32, BC_RES_NONE>(x, lane, a.head_dim, sink); break;
         case BC_RES_FP16_SCALE: encode_row<D / 32, BC_RES_FP16_SCALE>(x, lane, a.head_dim, sink); break;
@@ -793,12 +806,26 @@ __global__ void __launch_bounds__(kDecThreads, DecCfg<D, GC, COMP>::MIN_CTAS)
     }
     __syncthreads();
 
-    const int64_t row_base = (int64_t)slot * a.kv_stride + s_begin;
-    auto issue = [&](int tile, int stage) {
+    // Plane row of a tile's first key.  Paged caches (the STEP variant only)
+    // read the block table; tiles never straddle a page, since splits start on
+    // tile boundaries and pages hold a multiple of the tile's 128 positions.
+    auto row_of = [&](int tile) -> int64_t {
+        if constexpr (STEP) return plane_row(a, slot, s_begin + tile * T);
+        return (int64_t)slot * a.kv_stride + s_begin + tile * T;
+    };
+    auto issue = [&](int tile, int stage, int64_t row) {
         const int k0 = tile * T;
         const int nk = min(T, n_keys - k0);
         const int nk8 = (nk + 7) & ~7;
-        const int64_t row = row_base + k0;
+        if constexpr (STEP) {
+            if (row < 0) {
+                // page id outside the pool: complete the stage without a copy and abort
+                raise_device_error(&g_bc_device_error, BC_DEVERR_PAGE);
+                *abort_flag = 1;
+                mbar_arrive(&full[stage]);
+                return;
+            }
+        }
         uint8_t* sbuf = smem + stage * Cfg::STAGE_B;
         const uint32_t sign_b = nk8 * (D / 8), sc_b = nk8 * 2, nib_b = nk8 * (D / 2);
         const uint32_t total = 2 * (sign_b + sc_b + (COMP ? nib_b + sc_b : 0));
@@ -813,29 +840,14 @@ __global__ void __launch_bounds__(kDecThreads, DecCfg<D, GC, COMP>::MIN_CTAS)
             bulk_g2s(sbuf + Cfg::OFF_VNIB, (const uint8_t*)a.V.nib + row * (D / 2), nib_b, &full[stage]);
             bulk_g2s(sbuf + Cfg::OFF_VRS, (const uint8_t*)a.V.rscale + row * 2, sc_b, &full[stage]);
         }
-#if BC_DEC_L2_PREFETCH > 0
-        // Start the HBM reads of a later tile now, into L2, so its ring copy
-        // later finds the data close by without holding shared memory.
-        const int pt = tile + BC_DEC_L2_PREFETCH;
-        if (pt < n_tiles) {
-            const int pk0 = pt * T;
-            const int pn8 = (min(T, n_keys - pk0) + 7) & ~7;
-            const int64_t prow = row_base + pk0;
-            bulk_prefetch_l2((const uint8_t*)a.K.sign + prow * (D / 8), pn8 * (D / 8));
-            bulk_prefetch_l2((const uint8_t*)a.V.sign + prow * (D / 8), pn8 * (D / 8));
-            bulk_prefetch_l2((const uint8_t*)a.K.bscale + prow * 2, pn8 * 2);
-            bulk_prefetch_l2((const uint8_t*)a.V.bscale + prow * 2, pn8 * 2);
-            if (COMP) {
-                bulk_prefetch_l2((const uint8_t*)a.K.nib + prow * (D / 2), pn8 * (D / 2));
-                bulk_prefetch_l2((const uint8_t*)a.V.nib + prow * (D / 2), pn8 * (D / 2));
-                bulk_prefetch_l2((const uint8_t*)a.K.rscale + prow * 2, pn8 * 2);
-                bulk_prefetch_l2((const uint8_t*)a.V.rscale + prow * 2, pn8 * 2);
-            }
-        }
-#endif
     };
-    if (tid == 0)
-        for (int t = 0; t < min(NS, n_tiles); ++t) issue(t, t);
+    // thread 0: the plane row of the next tile to issue, read one refill ahead
+    // (a block-table load in paged caches)
+    int64_t next_row = 0;
+    if (tid == 0) {
+        for (int t = 0; t < min(NS, n_tiles); ++t) issue(t, t, row_of(t));
+        if (STEP && NS < n_tiles) next_row = row_of(NS);
+    }
 
     QState<D, GC> qs;
     prepare_query<D, GC, COMP, Cfg>(a, slot, hg, smem, qs, staged);
@@ -866,7 +878,12 @@ __global__ void __launch_bounds__(kDecThreads, DecCfg<D, GC, COMP>::MIN_CTAS)
             const int old = it - LAG;
             if (mbar_wait_bounded(&empty[old % NS], (uint32_t)(old / NS) & 1u)) {
                 fence_proxy_async_smem();
-                issue(old + NS, old % NS);
+                if constexpr (STEP) {
+                    issue(old + NS, old % NS, next_row);
+                    if (old + NS + 1 < n_tiles) next_row = row_of(old + NS + 1);
+                } else {
+                    issue(old + NS, old % NS, row_of(old + NS));
+                }
             } else {
                 *abort_flag = 1;
             }
@@ -1182,6 +1199,21 @@ bool valid_group(int g) { return g == 1 || g == 2 || g == 4 || g == 8; }
 
 }  // namespace
 
+// Device address of the library's error word, for kernels compiled in other
+// translation units (looked up once per device).
+unsigned int* bc_device_error_ptr() {
+    constexpr int kMaxDev = 64;
+    static unsigned int* ptrs[kMaxDev] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= kMaxDev) return nullptr;
+    if (!ptrs[dev]) {
+        void* p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_bc_device_error) == cudaSuccess) ptrs[dev] = static_cast<unsigned int*>(p);
+    }
+    return ptrs[dev];
+}
+
 extern "C" {
 
 unsigned int bc_get_device_error(int clear) {
@@ -1258,6 +1290,39 @@ int bc_decode_step(const void* q, const void* new_k, const void* new_v, bc_kv_pl
         if (append_res != BC_RES_NONE && append_res != BC_RES_FP16_SCALE && append_res != BC_RES_FP32_SCALE)
             return BC_ERR_ARG;
         // compensated attention reads the residual of the appended row
+        if (mode == BC_MODE_COMPENSATED && append_res == BC_RES_NONE) return BC_ERR_ARG;
+        if (!new_k || !new_v) return BC_ERR_ARG;
+        if (append_res != BC_RES_NONE && (!K.nib || !K.rscale || !V.nib || !V.rscale)) return BC_ERR_ARG;
+        if (append_res != BC_RES_NONE && (!bc_aligned(K.nib, 16) || !bc_aligned(V.nib, 16))) return BC_ERR_ALIGN;
+        if (!bc_aligned(new_k, 2) || !bc_aligned(new_v, 2)) return BC_ERR_ALIGN;
+        a.new_k = (const __half*)new_k;
+        a.new_v = (const __half*)new_v;
+        a.append_pos = append_pos;
+        a.append_res = append_res;
+    }
+    return run_decode(a, mode == BC_MODE_COMPENSATED, kVarStep, workspace, workspace_bytes, (cudaStream_t)stream);
+}
+
+int bc_decode_step_paged(const void* q, const void* new_k, const void* new_v, bc_kv_planes K, bc_kv_planes V,
+                         void* out, float* partial, bc_page_table pt, int n_slots, int group, int seq_len,
+                         int head_dim, int mode, int append_pos, int append_res, void* workspace,
+                         size_t workspace_bytes, void* stream) {
+    if (!pt.pages || pt.page_size <= 0 || pt.page_size % 128 != 0 || pt.n_pages <= 0 || pt.max_pages <= 0)
+        return BC_ERR_ARG;
+    if ((int64_t)pt.max_pages * pt.page_size < seq_len) return BC_ERR_ARG;
+    if (!bc_aligned(pt.pages, 4)) return BC_ERR_ALIGN;
+    // the pool is checked as a contiguous cache of n_pages slots of page_size positions
+    const int rc = check_decode_args(q, K, V, out, partial, n_slots, group, 0, pt.page_size, head_dim, mode);
+    if (rc != BC_OK || n_slots == 0) return rc;
+    if (seq_len < 0 || append_pos < -1 || append_pos >= seq_len) return BC_ERR_ARG;
+    DecodeArgs a = decode_args(q, K, V, out, partial, n_slots, group, seq_len, pt.page_size, head_dim);
+    a.pages = pt.pages;
+    a.max_pages = pt.max_pages;
+    a.page_size = pt.page_size;
+    a.n_pages = pt.n_pages;
+    if (append_pos >= 0) {
+        if (append_res != BC_RES_NONE && append_res != BC_RES_FP16_SCALE && append_res != BC_RES_FP32_SCALE)
+            return BC_ERR_ARG;
         if (mode == BC_MODE_COMPENSATED && append_res == BC_RES_NONE) return BC_ERR_ARG;
         if (!new_k || !new_v) return BC_ERR_ARG;
         if (append_res != BC_RES_NONE && (!K.nib || !K.rscale || !V.nib || !V.rscale)) return BC_ERR_ARG;

@@ -125,15 +125,25 @@ template <int NW, int RES>
 __global__ void __launch_bounds__(kEncWarps * 32) k_append_kv(const __half* __restrict__ k,
                                                               const __half* __restrict__ v, bc_kv_planes K,
                                                               bc_kv_planes V, int n_slots, int head_dim,
-                                                              int64_t kv_stride, int64_t pos) {
+                                                              int64_t kv_stride, int64_t pos, bc_page_table pt,
+                                                              unsigned int* err) {
     const int lane = threadIdx.x & 31;
     const int wid = blockIdx.x * kEncWarps + (threadIdx.x >> 5);
     if (wid >= 2 * n_slots) return;
     const bool is_v = wid >= n_slots;
     const int slot = is_v ? wid - n_slots : wid;
+    int64_t row = (int64_t)slot * kv_stride + pos;
+    if (pt.pages) {  // paged cache: the block table names the page
+        const int pg = __ldg(pt.pages + (int64_t)slot * pt.max_pages + pos / pt.page_size);
+        if (pg < 0 || pg >= pt.n_pages) {
+            if (lane == 0 && err) raise_device_error(err, BC_DEVERR_PAGE);
+            return;
+        }
+        row = (int64_t)pg * pt.page_size + pos % pt.page_size;
+    }
     float x[NW];
     load_vec<NW>((is_v ? v : k) + (int64_t)slot * head_dim, lane, x);
-    encode_row_planes<NW, RES>(x, lane, head_dim, is_v ? V : K, (int64_t)slot * kv_stride + pos);
+    encode_row_planes<NW, RES>(x, lane, head_dim, is_v ? V : K, row);
 }
 
 // Record <-> plane conversion (pure data movement, one warp per vector).
@@ -307,10 +317,12 @@ int bc_encode_planes(const void* src, bc_kv_planes out, int n_slots, int seq_len
     return BC_OK;
 }
 
-int bc_append_kv(const void* k, const void* v, bc_kv_planes K, bc_kv_planes V, int n_slots, int head_dim,
-                 int64_t kv_stride, int64_t pos, int residual_mode, void* stream) {
+static int append_kv(const void* k, const void* v, bc_kv_planes K, bc_kv_planes V, int n_slots, int head_dim,
+                     int64_t kv_stride, int64_t pos, int residual_mode, bc_page_table pt, void* stream) {
     if (!bc_valid_head_dim(head_dim)) return BC_ERR_HEAD_DIM;
-    if (n_slots < 0 || pos < 0 || pos >= kv_stride) return BC_ERR_ARG;
+    if (n_slots < 0 || pos < 0) return BC_ERR_ARG;
+    if (!pt.pages && pos >= kv_stride) return BC_ERR_ARG;
+    if (pt.pages && pos >= (int64_t)pt.max_pages * pt.page_size) return BC_ERR_ARG;
     if (residual_mode != BC_RES_NONE && residual_mode != BC_RES_FP32_SCALE && residual_mode != BC_RES_FP16_SCALE)
         return BC_ERR_ARG;
     if (n_slots == 0) return BC_OK;
@@ -319,24 +331,41 @@ int bc_append_kv(const void* k, const void* v, bc_kv_planes K, bc_kv_planes V, i
     if (rc) return rc;
     rc = check_planes(V, residual_mode != BC_RES_NONE);
     if (rc) return rc;
+    unsigned int* err = pt.pages ? bc_device_error_ptr() : nullptr;
     cudaStream_t st = (cudaStream_t)stream;
     const unsigned blocks = enc_blocks(2 * (int64_t)n_slots);
     switch (residual_mode) {
         case BC_RES_NONE:
             BC_DISPATCH_NW(head_dim, (k_append_kv<NW, BC_RES_NONE><<<blocks, kEncWarps * 32, 0, st>>>(
-                                          (const __half*)k, (const __half*)v, K, V, n_slots, head_dim, kv_stride, pos)));
+                                          (const __half*)k, (const __half*)v, K, V, n_slots, head_dim, kv_stride, pos,
+                                          pt, err)));
             break;
         case BC_RES_FP16_SCALE:
             BC_DISPATCH_NW(head_dim, (k_append_kv<NW, BC_RES_FP16_SCALE><<<blocks, kEncWarps * 32, 0, st>>>(
-                                          (const __half*)k, (const __half*)v, K, V, n_slots, head_dim, kv_stride, pos)));
+                                          (const __half*)k, (const __half*)v, K, V, n_slots, head_dim, kv_stride, pos,
+                                          pt, err)));
             break;
         default:
             BC_DISPATCH_NW(head_dim, (k_append_kv<NW, BC_RES_FP32_SCALE><<<blocks, kEncWarps * 32, 0, st>>>(
-                                          (const __half*)k, (const __half*)v, K, V, n_slots, head_dim, kv_stride, pos)));
+                                          (const __half*)k, (const __half*)v, K, V, n_slots, head_dim, kv_stride, pos,
+                                          pt, err)));
             break;
     }
     BC_LAUNCH_CHECK();
     return BC_OK;
+}
+
+int bc_append_kv(const void* k, const void* v, bc_kv_planes K, bc_kv_planes V, int n_slots, int head_dim,
+                 int64_t kv_stride, int64_t pos, int residual_mode, void* stream) {
+    return append_kv(k, v, K, V, n_slots, head_dim, kv_stride, pos, residual_mode, bc_page_table{}, stream);
+}
+
+int bc_append_kv_paged(const void* k, const void* v, bc_kv_planes K, bc_kv_planes V, bc_page_table pt, int n_slots,
+                       int head_dim, int64_t pos, int residual_mode, void* stream) {
+    if (!pt.pages || pt.page_size <= 0 || pt.page_size % 128 != 0 || pt.n_pages <= 0 || pt.max_pages <= 0)
+        return BC_ERR_ARG;
+    if (!bc_aligned(pt.pages, 4)) return BC_ERR_ALIGN;
+    return append_kv(k, v, K, V, n_slots, head_dim, pt.page_size, pos, residual_mode, pt, stream);
 }
 
 int bc_records_to_planes(const void* binvec, const void* resvec, bc_kv_planes out, int64_t n_vecs, int head_dim,

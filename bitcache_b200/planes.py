@@ -201,6 +201,86 @@ def decode_step(q: torch.Tensor, k: torch.Tensor | None, v: torch.Tensor | None,
     return out
 
 
+@dataclass
+class PageTable:
+    """Block table of a paged cache (bc_page_table).
+
+    The K and V pools are ``Planes`` with ``n_slots = n_pages`` and
+    ``kv_stride = page_size``; logical position ``pos`` of slot ``s`` lives in
+    pool row ``pages[s, pos // page_size] * page_size + pos % page_size``.
+    ``page_size`` is a multiple of 128 (the decode tile)."""
+
+    pages: torch.Tensor  # int32 [n_slots, max_pages], device
+    page_size: int
+    n_pages: int
+
+    def c(self) -> _lib.PageTable:
+        return _lib.PageTable(self.pages.data_ptr(), self.pages.shape[1], self.page_size, self.n_pages)
+
+    @property
+    def n_slots(self) -> int:
+        return self.pages.shape[0]
+
+
+def paginate(P: Planes, pt: PageTable, seq_len: int, pool: Planes | None = None) -> Planes:
+    """Copy positions [0, seq_len) of a contiguous cache into a page pool laid out by pt
+    (page-sized row blocks; the nibble interleave is per 8 rows, so blocks copy as bytes)."""
+    ps = pt.page_size
+    if pool is None:
+        pool = Planes.empty(pt.n_pages, ps, P.head_dim, P.compensated, P.sign.device)
+    table = pt.pages.cpu()
+    for s in range(pt.n_slots):
+        for j in range((seq_len + ps - 1) // ps):
+            pg = int(table[s, j])
+            for name in ("sign", "bscale", "nib", "rscale"):
+                src, dst = getattr(P, name), getattr(pool, name)
+                if src is not None:
+                    dst[pg].copy_(src[s, j * ps:(j + 1) * ps])
+    return pool
+
+
+def decode_step_paged(q: torch.Tensor, k: torch.Tensor | None, v: torch.Tensor | None, K: Planes, V: Planes,
+                      pt: PageTable, seq_len: int, append_pos: int = -1, mode: int = MODE_COMPENSATED,
+                      residual_mode: int = RES_FP32_SCALE, out: torch.Tensor | None = None,
+                      partial: torch.Tensor | None = None, want_out: bool = True) -> torch.Tensor | None:
+    """bc_decode_step_paged: optional append at logical append_pos, then attention over
+    logical keys [0, seq_len) of the paged cache (pools K, V and block table pt)."""
+    _check_half(q, "Q")
+    if append_pos >= 0:
+        _check_half(k, "K")
+        _check_half(v, "V")
+    d = q.shape[-1]
+    n_heads = q.numel() // d
+    n_slots = pt.n_slots
+    group = n_heads // n_slots
+    if group * n_slots != n_heads:
+        raise RuntimeError("number of query heads must be a multiple of the number of KV slots")
+    if want_out and out is None:
+        out = torch.empty((n_heads, d), dtype=torch.float16, device=q.device)
+    lib = _lib.load()
+    st = _stream(q)
+    wsb = lib.bc_decode_workspace_bytes(n_slots, group, seq_len, d)
+    ws = _lib.workspace(q.device, st, wsb, ("decode", n_slots, group))
+    _lib.check(lib.bc_decode_step_paged(q.data_ptr(), _lib.ptr(k) if append_pos >= 0 else None,
+                                        _lib.ptr(v) if append_pos >= 0 else None, K.c(), V.c(),
+                                        _lib.ptr(out) if want_out else None, _lib.ptr(partial), pt.c(), n_slots,
+                                        group, seq_len, d, mode, append_pos, residual_mode, _lib.ptr(ws),
+                                        ws.numel() if ws is not None else 0, st),
+               "decode_step_paged")
+    return out
+
+
+def append_kv_paged(k: torch.Tensor, v: torch.Tensor, K: Planes, V: Planes, pt: PageTable, pos: int,
+                    residual_mode: int = RES_FP32_SCALE) -> None:
+    """bc_append_kv_paged: one K and V token per slot at logical position pos."""
+    _check_half(k, "K")
+    _check_half(v, "V")
+    d = k.shape[-1]
+    lib = _lib.load()
+    _lib.check(lib.bc_append_kv_paged(k.data_ptr(), v.data_ptr(), K.c(), V.c(), pt.c(), pt.n_slots, d, pos,
+                                      residual_mode, _stream(k)), "append_kv_paged")
+
+
 def keep_count(seq_len: int, fraction: float) -> int:
     """Number of residuals kept per slot for a keep fraction (rounded to nearest, ties up)."""
     return int(seq_len * fraction + 0.5)

@@ -55,6 +55,8 @@ extern "C" {
 
 /* device-side error bits, read with bc_get_device_error() */
 #define BC_DEVERR_TIMEOUT 1u /* a bounded wait in a kernel gave up; outputs are invalid */
+#define BC_DEVERR_PAGE 2u    /* a block-table entry named a page outside the pool; that tile
+                                was not read or written and the outputs are invalid */
 
 /* residual modes for the encoders */
 #define BC_RES_NONE 0       /* binary only: sign + bscale */
@@ -165,6 +167,39 @@ int bc_decode_attention(const void* q, bc_kv_planes K, bc_kv_planes V, void* out
 int bc_decode_step(const void* q, const void* new_k, const void* new_v, bc_kv_planes K, bc_kv_planes V, void* out,
                    float* partial, int n_slots, int group, int seq_len, int64_t kv_stride, int head_dim, int mode,
                    int append_pos, int append_res, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---- paged caches ----------------------------------------------------
+ * A paged cache is a pool of pages, each page_size positions of one slot,
+ * stored as planes with n_slots = n_pages and kv_stride = page_size (so page
+ * p is plane rows [p*page_size, (p+1)*page_size)).  A block table maps the
+ * logical page j of slot s to its physical page:
+ *     pages[s*max_pages + j]   (int32, device memory)
+ * Logical position pos of slot s lives in plane row
+ *     pages[s*max_pages + pos/page_size]*page_size + pos%page_size.
+ * page_size must be a multiple of 128 (the decode tile), so a tile never
+ * straddles two pages.  Page ids are checked in the kernels: an id outside
+ * [0, n_pages) is not dereferenced; the kernel raises BC_DEVERR_PAGE instead.
+ * The reference's BitCache is a contiguous ring (bitcache/__init__.py:76-82);
+ * the north star's "paged binary+residual cache" is this layout. */
+typedef struct bc_page_table {
+    const int32_t* pages; /* device, [n_slots][max_pages] */
+    int32_t max_pages;    /* row stride of pages (logical pages per slot) */
+    int32_t page_size;    /* positions per page, a multiple of 128 */
+    int32_t n_pages;      /* pages in the pool: valid ids are 0..n_pages-1 */
+} bc_page_table;
+
+/* bc_decode_step over a paged cache: optional append of new_k/new_v at logical
+ * position append_pos (-1: none), then attention over logical keys [0, seq_len).
+ * K and V are the pools (kv_stride = pt.page_size).  Results are bit-identical
+ * to bc_decode_step on a contiguous cache holding the same rows. */
+int bc_decode_step_paged(const void* q, const void* new_k, const void* new_v, bc_kv_planes K, bc_kv_planes V,
+                         void* out, float* partial, bc_page_table pt, int n_slots, int group, int seq_len,
+                         int head_dim, int mode, int append_pos, int append_res, void* workspace,
+                         size_t workspace_bytes, void* stream);
+
+/* bc_append_kv into a paged cache at logical position pos of every slot. */
+int bc_append_kv_paged(const void* k, const void* v, bc_kv_planes K, bc_kv_planes V, bc_page_table pt, int n_slots,
+                       int head_dim, int64_t pos, int residual_mode, void* stream);
 
 /* Allocation-free bc_decode_attention, for callers that cannot allocate
  * device memory where they run attention (an engine that reserves all of its
