@@ -69,6 +69,8 @@ _SIGS = {
                                     c_int, c_int, c_void_p, c_size_t, c_void_p]),
     "bc_decode_step": (c_int, [c_void_p, c_void_p, c_void_p, KVPlanes, KVPlanes, c_void_p, c_void_p, c_int, c_int,
                                c_int, c_int64, c_int, c_int, c_int, c_int, c_void_p, c_size_t, c_void_p]),
+    "bc_decode_attention_entropy": (c_int, [c_void_p, KVPlanes, KVPlanes, c_void_p, c_void_p, c_void_p, c_int, c_int,
+                                            c_int, c_int64, c_int, c_int, c_void_p, c_size_t, c_void_p]),
     "bc_decode_step_paged": (c_int, [c_void_p, c_void_p, c_void_p, KVPlanes, KVPlanes, c_void_p, c_void_p, PageTable,
                                      c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_void_p, c_size_t, c_void_p]),
     "bc_append_kv_paged": (c_int, [c_void_p, c_void_p, KVPlanes, KVPlanes, PageTable, c_int, c_int, c_int64, c_int,

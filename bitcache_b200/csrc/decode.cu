@@ -91,7 +91,7 @@ struct DecCfg {
     static constexpr int QF_OFF = BODY_B;                       // float q[GC][D]
     static constexpr int Q16_OFF = QF_OFF + GC * D * 4;         // int Q16[GC][D]
     static constexpr int QSIGN_OFF = Q16_OFF + GC * D * 4;      // uint32 [GC][8]
-    static constexpr int QCONST_OFF = QSIGN_OFF + GC * 8 * 4;   // [GC][4]: bco, rco, off8
+    static constexpr int QCONST_OFF = QSIGN_OFF + GC * 8 * 4;   // [GC][4]: bco, rco, off8, eco
     static constexpr int QPK_OFF = QCONST_OFF + GC * 4 * 4;     // uint32 [GC][D/8][4] query packs
     static constexpr int FULL_OFF = QPK_OFF + (BC_DEC_QPACK_SMEM ? GC * (D / 8) * 16 : 0);  // mbarriers
     static constexpr int EMPTY_OFF = FULL_OFF + NS * 8;         // mbarriers: all warps done with a stage
@@ -127,6 +127,10 @@ struct DecodeArgs {
     // row pages[j * max_pages + s / page_size] * page_size + s % page_size
     const int* pages;
     int max_pages, page_size, n_pages;
+    // entropy variant: per query head H of the softmax over the binary scores
+    // without 1/sqrt(d) (reference adaptive_precision.cu:13-130)
+    float* entropy;  // [n_slots * group]
+    float* ws_ent;   // [n_slots * group][n_splits][3] split partials (m, z, w)
 };
 
 // Plane row of logical position `pos` of `slot`, or -1 for a page id outside
@@ -151,6 +155,7 @@ struct QState {
 #endif
     float bco[GC], rco[GC];
     int off8[GC];
+    float eco[GC];  // entropy variant: the query's tree-order mean |q| (adaptive_precision.cu:46-59)
 };
 
 // Value accumulators.  Pair p holds dims (p, p + NP) of the lane's DL-dim
@@ -168,6 +173,7 @@ struct SoftState {
     float l[GC], t[GC];  // per lane: sum of weights and sum of (a + 8c) of the lane's own keys
     f2 acc_s[GC][NP];    // sign part
     f2 acc_n[GC][NP];    // residual part
+    float em[GC], ez[GC], ew[GC];  // entropy variant, per lane: max, sum e^(s-max), sum e^(s-max) s
 };
 
 __device__ __forceinline__ uint8_t* aligned_smem(uint8_t* raw) {
@@ -245,6 +251,14 @@ __device__ __forceinline__ void prepare_query(const DecodeArgs& a, int slot, int
 #pragma unroll
             for (int j = 0; j < 32; ++j) sq += __shfl_sync(0xffffffffu, v, j);
         }
+        {
+            // entropy scale: the reference block's strided sums and stride-halving tree
+            float x[D / 32];
+#pragma unroll
+            for (int k = 0; k < D / 32; ++k) x[k] = qf[g * D + 32 * k + lane];
+            const float te = tree_abs_sum<D / 32>(x) / (float)D;
+            if (lane == 0) qc[g * 4 + 3] = te;
+        }
         if (lane == 0) {
             sq /= (float)D;
             qc[g * 4 + 0] = sq * inv_sqrt_d * kLog2e;
@@ -260,6 +274,7 @@ __device__ __forceinline__ void prepare_query(const DecodeArgs& a, int slot, int
         qs.bco[g] = qc[g * 4 + 0];
         qs.rco[g] = qc[g * 4 + 1];
         qs.off8[g] = reinterpret_cast<const int*>(qc)[g * 4 + 2];
+        qs.eco[g] = qc[g * 4 + 3];
 #if BC_DEC_QPACK_SMEM
         qs.pk = reinterpret_cast<const uint4*>(smem + Cfg::QPK_OFF);
         if (COMP) {
@@ -310,6 +325,9 @@ __device__ __forceinline__ void init_soft(SoftState<GC, NP>& st) {
         st.m[g] = -INFINITY;
         st.l[g] = 0.0f;
         st.t[g] = 0.0f;
+        st.em[g] = -INFINITY;
+        st.ez[g] = 0.0f;
+        st.ew[g] = 0.0f;
 #pragma unroll
         for (int p = 0; p < NP; ++p) {
             st.acc_s[g][p] = f2{0.0f, 0.0f};
@@ -330,7 +348,7 @@ __device__ __forceinline__ void init_soft(SoftState<GC, NP>& st) {
 //     score lane by shuffle.
 // Nibbles are stored offset-binary (u = code + 8), so no XOR is needed here.
 // ---------------------------------------------------------------------------
-template <int D, int GC, bool COMP, typename Cfg>
+template <int D, int GC, bool COMP, typename Cfg, bool ENT = false>
 __device__ __forceinline__ void consume_warp_tile(const QState<D, GC>& qs, SoftState<GC, Cfg::NP>& st,
                                                   const uint8_t* sb, int kw, int nk) {
     constexpr int NWD = Cfg::NWD, QPK = Cfg::QPK, KPW = Cfg::KPW, NP = Cfg::NP;
@@ -397,6 +415,22 @@ __device__ __forceinline__ void consume_warp_tile(const QState<D, GC>& qs, SoftS
         float s = qs.bco[g] * kbs * (float)(D - 2 * pop);
         if (COMP) s = fmaf(qs.rco[g] * krs, (float)(dot[g] - qs.off8[g]), s);
         s2[g] = valid ? s : -INFINITY;
+        if constexpr (ENT) {
+            // xnor_dot without 1/sqrt(d), online per lane (adaptive_precision.cu:69-102)
+            if (valid) {
+                const float sc = qs.eco[g] * kbs * (float)(D - 2 * pop);
+                if (sc > st.em[g]) {
+                    const float f = (st.em[g] == -INFINITY) ? 0.0f : __expf(st.em[g] - sc);
+                    st.ez[g] = st.ez[g] * f + 1.0f;
+                    st.ew[g] = st.ew[g] * f + sc;
+                    st.em[g] = sc;
+                } else {
+                    const float e = __expf(sc - st.em[g]);
+                    st.ez[g] += e;
+                    st.ew[g] += e * sc;
+                }
+            }
+        }
     }
     // ---- lazy rescale, weights -------------------------------------------------
     const float vbs = valid ? __half2float(reinterpret_cast<const __half*>(sb + Cfg::OFF_VBS)[kk]) : 0.0f;
@@ -514,12 +548,28 @@ __device__ __forceinline__ void consume_warp_tile(const QState<D, GC>& qs, SoftS
     }
 }
 
+// Entropy partials (max, sum e^(s-max), sum e^(s-max) s) merge by the
+// log-sum-exp rule; H = log z + max - w / max(z, 1e-12) (adaptive_precision.cu:120-128).
+struct EntPart {
+    float m, z, w;
+};
+
+__device__ __forceinline__ EntPart ent_merge(EntPart a, EntPart b) {
+    const float M = fmaxf(a.m, b.m);
+    if (M == -INFINITY) return a;
+    const float fa = (a.m == -INFINITY) ? 0.0f : __expf(a.m - M);
+    const float fb = (b.m == -INFINITY) ? 0.0f : __expf(b.m - M);
+    return EntPart{M, a.z * fa + b.z * fb, a.w * fa + b.w * fb};
+}
+
+__device__ __forceinline__ float ent_value(EntPart t) { return logf(t.z) + t.m - t.w / fmaxf(t.z, 1e-12f); }
+
 // ---------------------------------------------------------------------------
 // End of a CTA: reduce each warp, merge the warps (log-sum-exp), then either
 // write the outputs (single split) or publish a partial and let the last CTA
 // of the (slot, head group) combine all splits.
 // ---------------------------------------------------------------------------
-template <int D, int GC, typename Cfg>
+template <int D, int GC, typename Cfg, bool ENT = false>
 __device__ __forceinline__ void finish_cta(const DecodeArgs& a, int slot, int hg, int split, uint8_t* smem,
                                            SoftState<GC, Cfg::NP>& st) {
     constexpr int KPW = Cfg::KPW, DL = Cfg::DL, NP = Cfg::NP;
@@ -557,9 +607,37 @@ __device__ __forceinline__ void finish_cta(const DecodeArgs& a, int slot, int hg
             rec[1] = l;
         }
     }
+    __shared__ EntPart s_ent[ENT ? kWarps : 1][ENT ? GC : 1];
+    if constexpr (ENT) {
+#pragma unroll
+        for (int g = 0; g < GC; ++g) {
+            EntPart e{st.em[g], st.ez[g], st.ew[g]};
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1)
+                e = ent_merge(e, EntPart{__shfl_xor_sync(0xffffffffu, e.m, off), __shfl_xor_sync(0xffffffffu, e.z, off),
+                                         __shfl_xor_sync(0xffffffffu, e.w, off)});
+            if (lane == 0) s_ent[warp][g] = e;
+        }
+    }
     __syncthreads();
     const bool single = (a.n_splits == 1);
     const int64_t head0 = (int64_t)slot * a.group + (int64_t)hg * GC;
+    if constexpr (ENT) {
+        if (tid < GC) {
+            EntPart e = s_ent[0][tid];
+#pragma unroll
+            for (int w = 1; w < kWarps; ++w) e = ent_merge(e, s_ent[w][tid]);
+            const int64_t h = head0 + tid;
+            if (single) {
+                a.entropy[h] = ent_value(e);
+            } else {
+                float* p = a.ws_ent + (h * a.n_splits + split) * 3;
+                p[0] = e.m;
+                p[1] = e.z;
+                p[2] = e.w;
+            }
+        }
+    }
     for (int idx = tid; idx < GC * D; idx += kDecThreads) {
         const int g = idx / D, i = idx % D;
         float M = -INFINITY;
@@ -646,6 +724,16 @@ __device__ __forceinline__ void finish_cta(const DecodeArgs& a, int slot, int hg
                 p[1] = L;
             }
             p[2 + i] = O;
+        }
+    }
+    if constexpr (ENT) {
+        if (tid < GC) {
+            const int64_t h = head0 + tid;
+            const float* base = a.ws_ent + h * a.n_splits * 3;
+            EntPart e{-INFINITY, 0.0f, 0.0f};
+            for (int j = 0; j < a.n_splits; ++j)
+                e = ent_merge(e, EntPart{__ldcg(base + 3 * j), __ldcg(base + 3 * j + 1), __ldcg(base + 3 * j + 2)});
+            a.entropy[h] = ent_value(e);
         }
     }
     if (tid == 0) a.ws_cnt[(int64_t)slot * a.n_hgroups + hg] = 0u;  // leave the counter zeroed
@@ -758,9 +846,12 @@ __device__ __noinline__ void patch_stage_row(uint8_t* sb, int kk, const uint8_t*
 // released it (per-stage "empty" mbarrier, one arrival per warp).  Warps
 // otherwise run free: no CTA-wide barrier per tile.
 // ---------------------------------------------------------------------------
-template <int D, int GC, bool COMP, bool STEP = false>
+// VAR: 0 attention, 1 fused decode step (append + attend, paged caches),
+// 2 attention plus the per-head entropy of the binary-score softmax.
+template <int D, int GC, bool COMP, int VAR = 0>
 __global__ void __launch_bounds__(kDecThreads, DecCfg<D, GC, COMP>::MIN_CTAS)
     k_decode_planes(const DecodeArgs a) {
+    constexpr bool STEP = VAR == 1, ENT = VAR == 2;
     using Cfg = DecCfg<D, GC, COMP>;
     constexpr int NS = Cfg::NS, LAG = Cfg::LAG, T = Cfg::T;
     extern __shared__ __align__(128) uint8_t smem_raw[];
@@ -895,7 +986,7 @@ __global__ void __launch_bounds__(kDecThreads, DecCfg<D, GC, COMP>::MIN_CTAS)
         if constexpr (STEP) {
             if (it == patch_it) patch_stage_row<D, COMP, Cfg>(smem + stage * Cfg::STAGE_B, patch_kk, smem);
         }
-        consume_warp_tile<D, GC, COMP, Cfg>(qs, st, smem + stage * Cfg::STAGE_B, warp * 32, nk);
+        consume_warp_tile<D, GC, COMP, Cfg, ENT>(qs, st, smem + stage * Cfg::STAGE_B, warp * 32, nk);
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[stage]);
     }
@@ -911,7 +1002,7 @@ __global__ void __launch_bounds__(kDecThreads, DecCfg<D, GC, COMP>::MIN_CTAS)
         }
         return;
     }
-    finish_cta<D, GC, Cfg>(a, slot, hg, split, smem, st);
+    finish_cta<D, GC, Cfg, ENT>(a, slot, hg, split, smem, st);
 }
 
 // ---------------------------------------------------------------------------
@@ -1075,10 +1166,13 @@ Plan make_plan(int n_slots, int group, int seq_len, int d, bool comp, int capaci
     return p;
 }
 
+// Workspace: ticket counters, then split partials (m, l, o[d]), then the
+// entropy variant's split partials (m, z, w).
 size_t ws_bytes_for(int n_slots, int group, int n_splits, int d, int n_hgroups) {
     const size_t part = (size_t)n_slots * group * n_splits * (d + 2) * sizeof(float);
+    const size_t ent = (size_t)n_slots * group * n_splits * 3 * sizeof(float);
     const size_t cnt = (size_t)n_slots * n_hgroups * sizeof(unsigned);
-    return ((part + 255) & ~(size_t)255) + ((cnt + 255) & ~(size_t)255);
+    return ((part + 255) & ~(size_t)255) + ((cnt + 255) & ~(size_t)255) + ((ent + 255) & ~(size_t)255);
 }
 
 // Workspace bound over both modes: the counter region is sized for one head
@@ -1093,7 +1187,7 @@ size_t ws_bound(int n_slots, int group, int seq_len, int d) {
     return best;
 }
 
-enum Variant { kVarPlanes = 0, kVarRecords = 1, kVarStep = 2 };
+enum Variant { kVarPlanes = 0, kVarRecords = 1, kVarStep = 2, kVarEntropy = 3 };
 
 template <int D, int GC, bool COMP>
 int launch_decode(const DecodeArgs& a, int var, cudaStream_t st) {
@@ -1108,9 +1202,11 @@ int launch_decode(const DecodeArgs& a, int var, cudaStream_t st) {
         }
     }
     if (var == kVarStep)
-        k_decode_planes<D, GC, COMP, true><<<grid, kDecThreads, Cfg::SMEM_B, st>>>(a);
+        k_decode_planes<D, GC, COMP, 1><<<grid, kDecThreads, Cfg::SMEM_B, st>>>(a);
+    else if (var == kVarEntropy)
+        k_decode_planes<D, GC, COMP, 2><<<grid, kDecThreads, Cfg::SMEM_B, st>>>(a);
     else
-        k_decode_planes<D, GC, COMP, false><<<grid, kDecThreads, Cfg::SMEM_B, st>>>(a);
+        k_decode_planes<D, GC, COMP, 0><<<grid, kDecThreads, Cfg::SMEM_B, st>>>(a);
     BC_LAUNCH_CHECK();
     return BC_OK;
 }
@@ -1129,7 +1225,7 @@ template <int D, int GC, bool COMP>
 int capacity_of(int var) {
     using Cfg = DecCfg<D, GC, COMP>;
     constexpr int kMaxDev = 64;
-    static int cap[3][kMaxDev] = {};
+    static int cap[4][kMaxDev] = {};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev >= 0 && dev < kMaxDev && cap[var][dev] > 0) return cap[var][dev];
@@ -1143,8 +1239,9 @@ int capacity_of(int var) {
         }
     }
     if (!done)
-        per_sm = (var == kVarStep) ? set_smem_and_occupancy(k_decode_planes<D, GC, COMP, true>, Cfg::SMEM_B)
-                                   : set_smem_and_occupancy(k_decode_planes<D, GC, COMP, false>, Cfg::SMEM_B);
+        per_sm = (var == kVarStep)      ? set_smem_and_occupancy(k_decode_planes<D, GC, COMP, 1>, Cfg::SMEM_B)
+                 : (var == kVarEntropy) ? set_smem_and_occupancy(k_decode_planes<D, GC, COMP, 2>, Cfg::SMEM_B)
+                                        : set_smem_and_occupancy(k_decode_planes<D, GC, COMP, 0>, Cfg::SMEM_B);
     const int c = sms * max(1, per_sm);
     if (dev >= 0 && dev < kMaxDev) cap[var][dev] = c;
     return c;
@@ -1164,11 +1261,15 @@ int run_decode_t(DecodeArgs a, int var, void* ws, size_t ws_bytes, cudaStream_t 
         // zero (every completed call resets its own); partials follow and are
         // always written before they are read.
         const size_t cnt = (size_t)a.n_slots * p.n_hgroups * sizeof(unsigned);
-        a.ws_cnt = reinterpret_cast<unsigned*>(ws);
-        a.ws_part = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(ws) + ((cnt + 255) & ~(size_t)255));
+        const size_t part = (size_t)a.n_slots * a.group * p.n_splits * (D + 2) * sizeof(float);
+        uint8_t* base = reinterpret_cast<uint8_t*>(ws);
+        a.ws_cnt = reinterpret_cast<unsigned*>(base);
+        a.ws_part = reinterpret_cast<float*>(base + ((cnt + 255) & ~(size_t)255));
+        a.ws_ent = reinterpret_cast<float*>(base + ((cnt + 255) & ~(size_t)255) + ((part + 255) & ~(size_t)255));
     } else {
         a.ws_part = nullptr;
         a.ws_cnt = nullptr;
+        a.ws_ent = nullptr;
     }
     return launch_decode<D, GC, COMP>(a, var, st);
 }
@@ -1277,6 +1378,18 @@ int bc_decode_attention(const void* q, bc_kv_planes K, bc_kv_planes V, void* out
     if (rc != BC_OK || n_slots == 0) return rc;
     const DecodeArgs a = decode_args(q, K, V, out, partial, n_slots, group, seq_len, kv_stride, head_dim);
     return run_decode(a, mode == BC_MODE_COMPENSATED, kVarPlanes, workspace, workspace_bytes, (cudaStream_t)stream);
+}
+
+int bc_decode_attention_entropy(const void* q, bc_kv_planes K, bc_kv_planes V, void* out, float* partial,
+                                float* entropy, int n_slots, int group, int seq_len, int64_t kv_stride, int head_dim,
+                                int mode, void* workspace, size_t workspace_bytes, void* stream) {
+    const int rc = check_decode_args(q, K, V, out, partial, n_slots, group, seq_len, kv_stride, head_dim, mode);
+    if (rc != BC_OK || n_slots == 0) return rc;
+    if (!entropy) return BC_ERR_ARG;
+    if (!bc_aligned(entropy, 4)) return BC_ERR_ALIGN;
+    DecodeArgs a = decode_args(q, K, V, out, partial, n_slots, group, seq_len, kv_stride, head_dim);
+    a.entropy = entropy;
+    return run_decode(a, mode == BC_MODE_COMPENSATED, kVarEntropy, workspace, workspace_bytes, (cudaStream_t)stream);
 }
 
 int bc_decode_step(const void* q, const void* new_k, const void* new_v, bc_kv_planes K, bc_kv_planes V, void* out,

@@ -281,6 +281,32 @@ def append_kv_paged(k: torch.Tensor, v: torch.Tensor, K: Planes, V: Planes, pt: 
                                       residual_mode, _stream(k)), "append_kv_paged")
 
 
+def decode_attention_entropy(q: torch.Tensor, K: Planes, V: Planes, seq_len: int, mode: int = MODE_COMPENSATED,
+                             out: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+    """Decode attention and, from the same pass, the per-head entropy of the softmax
+    over binary scores (the reference's compute_head_entropy).  Returns (out fp16
+    [n_heads, d], entropy fp32 [n_heads])."""
+    _check_half(q, "Q")
+    d = q.shape[-1]
+    n_heads = q.numel() // d
+    n_slots = K.n_slots
+    group = n_heads // n_slots
+    if group * n_slots != n_heads:
+        raise RuntimeError("number of query heads must be a multiple of the number of KV slots")
+    if out is None:
+        out = torch.empty((n_heads, d), dtype=torch.float16, device=q.device)
+    ent = torch.empty(n_heads, dtype=torch.float32, device=q.device)
+    lib = _lib.load()
+    st = _stream(q)
+    wsb = lib.bc_decode_workspace_bytes(n_slots, group, seq_len, d)
+    ws = _lib.workspace(q.device, st, wsb, ("decode", n_slots, group))
+    _lib.check(lib.bc_decode_attention_entropy(q.data_ptr(), K.c(), V.c(), out.data_ptr(), None, ent.data_ptr(),
+                                               n_slots, group, seq_len, K.kv_stride, d, mode, _lib.ptr(ws),
+                                               ws.numel() if ws is not None else 0, st),
+               "decode_attention_entropy")
+    return out, ent
+
+
 def keep_count(seq_len: int, fraction: float) -> int:
     """Number of residuals kept per slot for a keep fraction (rounded to nearest, ties up)."""
     return int(seq_len * fraction + 0.5)

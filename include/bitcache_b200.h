@@ -155,6 +155,17 @@ int bc_decode_attention(const void* q, bc_kv_planes K, bc_kv_planes V, void* out
                         int group, int seq_len, int64_t kv_stride, int head_dim, int mode, void* workspace,
                         size_t workspace_bytes, void* stream);
 
+/* bc_decode_attention plus, in the same pass over the cache, the reference's
+ * compute_head_entropy (adaptive_precision.cu:13-130; launch_compute_head_entropy,
+ * adaptive_precision.cuh:14-23) for every query head: entropy[h] = H of the
+ * softmax over the binary scores scale_q*scale_k*(2*matches - d) without
+ * 1/sqrt(d), scale_q the query's mean |q| in the reference's tree order.
+ * The reference needs a separate pass over K for it. fp32 [n_slots*group].
+ * Workspace as bc_decode_workspace_bytes. */
+int bc_decode_attention_entropy(const void* q, bc_kv_planes K, bc_kv_planes V, void* out, float* partial,
+                                float* entropy, int n_slots, int group, int seq_len, int64_t kv_stride, int head_dim,
+                                int mode, void* workspace, size_t workspace_bytes, void* stream);
+
 /* Fused decode step: bc_append_kv of new_k / new_v (fp16 [n_slots][head_dim]) at plane
  * position append_pos with append_res arithmetic, then bc_decode_attention over keys
  * [0, seq_len), in ONE launch.  Replaces the reference's BitCache.append followed by

@@ -296,3 +296,35 @@ def test_workspace_counters_left_zero_and_no_device_error(cuda, slots, group):
     n_cnt = slots * group  # upper bound of the counter region (one head per CTA)
     assert not _lib._ws[key][: 4 * n_cnt].any(), "split-K ticket counters not returned to zero"
     assert _lib.device_error() == 0
+
+
+@pytest.mark.parametrize("slots,group,S,d,comp", [
+    (8, 1, 1024, 128, True),      # C1 shape
+    (32, 1, 4096, 128, True),     # several splits per slot
+    (3, 4, 700, 64, True),        # grouped-query heads
+    (2, 8, 333, 128, False),
+    (4, 1, 1, 256, True),
+    (5, 2, 2049, 32, False),
+])
+def test_fused_entropy_matches_reference(cuda, slots, group, S, d, comp):
+    """Entropy computed inside the attention pass equals the reference's
+    compute_head_entropy (its own kernel, on records) and the attention output
+    equals the plain kernel's."""
+    g = torch.Generator().manual_seed(S + d + group)
+    q = (torch.randn(slots * group, d, generator=g) * 0.5).half().to(cuda)
+    k = (torch.randn(slots, S, d, generator=g) * 0.5).half().to(cuda)
+    v = (torch.randn(slots, S, d, generator=g) * 0.5).half().to(cuda)
+    stride = planes.round_stride(S)
+    K = planes.Planes.empty(slots, stride, d, True, cuda)
+    V = planes.Planes.empty(slots, stride, d, True, cuda)
+    planes.encode_planes(k, K, planes.RES_FP16_SCALE)
+    planes.encode_planes(v, V, planes.RES_FP16_SCALE)
+    mode = planes.MODE_COMPENSATED if comp else planes.MODE_BINARY
+    out, ent = planes.decode_attention_entropy(q, K, V, S, mode)
+    plain = planes.decode_attention(q, K, V, S, mode)
+    # reference kernel: one record row per query head (the KV slot repeated for the group)
+    kb = _C.binary_encode(k.repeat_interleave(group, 0).reshape(-1, d).contiguous())
+    ref = refgpu.head_entropy(q, kb, 1, slots * group, S, d)
+    torch.cuda.synchronize()
+    torch.testing.assert_close(ent, ref, rtol=1e-4, atol=1e-4)
+    close(out, plain, f"entropy variant output slots={slots} g={group}")
