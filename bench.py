@@ -172,6 +172,8 @@ def run_reference(args):
     S, d = w.seq_len, w.head_dim
     used = min(threads, q.shape[0])  # the port parallelises over query heads
     bytes_step = workloads.step_cache_bytes(w.batch, w.n_kv_heads, S, d, comp)
+    if comp and args.config == "C5":  # adaptive config: the same byte model as our arm
+        bytes_step = workloads.adaptive_step_bytes(w.batch, w.n_kv_heads, S, d, w.extra.get("keep", 0.25))
     for _ in range(max(0, args.warmup)):
         time_cpu_steps(q, K, V, w.group, S, comp, 1, threads)
     t = time_cpu_steps(q, K, V, w.group, S, comp, args.steps, threads)
@@ -266,8 +268,17 @@ def main():
     v_all = w.v.reshape(n_slots, S, d)[a:b, s_a:s_b].contiguous()
     q_all = w.q.reshape(n_slots * G, d)[a * G:b * G].contiguous()
     stride = planes.round_stride(my_S)
-    bytes_rank = workloads.step_cache_bytes(1, my_slots, my_S, d, comp)
-    bytes_total = workloads.step_cache_bytes(w.batch, w.n_kv_heads, S, d, comp)
+    # C5 is the adaptive-precision config: the residual is kept for a fraction of
+    # the positions (compact layout, unkept residuals neither stored nor read)
+    keep_frac = w.extra.get("keep") if (comp and args.config == "C5") else None
+    adaptive = keep_frac is not None
+    n_keep = planes.keep_count(my_S, keep_frac) if adaptive else my_S
+    if adaptive:
+        bytes_rank = workloads.adaptive_step_bytes(1, my_slots, my_S, d, keep_frac)
+        bytes_total = workloads.adaptive_step_bytes(w.batch, w.n_kv_heads, S, d, keep_frac)
+    else:
+        bytes_rank = workloads.step_cache_bytes(1, my_slots, my_S, d, comp)
+        bytes_total = workloads.step_cache_bytes(w.batch, w.n_kv_heads, S, d, comp)
     # Inputs larger than L2: rotate through enough cache copies that one step's
     # data is evicted before it is read again.
     copies = max(1, math.ceil(3 * L2_BYTES / max(1, bytes_rank)))
@@ -277,6 +288,11 @@ def main():
         V = planes.Planes.empty(my_slots, stride, d, comp, dev, zero=False)
         planes.encode_planes(k_all, K, res_mode)
         planes.encode_planes(v_all, V, res_mode)
+        if adaptive:
+            keep = planes.select_positions_topk(K, V, my_S, n_keep)
+            K, V = planes.compact_adaptive(K, V, keep, my_S, n_keep)
+            del keep
+            torch.cuda.empty_cache()
         Ks.append(K)
         Vs.append(V)
     torch.cuda.synchronize()
@@ -286,7 +302,9 @@ def main():
 
     def step(i):
         K, V = Ks[i % copies], Vs[i % copies]
-        if seq_split:
+        if adaptive:
+            planes.decode_attention_adaptive(q_all, K, V, my_S, n_keep, out=out)
+        elif seq_split:
             planes.decode_attention(q_all, K, V, my_S, mode, partial=part, want_out=False)
         else:
             planes.decode_attention(q_all, K, V, my_S, mode, out=out)
@@ -350,7 +368,39 @@ def main():
 
     # ---- end to end through the public API (pinned host buffers) ----------
     e2e = None
-    if world == 1 or args.split == "heads":
+    if adaptive:
+        # adaptive cache (snapshot after selection): pinned host Q in, output out
+        qh = q_all.cpu().pin_memory()
+        oh = torch.empty(q_all.shape, dtype=torch.float16).pin_memory()
+        qd = torch.empty_like(q_all)
+        Kc, Vc = Ks[0], Vs[0]
+
+        def e2e_step():
+            qd.copy_(qh, non_blocking=True)
+            o = planes.decode_attention_adaptive(qd, Kc, Vc, my_S, n_keep)
+            oh.copy_(o, non_blocking=True)
+
+        for _ in range(max(3, args.warmup)):
+            e2e_step()
+        torch.cuda.synchronize()
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            e2e_step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        e2e_ms = e0.elapsed_time(e1) / args.steps
+        if pg is not None:
+            t = torch.tensor([e2e_ms], device=dev, dtype=torch.float64)
+            pg.all_reduce(t, op=pg.ReduceOp.MAX)
+            e2e_ms = float(t[0])
+        e2e = {"value": bytes_total / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s", "ms_per_step": e2e_ms,
+               "h2d_bytes_per_step": qh.numel() * 2 * world, "d2h_bytes_per_step": oh.numel() * 2 * world,
+               "path": "planes.decode_attention_adaptive on the compact cache, pinned host Q in, output out",
+               "gpu_launches_per_step": 1}
+    elif world == 1 or args.split == "heads":
         cache = BitCache(w.batch if world == 1 else 1, my_slots * G if world > 1 else w.n_heads, d, max_seq=my_S,
                          device=str(dev), compensated=comp, n_kv_heads=my_slots if world > 1 else w.n_kv_heads)
         cache.prefill(k_all.view(cache.batch, cache.n_kv_heads, my_S, d), v_all.view(cache.batch, cache.n_kv_heads, my_S, d))
@@ -428,10 +478,12 @@ def main():
         "dtype": "u32 sign words, u8 INT4 codes, f32 accumulate (fp16 in/out)",
         "data": "synthetic (seeded torch generator, BASELINE config shapes)",
         "config": {"workload": f"{args.config}: B={w.batch} H={w.n_heads} Hkv={w.n_kv_heads} S={S} d={d} "
-                               f"{'compensated' if comp else 'binary'}",
+                               + (f"adaptive, residual kept for {keep_frac:.0%} of positions (compact layout)"
+                                  if adaptive else ('compensated' if comp else 'binary')),
                    "parallelism": (f"{args.split}-split x{world}" if world > 1 else "single GPU"),
                    "l2": f"inputs larger than L2: {copies} rotating cache copies of {bytes_rank / 1e6:.1f} MB per rank",
-                   "bytes_per_vector": workloads.vector_footprint(d, comp),
+                   "bytes_per_vector": (bytes_total / (2 * w.batch * w.n_kv_heads * S)) if adaptive
+                   else workloads.vector_footprint(d, comp),
                    "stored_bytes_per_vector": planes.vector_bytes(d, comp)},
         "pct_of_hbm_peak": 100.0 * value / world / hbm,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,

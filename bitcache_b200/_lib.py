@@ -71,6 +71,13 @@ _SIGS = {
                                c_int, c_int64, c_int, c_int, c_int, c_int, c_void_p, c_size_t, c_void_p]),
     "bc_decode_attention_entropy": (c_int, [c_void_p, KVPlanes, KVPlanes, c_void_p, c_void_p, c_void_p, c_int, c_int,
                                             c_int, c_int64, c_int, c_int, c_void_p, c_size_t, c_void_p]),
+    "bc_select_positions_topk": (c_int, [KVPlanes, KVPlanes, c_int, c_int, c_int64, c_int, c_int, c_void_p,
+                                         c_void_p, c_size_t, c_void_p]),
+    "bc_compact_adaptive": (c_int, [KVPlanes, KVPlanes, c_void_p, c_int, c_int, c_int64, c_int, c_int, KVPlanes,
+                                    KVPlanes, c_int64, c_int64, c_void_p]),
+    "bc_decode_adaptive_workspace_bytes": (c_size_t, [c_int, c_int, c_int, c_int, c_int]),
+    "bc_decode_attention_adaptive": (c_int, [c_void_p, KVPlanes, KVPlanes, c_void_p, c_void_p, c_int, c_int, c_int,
+                                             c_int, c_int64, c_int64, c_int, c_void_p, c_size_t, c_void_p]),
     "bc_decode_step_paged": (c_int, [c_void_p, c_void_p, c_void_p, KVPlanes, KVPlanes, c_void_p, c_void_p, PageTable,
                                      c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_void_p, c_size_t, c_void_p]),
     "bc_append_kv_paged": (c_int, [c_void_p, c_void_p, KVPlanes, KVPlanes, PageTable, c_int, c_int, c_int64, c_int,

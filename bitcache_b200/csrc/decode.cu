@@ -131,6 +131,13 @@ struct DecodeArgs {
     // without 1/sqrt(d) (reference adaptive_precision.cu:13-130)
     float* entropy;  // [n_slots * group]
     float* ws_ent;   // [n_slots * group][n_splits][3] split partials (m, z, w)
+    // compact adaptive caches (VAR 3): positions [0, n_keep) of a slot carry
+    // residuals (residual planes at row stride res_stride); the binary-only
+    // rest sits at sign/scale rows [b0, b0 + seq_len - n_keep).  Splits
+    // [0, nc) cover the first segment with keys_per_split keys each, the
+    // remaining splits the second with kps_bin keys each.
+    int n_keep, nc, kps_bin, b0;
+    int64_t res_stride;
 };
 
 // Plane row of logical position `pos` of `slot`, or -1 for a page id outside
@@ -847,11 +854,13 @@ __device__ __noinline__ void patch_stage_row(uint8_t* sb, int kk, const uint8_t*
 // otherwise run free: no CTA-wide barrier per tile.
 // ---------------------------------------------------------------------------
 // VAR: 0 attention, 1 fused decode step (append + attend, paged caches),
-// 2 attention plus the per-head entropy of the binary-score softmax.
+// 2 attention plus the per-head entropy of the binary-score softmax,
+// 3 attention over a compact adaptive cache (compensated keys, then
+// binary-only keys; instantiated with COMP = true).
 template <int D, int GC, bool COMP, int VAR = 0>
 __global__ void __launch_bounds__(kDecThreads, DecCfg<D, GC, COMP>::MIN_CTAS)
     k_decode_planes(const DecodeArgs a) {
-    constexpr bool STEP = VAR == 1, ENT = VAR == 2;
+    constexpr bool STEP = VAR == 1, ENT = VAR == 2, ADA = VAR == 3;
     using Cfg = DecCfg<D, GC, COMP>;
     constexpr int NS = Cfg::NS, LAG = Cfg::LAG, T = Cfg::T;
     extern __shared__ __align__(128) uint8_t smem_raw[];
@@ -863,8 +872,21 @@ __global__ void __launch_bounds__(kDecThreads, DecCfg<D, GC, COMP>::MIN_CTAS)
     uint64_t* empty = reinterpret_cast<uint64_t*>(smem + Cfg::EMPTY_OFF);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + Cfg::FLAG_OFF);
 
-    const int s_begin = split * a.keys_per_split;
-    const int s_end = min(a.seq_len, s_begin + a.keys_per_split);
+    // adaptive caches: this CTA's segment (binary-only keys when seg_bin)
+    const bool seg_bin = ADA && split >= a.nc;
+    int s_begin, s_end;
+    if constexpr (ADA) {
+        if (seg_bin) {
+            s_begin = (split - a.nc) * a.kps_bin;
+            s_end = min(a.seq_len - a.n_keep, s_begin + a.kps_bin);
+        } else {
+            s_begin = split * a.keys_per_split;
+            s_end = min(a.n_keep, s_begin + a.keys_per_split);
+        }
+    } else {
+        s_begin = split * a.keys_per_split;
+        s_end = min(a.seq_len, s_begin + a.keys_per_split);
+    }
     const int n_keys = max(0, s_end - s_begin);
     const int n_tiles = (n_keys + T - 1) / T;
 
@@ -902,6 +924,7 @@ __global__ void __launch_bounds__(kDecThreads, DecCfg<D, GC, COMP>::MIN_CTAS)
     // tile boundaries and pages hold a multiple of the tile's 128 positions.
     auto row_of = [&](int tile) -> int64_t {
         if constexpr (STEP) return plane_row(a, slot, s_begin + tile * T);
+        if constexpr (ADA) return (int64_t)slot * a.kv_stride + (seg_bin ? a.b0 : 0) + s_begin + tile * T;
         return (int64_t)slot * a.kv_stride + s_begin + tile * T;
     };
     auto issue = [&](int tile, int stage, int64_t row) {
@@ -919,17 +942,20 @@ __global__ void __launch_bounds__(kDecThreads, DecCfg<D, GC, COMP>::MIN_CTAS)
         }
         uint8_t* sbuf = smem + stage * Cfg::STAGE_B;
         const uint32_t sign_b = nk8 * (D / 8), sc_b = nk8 * 2, nib_b = nk8 * (D / 2);
-        const uint32_t total = 2 * (sign_b + sc_b + (COMP ? nib_b + sc_b : 0));
+        const bool res = COMP && !seg_bin;
+        const uint32_t total = 2 * (sign_b + sc_b + (res ? nib_b + sc_b : 0));
+        // residual planes: their own row stride in adaptive caches
+        const int64_t rrow = ADA ? (int64_t)slot * a.res_stride + s_begin + k0 : row;
         mbar_arrive_expect_tx(&full[stage], total);
         bulk_g2s(sbuf + Cfg::OFF_KSIGN, (const uint8_t*)a.K.sign + row * (D / 8), sign_b, &full[stage]);
         bulk_g2s(sbuf + Cfg::OFF_KBS, (const uint8_t*)a.K.bscale + row * 2, sc_b, &full[stage]);
         bulk_g2s(sbuf + Cfg::OFF_VSIGN, (const uint8_t*)a.V.sign + row * (D / 8), sign_b, &full[stage]);
         bulk_g2s(sbuf + Cfg::OFF_VBS, (const uint8_t*)a.V.bscale + row * 2, sc_b, &full[stage]);
-        if (COMP) {
-            bulk_g2s(sbuf + Cfg::OFF_KNIB, (const uint8_t*)a.K.nib + row * (D / 2), nib_b, &full[stage]);
-            bulk_g2s(sbuf + Cfg::OFF_KRS, (const uint8_t*)a.K.rscale + row * 2, sc_b, &full[stage]);
-            bulk_g2s(sbuf + Cfg::OFF_VNIB, (const uint8_t*)a.V.nib + row * (D / 2), nib_b, &full[stage]);
-            bulk_g2s(sbuf + Cfg::OFF_VRS, (const uint8_t*)a.V.rscale + row * 2, sc_b, &full[stage]);
+        if (res) {
+            bulk_g2s(sbuf + Cfg::OFF_KNIB, (const uint8_t*)a.K.nib + rrow * (D / 2), nib_b, &full[stage]);
+            bulk_g2s(sbuf + Cfg::OFF_KRS, (const uint8_t*)a.K.rscale + rrow * 2, sc_b, &full[stage]);
+            bulk_g2s(sbuf + Cfg::OFF_VNIB, (const uint8_t*)a.V.nib + rrow * (D / 2), nib_b, &full[stage]);
+            bulk_g2s(sbuf + Cfg::OFF_VRS, (const uint8_t*)a.V.rscale + rrow * 2, sc_b, &full[stage]);
         }
     };
     // thread 0: the plane row of the next tile to issue, read one refill ahead
@@ -986,7 +1012,10 @@ __global__ void __launch_bounds__(kDecThreads, DecCfg<D, GC, COMP>::MIN_CTAS)
         if constexpr (STEP) {
             if (it == patch_it) patch_stage_row<D, COMP, Cfg>(smem + stage * Cfg::STAGE_B, patch_kk, smem);
         }
-        consume_warp_tile<D, GC, COMP, Cfg, ENT>(qs, st, smem + stage * Cfg::STAGE_B, warp * 32, nk);
+        if (ADA && seg_bin)
+            consume_warp_tile<D, GC, false, Cfg>(qs, st, smem + stage * Cfg::STAGE_B, warp * 32, nk);
+        else
+            consume_warp_tile<D, GC, COMP, Cfg, ENT>(qs, st, smem + stage * Cfg::STAGE_B, warp * 32, nk);
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[stage]);
     }
@@ -1187,7 +1216,7 @@ size_t ws_bound(int n_slots, int group, int seq_len, int d) {
     return best;
 }
 
-enum Variant { kVarPlanes = 0, kVarRecords = 1, kVarStep = 2, kVarEntropy = 3 };
+enum Variant { kVarPlanes = 0, kVarRecords = 1, kVarStep = 2, kVarEntropy = 3, kVarAdaptive = 4 };
 
 template <int D, int GC, bool COMP>
 int launch_decode(const DecodeArgs& a, int var, cudaStream_t st) {
@@ -1205,7 +1234,9 @@ int launch_decode(const DecodeArgs& a, int var, cudaStream_t st) {
         k_decode_planes<D, GC, COMP, 1><<<grid, kDecThreads, Cfg::SMEM_B, st>>>(a);
     else if (var == kVarEntropy)
         k_decode_planes<D, GC, COMP, 2><<<grid, kDecThreads, Cfg::SMEM_B, st>>>(a);
-    else
+    else if (var == kVarAdaptive) {
+        if constexpr (COMP) k_decode_planes<D, GC, COMP, 3><<<grid, kDecThreads, Cfg::SMEM_B, st>>>(a);
+    } else
         k_decode_planes<D, GC, COMP, 0><<<grid, kDecThreads, Cfg::SMEM_B, st>>>(a);
     BC_LAUNCH_CHECK();
     return BC_OK;
@@ -1225,7 +1256,7 @@ template <int D, int GC, bool COMP>
 int capacity_of(int var) {
     using Cfg = DecCfg<D, GC, COMP>;
     constexpr int kMaxDev = 64;
-    static int cap[4][kMaxDev] = {};
+    static int cap[5][kMaxDev] = {};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev >= 0 && dev < kMaxDev && cap[var][dev] > 0) return cap[var][dev];
@@ -1238,6 +1269,12 @@ int capacity_of(int var) {
             done = true;
         }
     }
+    if constexpr (COMP) {
+        if (var == kVarAdaptive) {
+            per_sm = set_smem_and_occupancy(k_decode_planes<D, GC, COMP, 3>, Cfg::SMEM_B);
+            done = true;
+        }
+    }
     if (!done)
         per_sm = (var == kVarStep)      ? set_smem_and_occupancy(k_decode_planes<D, GC, COMP, 1>, Cfg::SMEM_B)
                  : (var == kVarEntropy) ? set_smem_and_occupancy(k_decode_planes<D, GC, COMP, 2>, Cfg::SMEM_B)
@@ -1247,13 +1284,40 @@ int capacity_of(int var) {
     return c;
 }
 
+// Adaptive caches: split the compensated segment (n_keep keys) and the
+// binary one (seq_len - n_keep) so that one resident wave covers both, giving
+// a binary split kBinKeysPerComp times the keys of a compensated split (a
+// binary key costs about 40% of a compensated one).
+constexpr int kBinKeysPerComp = 5;  // in halves: 2.5x
+void plan_adaptive(DecodeArgs& a, int gc, int capacity) {
+    const int n_hgroups = a.group / gc;
+    const int64_t units = (int64_t)a.n_slots * n_hgroups;
+    const int tiles_c = (a.n_keep + kTile - 1) / kTile;
+    const int tiles_b = (a.seq_len - a.n_keep + kTile - 1) / kTile;
+    const int eff = max(1, tiles_c + (tiles_b * 2 + kBinKeysPerComp - 1) / kBinKeysPerComp);
+    int splits = units < capacity ? (int)(capacity / units) : 1;
+    splits = max(1, min(splits, eff));
+    const int tps = (eff + splits - 1) / splits;
+    a.keys_per_split = tps * kTile;
+    a.kps_bin = ((tps * kBinKeysPerComp + 1) / 2) * kTile;
+    a.nc = (a.n_keep + a.keys_per_split - 1) / a.keys_per_split;
+    const int nb = (a.seq_len - a.n_keep + a.kps_bin - 1) / a.kps_bin;
+    a.n_splits = max(1, a.nc + nb);
+    a.n_hgroups = n_hgroups;
+}
+
 template <int D, int GC, bool COMP>
 int run_decode_t(DecodeArgs a, int var, void* ws, size_t ws_bytes, cudaStream_t st) {
     const int cap = min(capacity_of<D, GC, COMP>(var), kMaxCtasPlan);
-    Plan p = make_plan(a.n_slots, a.group, a.seq_len, D, COMP, cap);
-    a.n_splits = p.n_splits;
-    a.keys_per_split = p.keys_per_split;
-    a.n_hgroups = p.n_hgroups;
+    if (var == kVarAdaptive) {
+        plan_adaptive(a, GC, cap);
+    } else {
+        Plan p = make_plan(a.n_slots, a.group, a.seq_len, D, COMP, cap);
+        a.n_splits = p.n_splits;
+        a.keys_per_split = p.keys_per_split;
+        a.n_hgroups = p.n_hgroups;
+    }
+    Plan p{a.n_splits, a.keys_per_split, a.n_hgroups, GC, kTile};
     if (p.n_splits > 1) {
         const size_t need = ws_bytes_for(a.n_slots, a.group, p.n_splits, D, p.n_hgroups);
         if (ws == nullptr || ws_bytes < need) return BC_ERR_WORKSPACE;
@@ -1378,6 +1442,42 @@ int bc_decode_attention(const void* q, bc_kv_planes K, bc_kv_planes V, void* out
     if (rc != BC_OK || n_slots == 0) return rc;
     const DecodeArgs a = decode_args(q, K, V, out, partial, n_slots, group, seq_len, kv_stride, head_dim);
     return run_decode(a, mode == BC_MODE_COMPENSATED, kVarPlanes, workspace, workspace_bytes, (cudaStream_t)stream);
+}
+
+size_t bc_decode_adaptive_workspace_bytes(int n_slots, int group, int seq_len, int n_keep, int head_dim) {
+    if (n_slots <= 0 || !valid_group(group) || seq_len < 0 || n_keep < 0 || n_keep > seq_len ||
+        !bc_valid_head_dim(head_dim))
+        return 0;
+    size_t best = 0;
+    for (int gc = 1; gc <= 2 && gc <= group; gc *= 2) {  // compensated CTAs hold one or two heads
+        DecodeArgs a{};
+        a.n_slots = n_slots;
+        a.group = group;
+        a.seq_len = seq_len;
+        a.n_keep = n_keep;
+        plan_adaptive(a, gc, kMaxCtasPlan);
+        const size_t b = ws_bytes_for(n_slots, group, a.n_splits, head_dim, group);
+        best = b > best ? b : best;
+    }
+    return best;
+}
+
+int bc_decode_attention_adaptive(const void* q, bc_kv_planes K, bc_kv_planes V, void* out, float* partial,
+                                 int n_slots, int group, int seq_len, int n_keep, int64_t kv_stride,
+                                 int64_t res_stride, int head_dim, void* workspace, size_t workspace_bytes,
+                                 void* stream) {
+    const int rc = check_decode_args(q, K, V, out, partial, n_slots, group, seq_len, kv_stride, head_dim,
+                                     BC_MODE_COMPENSATED);
+    if (rc != BC_OK || n_slots == 0) return rc;
+    const int b0 = (n_keep + 7) & ~7;
+    if (n_keep < 0 || n_keep > seq_len || kv_stride < (int64_t)b0 + (seq_len - n_keep) || res_stride < n_keep)
+        return BC_ERR_ARG;
+    if (res_stride % 8 != 0) return BC_ERR_ALIGN;
+    DecodeArgs a = decode_args(q, K, V, out, partial, n_slots, group, seq_len, kv_stride, head_dim);
+    a.n_keep = n_keep;
+    a.b0 = b0;
+    a.res_stride = res_stride;
+    return run_decode(a, true, kVarAdaptive, workspace, workspace_bytes, (cudaStream_t)stream);
 }
 
 int bc_decode_attention_entropy(const void* q, bc_kv_planes K, bc_kv_planes V, void* out, float* partial,

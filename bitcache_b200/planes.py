@@ -307,6 +307,69 @@ def decode_attention_entropy(q: torch.Tensor, K: Planes, V: Planes, seq_len: int
     return out, ent
 
 
+def select_positions_topk(K: Planes, V: Planes, seq_len: int, n_keep: int) -> torch.Tensor:
+    """Per-position adaptive precision: uint8 keep mask [n_slots, kv_stride] of the n_keep
+    positions per slot with the largest K + V residual energy (bc_select_positions_topk)."""
+    if not (K.compensated and V.compensated):
+        raise RuntimeError("select_positions_topk needs compensated (residual) caches")
+    lib = _lib.load()
+    st = _lib.stream_of(K.sign.device)
+    keep = torch.zeros((K.n_slots, K.kv_stride), dtype=torch.uint8, device=K.sign.device)
+    wsb = lib.bc_select_workspace_bytes(K.n_slots, K.kv_stride)
+    ws = torch.empty(max(wsb, 16), dtype=torch.uint8, device=K.sign.device)
+    _lib.check(lib.bc_select_positions_topk(K.c(), V.c(), K.n_slots, seq_len, K.kv_stride, K.head_dim, n_keep,
+                                            keep.data_ptr(), ws.data_ptr(), ws.numel(), st),
+               "select_positions_topk")
+    return keep
+
+
+def compact_adaptive(K: Planes, V: Planes, keep: torch.Tensor, seq_len: int, n_keep: int) -> tuple[Planes, Planes]:
+    """Compact adaptive cache (bc_compact_adaptive): kept positions first with their
+    residuals, the rest binary only from row round8(n_keep); the residual planes hold
+    only the kept rows.  Returns (Kc, Vc); their sign planes' stride is kv_stride of
+    the result, the residual planes' stride nib.shape[1]."""
+    b0 = round_stride(n_keep)
+    c_stride = round_stride(b0 + seq_len - n_keep)
+    r_stride = max(8, b0)
+
+    def mk(P: Planes) -> Planes:
+        dev = P.sign.device
+        return Planes(torch.zeros((P.n_slots, c_stride, P.head_dim // 32), dtype=torch.int32, device=dev),
+                      torch.zeros((P.n_slots, c_stride), dtype=torch.float16, device=dev),
+                      torch.full((P.n_slots, r_stride, P.head_dim // 2), 0x88, dtype=torch.uint8, device=dev),
+                      torch.zeros((P.n_slots, r_stride), dtype=torch.float16, device=dev), P.head_dim)
+
+    Kc, Vc = mk(K), mk(V)
+    lib = _lib.load()
+    _lib.check(lib.bc_compact_adaptive(K.c(), V.c(), keep.data_ptr(), K.n_slots, seq_len, K.kv_stride, K.head_dim,
+                                       n_keep, Kc.c(), Vc.c(), c_stride, r_stride,
+                                       _lib.stream_of(K.sign.device)), "compact_adaptive")
+    return Kc, Vc
+
+
+def decode_attention_adaptive(q: torch.Tensor, Kc: Planes, Vc: Planes, seq_len: int, n_keep: int,
+                              out: torch.Tensor | None = None) -> torch.Tensor:
+    """Decode attention over a compact adaptive cache (bc_decode_attention_adaptive)."""
+    _check_half(q, "Q")
+    d = q.shape[-1]
+    n_heads = q.numel() // d
+    n_slots = Kc.n_slots
+    group = n_heads // n_slots
+    if group * n_slots != n_heads:
+        raise RuntimeError("number of query heads must be a multiple of the number of KV slots")
+    if out is None:
+        out = torch.empty((n_heads, d), dtype=torch.float16, device=q.device)
+    lib = _lib.load()
+    st = _stream(q)
+    wsb = lib.bc_decode_adaptive_workspace_bytes(n_slots, group, seq_len, n_keep, d)
+    ws = _lib.workspace(q.device, st, wsb, ("decode", n_slots, group))
+    _lib.check(lib.bc_decode_attention_adaptive(q.data_ptr(), Kc.c(), Vc.c(), out.data_ptr(), None, n_slots, group,
+                                                seq_len, n_keep, Kc.kv_stride, Kc.nib.shape[1], d, _lib.ptr(ws),
+                                                ws.numel() if ws is not None else 0, st),
+               "decode_attention_adaptive")
+    return out
+
+
 def keep_count(seq_len: int, fraction: float) -> int:
     """Number of residuals kept per slot for a keep fraction (rounded to nearest, ties up)."""
     return int(seq_len * fraction + 0.5)

@@ -114,6 +114,14 @@ def vector_footprint(head_dim: int, compensated: bool = True) -> int:
     return 82 if head_dim == 128 else 5 * head_dim // 8 + 4
 
 
+def adaptive_step_bytes(batch: int, n_kv_heads: int, seq_len: int, head_dim: int, keep: float) -> int:
+    """Algorithmic bytes of one decode step over a compact adaptive cache: sign and scale
+    of every vector, the residual (d/2 + 2 B) of the kept fraction only; 34.5 B per
+    vector at head_dim 128 and keep 0.25."""
+    per = (head_dim // 8 + 2) + keep * (head_dim // 2 + 2)
+    return int(round(2 * batch * n_kv_heads * seq_len * per))
+
+
 def step_cache_bytes(batch: int, n_kv_heads: int, seq_len: int, head_dim: int, compensated: bool = True) -> int:
     """Algorithmic bytes of one decode step: K and V of every (batch, kv head, position) read once."""
     return 2 * batch * n_kv_heads * seq_len * vector_footprint(head_dim, compensated)

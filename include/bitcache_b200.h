@@ -212,6 +212,35 @@ int bc_decode_step_paged(const void* q, const void* new_k, const void* new_v, bc
 int bc_append_kv_paged(const void* k, const void* v, bc_kv_planes K, bc_kv_planes V, bc_page_table pt, int n_slots,
                        int head_dim, int64_t pos, int residual_mode, void* stream);
 
+/* ---- compact adaptive caches (per-position adaptive precision) ----------
+ * bc_select_positions_topk: like bc_select_residual_topk, but one choice per
+ * position for K and V together, keyed by the fp32 sum of the K and V keys;
+ * writes keep (uint8 [n_slots][kv_stride], 1 = keep the residuals).
+ * bc_compact_adaptive: stable partition of each slot's positions by keep into
+ * new planes Kc, Vc: kept positions in order at sign/scale rows [0, n_keep)
+ * and residual rows [0, n_keep) (residual row stride r_stride >= round8(n_keep));
+ * the rest, binary only, at sign/scale rows [b0, b0 + seq_len - n_keep),
+ * b0 = n_keep rounded up to 8 (sign/scale row stride c_stride).  Residuals of
+ * the unkept positions are neither stored nor read: at head_dim 128 a decode
+ * step then reads 0.25*84 + 0.75*18 = 34.5 B per vector at a 25% keep rate.
+ * bc_decode_attention_adaptive: compensated attention over the kept keys and
+ * binary attention over the rest, in one launch (their splits merge in the
+ * kernel).  Equal, within the attention tolerance, to bc_decode_attention
+ * with the unkept residuals zeroed (scale 0, codes 0).  Attention is
+ * invariant to the key order, so the permutation needs no record.
+ * No counterpart in the reference (its adaptive precision is per head). */
+int bc_select_positions_topk(bc_kv_planes K, bc_kv_planes V, int n_slots, int seq_len, int64_t kv_stride,
+                             int head_dim, int n_keep, uint8_t* keep, void* workspace, size_t workspace_bytes,
+                             void* stream);
+int bc_compact_adaptive(bc_kv_planes K, bc_kv_planes V, const uint8_t* keep, int n_slots, int seq_len,
+                        int64_t kv_stride, int head_dim, int n_keep, bc_kv_planes Kc, bc_kv_planes Vc,
+                        int64_t c_stride, int64_t r_stride, void* stream);
+size_t bc_decode_adaptive_workspace_bytes(int n_slots, int group, int seq_len, int n_keep, int head_dim);
+int bc_decode_attention_adaptive(const void* q, bc_kv_planes K, bc_kv_planes V, void* out, float* partial,
+                                 int n_slots, int group, int seq_len, int n_keep, int64_t kv_stride,
+                                 int64_t res_stride, int head_dim, void* workspace, size_t workspace_bytes,
+                                 void* stream);
+
 /* Allocation-free bc_decode_attention, for callers that cannot allocate
  * device memory where they run attention (an engine that reserves all of its
  * GPU memory at start-up and forbids allocation in the decode loop, or a

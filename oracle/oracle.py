@@ -165,6 +165,32 @@ def select_residual_topk(nib: np.ndarray, rscale: np.ndarray, seq_len: int, n_ke
     return keep
 
 
+def residual_keys(nib_rows: np.ndarray, rscale: np.ndarray) -> np.ndarray:
+    """Per-vector selection key fp32(rs*rs) * float(sum code^2) (the key of
+    orc_select_residual_topk), from reference-format nibble rows [.., d/2] and fp16 bits."""
+    lo = (nib_rows & 0x0F).astype(np.int64)
+    hi = (nib_rows >> 4).astype(np.int64)
+    lo = np.where(lo >= 8, lo - 16, lo)
+    hi = np.where(hi >= 8, hi - 16, hi)
+    ss = (lo * lo + hi * hi).sum(-1)
+    rs = rscale.view(np.float16).astype(np.float32)
+    return ((rs * rs).astype(np.float32) * ss.astype(np.float32)).astype(np.float32)
+
+
+def select_positions_topk(k_nib: np.ndarray, k_rs: np.ndarray, v_nib: np.ndarray, v_rs: np.ndarray, seq_len: int,
+                          n_keep: int) -> np.ndarray:
+    """Joint per-position selection (the rule of bc_select_positions_topk): key =
+    fp32(key_K + key_V); the n_keep largest per slot, ties to the lower position.
+    Returns keep uint8 [slots, seq_len]."""
+    key = (residual_keys(k_nib[:, :seq_len], k_rs[:, :seq_len]) +
+           residual_keys(v_nib[:, :seq_len], v_rs[:, :seq_len])).astype(np.float32)
+    keep = np.zeros(key.shape, np.uint8)
+    for j in range(key.shape[0]):
+        order = np.lexsort((np.arange(seq_len), -key[j].astype(np.float64)))
+        keep[j, order[:n_keep]] = 1
+    return keep
+
+
 def lse_merge(parts: np.ndarray) -> np.ndarray:
     """parts float32 [n_parts, n_heads, d+2] -> float32 [n_heads, d]."""
     pp = np.ascontiguousarray(parts, np.float32)

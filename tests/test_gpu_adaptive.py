@@ -85,3 +85,75 @@ def test_bitcache_keep_residuals(cuda):
     part = cache.attend(q.to(cuda)).float().cpu().flatten()
     cos = lambda a: float(torch.nn.functional.cosine_similarity(a, exact, dim=0))  # noqa: E731
     assert cos(binary) - 0.01 <= cos(part) <= cos(full) + 0.01
+
+
+# ---- compact adaptive caches: joint K+V selection per position, kept rows first ----
+
+def host_rows(P, rows_stride=None):
+    """Host copy with per-row nibbles (reference byte order) even when the residual
+    planes have their own row stride."""
+    return {"words": P.sign.cpu().numpy().view(np.uint32), "bscale": P.bscale.cpu().numpy().view(np.uint16),
+            "nib": planes.nib_rows(P.nib, P.head_dim).cpu().numpy(), "rscale": P.rscale.cpu().numpy().view(np.uint16)}
+
+
+@pytest.mark.parametrize("slots,group,S,d,frac", [
+    (4, 1, 777, 128, 0.25),
+    (3, 2, 1000, 64, 0.25),
+    (2, 4, 513, 256, 0.5),
+    (5, 1, 300, 128, 0.0),
+    (2, 1, 129, 128, 1.0),
+    (3, 8, 2048, 128, 0.25),
+])
+def test_compact_adaptive_matches_zeroed_oracle(cuda, slots, group, S, d, frac):
+    stride = planes.round_stride(S)
+    K, _ = build(cuda, slots, S, stride, d, seed=S + d, dup=True)
+    V, _ = build(cuda, slots, S, stride, d, seed=S + d + 1)
+    n_keep = planes.keep_count(S, frac)
+    hk, hv = host(K), host(V)
+    keep = planes.select_positions_topk(K, V, S, n_keep)
+    want_keep = O.select_positions_topk(hk["nib"], hk["rscale"], hv["nib"], hv["rscale"], S, n_keep)
+    assert np.array_equal(keep[:, :S].cpu().numpy(), want_keep)
+    Kc, Vc = planes.compact_adaptive(K, V, keep, S, n_keep)
+    # rows moved as a stable partition: kept first, the rest from round8(n_keep)
+    b0 = planes.round_stride(n_keep)
+    hkc, hvc = host_rows(Kc), host_rows(Vc)
+    for j in range(slots):
+        kept = np.nonzero(want_keep[j])[0]
+        rest = np.nonzero(want_keep[j] == 0)[0]
+        for h0, hc in ((hk, hkc), (hv, hvc)):
+            assert np.array_equal(hc["words"][j, :n_keep], h0["words"][j, kept])
+            assert np.array_equal(hc["words"][j, b0:b0 + len(rest)], h0["words"][j, rest])
+            assert np.array_equal(hc["bscale"][j, b0:b0 + len(rest)], h0["bscale"][j, rest])
+            assert np.array_equal(hc["nib"][j, :n_keep], h0["nib"][j, kept])
+            assert np.array_equal(hc["rscale"][j, :n_keep], h0["rscale"][j, kept])
+    # attention: equal (within tolerance) to compensated attention with the unkept residuals zeroed
+    g = torch.Generator().manual_seed(S)
+    q = (torch.randn(slots * group, d, generator=g) / d ** 0.5).half()
+    got = planes.decode_attention_adaptive(q.to(cuda), Kc, Vc, S, n_keep).float().cpu().numpy()
+    m = want_keep.astype(bool)
+    for h0 in (hk, hv):
+        h0["rscale"] = h0["rscale"].copy()
+        h0["nib"] = h0["nib"].copy()
+        h0["rscale"][:, :S] = np.where(m, h0["rscale"][:, :S], 0)
+        h0["nib"][:, :S] = np.where(m[..., None], h0["nib"][:, :S], 0)
+    want = O.attention(q.numpy(), hk, hv, group, S, stride, True).view(np.float16).astype(np.float32)
+    assert np.max(np.abs(got - want)) <= 2e-3
+    if np.linalg.norm(want) > 1e-6:
+        assert float((got * want).sum() / (np.linalg.norm(got) * np.linalg.norm(want))) >= 0.9999
+
+
+def test_compact_adaptive_c5_shape_bytes(cuda):
+    """C5-like slot count at a short length: the compact cache stores the residual
+    planes for the kept quarter only."""
+    slots, S, d = 64, 512, 128
+    K, _ = build(cuda, slots, S, S, d, seed=5)
+    V, _ = build(cuda, slots, S, S, d, seed=6)
+    n_keep = planes.keep_count(S, 0.25)
+    keep = planes.select_positions_topk(K, V, S, n_keep)
+    assert (keep[:, :S].sum(1) == n_keep).all()
+    Kc, Vc = planes.compact_adaptive(K, V, keep, S, n_keep)
+    assert Kc.nib.shape[1] == planes.round_stride(n_keep)
+    q = (torch.randn(slots, d) / d ** 0.5).half().to(cuda)
+    out = planes.decode_attention_adaptive(q, Kc, Vc, S, n_keep)
+    torch.cuda.synchronize()
+    assert torch.isfinite(out.float()).all()

@@ -158,3 +158,23 @@ def test_oracle_topk_selection_matches_numpy():
         want = np.zeros(S, np.uint8)
         want[order[:37]] = 1
         assert np.array_equal(keep[j], want)
+
+
+def test_oracle_joint_selection_matches_bruteforce():
+    rng = np.random.default_rng(9)
+    slots, S, d = 2, 150, 32
+    kn = rng.integers(0, 256, (slots, S, d // 2), dtype=np.uint8)
+    vn = rng.integers(0, 256, (slots, S, d // 2), dtype=np.uint8)
+    kn[:, 40:50] = kn[:, 3:4]
+    vn[:, 40:50] = vn[:, 3:4]
+    kr = (rng.random((slots, S)) * 0.5).astype(np.float16)
+    vr = (rng.random((slots, S)) * 0.5).astype(np.float16)
+    kr[:, 40:50] = kr[:, 3:4]
+    vr[:, 40:50] = vr[:, 3:4]
+    keep = O.select_positions_topk(kn, kr.view(np.uint16), vn, vr.view(np.uint16), S, 33)
+    key = (O.residual_keys(kn, kr.view(np.uint16)) + O.residual_keys(vn, vr.view(np.uint16))).astype(np.float32)
+    for j in range(slots):
+        order = sorted(range(S), key=lambda s: (-float(key[j, s]), s))
+        want = np.zeros(S, np.uint8)
+        want[order[:33]] = 1
+        assert np.array_equal(keep[j], want)
