@@ -120,6 +120,206 @@ __global__ void __launch_bounds__(kEncWarps * 32) k_encode_planes(const __half* 
     }
 }
 
+// ---------------------------------------------------------------------------
+// Prefill encode, one vector per lane (head_dim <= 128).  The per-warp encoder
+// above spends ~6 shuffles and ballots per 32 elements; here each lane owns a
+// whole vector, so the arithmetic is the same per element but nothing crosses
+// lanes.  Every lane copies its fp16 row (one 1-D bulk copy) into a padded
+// shared-memory row of its warp's double buffer, so the 16-byte reads that
+// follow spread over all banks.  The mean-|x| sum is evaluated in the
+// reference's block-tree order (leaf t = |x_t|, strides 64, 32, ..., 1), depth
+// first so that only one partial per level is live; the residual uses the
+// same operations as quantise_residual (fast-math 7/absmax, cvt.rni, clamp),
+// so the planes are bit-identical to the per-warp encoder's.
+// ---------------------------------------------------------------------------
+constexpr int kLpvWarps = 4;
+
+template <int D>
+struct LpvCfg {
+    static constexpr int ROWB = 2 * D + 16;         // padded row: consecutive lanes start 16 B apart in bank terms
+    static constexpr int BUFB = 32 * ROWB;          // one batch of 32 vectors
+    static constexpr int WARPB = 2 * BUFB + 16;     // double buffer + 2 mbarriers
+    static constexpr int SMEM_B = kLpvWarps * WARPB + 128;
+};
+
+// Eight fp32 values of one 16-byte chunk of fp16 elements.
+__device__ __forceinline__ void lpv_chunk(const uint4& t, float (&x)[8]) {
+    const uint32_t w[4] = {t.x, t.y, t.z, t.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+        x[2 * i] = f.x;
+        x[2 * i + 1] = f.y;
+    }
+}
+
+// The reference's 128-leaf stride-halving tree (leaf t = |x_t|, 0 beyond
+// head_dim; strides 64, 32, ..., 1), split by the position j = t % 8 within a
+// 16-byte chunk k = t / 8: strides 64, 32, 16, 8 pair chunks differing in bit
+// 3, 2, 1, 0 of k, so for each j the partial after stride 8 is the same tree
+// over the 16 chunks, whose root joins the chunks differing in bit 0.
+// lpv_tree16 walks it depth first (level L joins chunks differing in bit L;
+// one chunk read per leaf, four levels live); strides 4, 2, 1 then combine
+// the eight per-position partials.
+template <int D, int L, int K>
+__device__ __forceinline__ void lpv_tree16(const uint4* row, float (&out)[8]) {
+    if constexpr (L == 4) {  // leaf: chunk K
+        if constexpr (8 * K >= D) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) out[j] = 0.0f;
+        } else {
+            float x[8];
+            lpv_chunk(row[K], x);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) out[j] = fabsf(x[j]);
+        }
+    } else if constexpr (8 * (K + (1 << L)) >= D) {
+        // the right subtree covers chunks beyond head_dim only: adding +0.0f is exact for a >= 0
+        lpv_tree16<D, L + 1, K>(row, out);
+    } else {
+        float right[8];
+        lpv_tree16<D, L + 1, K>(row, out);
+        lpv_tree16<D, L + 1, K + (1 << L)>(row, right);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) out[j] += right[j];
+    }
+}
+
+template <int D>
+__device__ __forceinline__ float lpv_abs_sum(const uint4* row) {
+    float a[8];
+    lpv_tree16<D, 0, 0>(row, a);
+    const float u0 = a[0] + a[4], u1 = a[1] + a[5], u2 = a[2] + a[6], u3 = a[3] + a[7];  // stride 4
+    const float v0 = u0 + u2, v1 = u1 + u3;                                              // stride 2
+    return v0 + v1;                                                                      // stride 1
+}
+
+// Encode the vector in shared-memory row `row` into plane row v (lane-local).
+template <int NW, int RES>
+__device__ __forceinline__ void lpv_encode_row(const uint4* row, bc_kv_planes P, int64_t v, int seq_len,
+                                               int64_t kv_stride, int head_dim) {
+    constexpr int D = 32 * NW;
+    const float mean_abs = lpv_abs_sum<D>(row) / (float)head_dim;
+    const uint16_t sb = f2h_bits(mean_abs);
+    const float sc = (RES == BC_RES_FP16_SCALE) ? __half2float(__ushort_as_half(sb)) : mean_abs;
+    // signs (x >= 0, so -0 -> 1 and NaN -> 0) and the residual absmax in one pass
+    uint32_t w[NW];
+    float absmax = 0.0f;
+#pragma unroll
+    for (int k = 0; k < NW; ++k) {
+        uint32_t word = 0;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            float x[8];
+            lpv_chunk(row[4 * k + c], x);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const bool bit = x[j] >= 0.0f;
+                word |= (bit ? 1u : 0u) << (8 * c + j);
+                if (RES != BC_RES_NONE) absmax = fmaxf(absmax, fabsf(x[j] - (bit ? sc : -sc)));
+            }
+        }
+        w[k] = word;
+    }
+    const int64_t slot = v / seq_len, pos = v - slot * seq_len;
+    const int64_t r = slot * kv_stride + pos;
+    uint32_t* srow = reinterpret_cast<uint32_t*>(P.sign) + r * NW;
+    if constexpr (NW == 4) {
+        *reinterpret_cast<uint4*>(srow) = make_uint4(w[0], w[1], w[2], w[3]);
+    } else if constexpr (NW == 2) {
+        *reinterpret_cast<uint2*>(srow) = make_uint2(w[0], w[1]);
+    } else {
+#pragma unroll
+        for (int k = 0; k < NW; ++k) srow[k] = w[k];
+    }
+    reinterpret_cast<uint16_t*>(P.bscale)[r] = sb;
+    if constexpr (RES != BC_RES_NONE) {
+        const float inv_absmax = (absmax > 0.0f) ? (7.0f / absmax) : 0.0f;
+        // Rounding.  With inv_absmax > 0 the scale is finite and every r finite
+        // with |r * inv_absmax| <= 7 (to a few ulp), so adding 1.5 * 2^23 rounds
+        // to the nearest integer, ties to even, exactly as cvt.rni, and leaves
+        // the code's two's complement in the low 4 bits; the reference's clamp
+        // to [-7, 7] never binds.  inv_absmax == 0 (zero, NaN or infinite input)
+        // gives code 0 everywhere, as cvt.rni of 0 or NaN does.
+        const bool live = inv_absmax > 0.0f;
+        constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
+        uint8_t* nb = reinterpret_cast<uint8_t*>(P.nib);
+#pragma unroll
+        for (int k = 0; k < NW; ++k) {
+            uint32_t wd[4];
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                float x[8];
+                lpv_chunk(row[4 * k + c], x);
+                uint32_t word = 0;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    const float rec = ((w[k] >> (8 * c + j)) & 1u) ? sc : -sc;
+                    // __fmul_rn: the product is rounded to fp32 first, as before cvt.rni
+                    // (a contracted fma would round the exact product instead)
+                    const uint32_t q = __float_as_uint(__fadd_rn(__fmul_rn(x[j] - rec, inv_absmax), kRound));
+                    word |= (q & 0xFu) << (4 * j);
+                }
+                wd[c] = live ? word ^ 0x88888888u : 0x88888888u;  // offset-binary: code + 8
+            }
+            *reinterpret_cast<uint4*>(nb + nib_chunk_offset(r, k, D)) = make_uint4(wd[0], wd[1], wd[2], wd[3]);
+        }
+        reinterpret_cast<uint16_t*>(P.rscale)[r] = f2h_bits(absmax);
+    }
+}
+
+template <int NW, int RES>
+__global__ void __launch_bounds__(kLpvWarps * 32, 3) k_encode_planes_lpv(const __half* __restrict__ src, bc_kv_planes P,
+                                                                      int seq_len, int64_t kv_stride, int head_dim,
+                                                                      int64_t n, unsigned int* err) {
+    constexpr int D = 32 * NW;
+    using C = LpvCfg<D>;
+    extern __shared__ __align__(128) uint8_t lpv_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(lpv_raw) + 127) & ~uintptr_t(127));
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    uint8_t* wbuf = smem + warp * C::WARPB;
+    uint64_t* full = reinterpret_cast<uint64_t*>(wbuf + 2 * C::BUFB);
+    const int64_t n_batches = (n + 31) / 32;
+    const int64_t stride_b = (int64_t)gridDim.x * kLpvWarps;
+    const int64_t first = (int64_t)blockIdx.x * kLpvWarps + warp;
+    if (lane == 0) {
+        mbar_init(&full[0], 1);
+        mbar_init(&full[1], 1);
+        fence_mbar_init();
+    }
+    __syncwarp();
+    auto issue = [&](int64_t b, int buf) {
+        const int cnt = (int)min((int64_t)32, n - 32 * b);
+        if (lane == 0) mbar_arrive_expect_tx(&full[buf], (uint32_t)cnt * 2 * D);
+        __syncwarp();
+        if (lane < cnt)
+            bulk_g2s(wbuf + buf * C::BUFB + lane * C::ROWB, src + (32 * b + lane) * D, 2 * D, &full[buf]);
+    };
+    if (first < n_batches) issue(first, 0);
+    if (first + stride_b < n_batches) issue(first + stride_b, 1);
+    int it = 0;
+    for (int64_t b = first; b < n_batches; b += stride_b, ++it) {
+        const int buf = it & 1;
+        if (!mbar_wait_bounded(&full[buf], (uint32_t)(it >> 1) & 1u)) {
+            if (lane == 0) raise_device_error(err, BC_DEVERR_TIMEOUT);
+            // drain what is still in flight (bounded), then leave
+            if (b + stride_b < n_batches) mbar_wait_bounded(&full[buf ^ 1], (uint32_t)((it + 1) >> 1) & 1u);
+            return;
+        }
+        const int64_t v = 32 * b + lane;
+        if (v < n) {
+            const uint4* row = reinterpret_cast<const uint4*>(wbuf + buf * C::BUFB + lane * C::ROWB);
+            lpv_encode_row<NW, RES>(row, P, v, seq_len, kv_stride, head_dim);
+        }
+        __syncwarp();
+        // the buffer is read: refill it with the batch two steps ahead
+        if (b + 2 * stride_b < n_batches) {
+            fence_proxy_async_smem();
+            issue(b + 2 * stride_b, buf);
+        }
+    }
+}
+
 // Append one K and one V token per slot: warps [0, n_slots) encode K, the rest V.
 template <int NW, int RES>
 __global__ void __launch_bounds__(kEncWarps * 32) k_append_kv(const __half* __restrict__ k,
@@ -210,6 +410,49 @@ using namespace bc;
 
 static inline unsigned enc_blocks(int64_t n) { return (unsigned)((n + kEncWarps - 1) / kEncWarps); }
 
+template <int NW, int RES>
+static int launch_lpv(const void* src, bc_kv_planes out, int64_t n, int seq_len, int64_t kv_stride, int head_dim,
+                      int sms, cudaStream_t st) {
+    constexpr int smem = LpvCfg<32 * NW>::SMEM_B;
+    static bool attr_set[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+        cudaFuncSetAttribute(k_encode_planes_lpv<NW, RES>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        attr_set[dev] = true;
+    }
+    int per_sm = 1;
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_encode_planes_lpv<NW, RES>, kLpvWarps * 32, smem);
+    const int64_t batches = (n + 31) / 32;
+    const int64_t want = (batches + kLpvWarps - 1) / kLpvWarps;
+    const int64_t cap = (int64_t)sms * (per_sm > 0 ? per_sm : 1);
+    const unsigned blocks = (unsigned)(want < cap ? want : cap);
+    k_encode_planes_lpv<NW, RES><<<blocks, kLpvWarps * 32, smem, st>>>((const __half*)src, out, seq_len, kv_stride,
+                                                                        head_dim, n, bc_device_error_ptr());
+    BC_LAUNCH_CHECK();
+    return BC_OK;
+}
+
+template <int RES>
+static int lpv_dispatch(const void* src, bc_kv_planes out, int64_t n, int seq_len, int64_t kv_stride, int head_dim,
+                        int sms, cudaStream_t st) {
+    switch (head_dim / 32) {
+        case 1: return launch_lpv<1, RES>(src, out, n, seq_len, kv_stride, head_dim, sms, st);
+        case 2: return launch_lpv<2, RES>(src, out, n, seq_len, kv_stride, head_dim, sms, st);
+        case 3: return launch_lpv<3, RES>(src, out, n, seq_len, kv_stride, head_dim, sms, st);
+        default: return launch_lpv<4, RES>(src, out, n, seq_len, kv_stride, head_dim, sms, st);
+    }
+}
+
+static int encode_planes_lpv(const void* src, bc_kv_planes out, int64_t n, int seq_len, int64_t kv_stride,
+                             int head_dim, int residual_mode, int sms, cudaStream_t st) {
+    switch (residual_mode) {
+        case BC_RES_NONE: return lpv_dispatch<BC_RES_NONE>(src, out, n, seq_len, kv_stride, head_dim, sms, st);
+        case BC_RES_FP16_SCALE: return lpv_dispatch<BC_RES_FP16_SCALE>(src, out, n, seq_len, kv_stride, head_dim, sms, st);
+        default: return lpv_dispatch<BC_RES_FP32_SCALE>(src, out, n, seq_len, kv_stride, head_dim, sms, st);
+    }
+}
+
 extern "C" {
 
 int64_t bc_sizeof_binary_vec(void) { return kBinRecBytes; }
@@ -299,6 +542,8 @@ int bc_encode_planes(const void* src, bc_kv_planes out, int n_slots, int seq_len
     const int64_t want = (n + (int64_t)kEncWarps * kVecsPerWarp - 1) / ((int64_t)kEncWarps * kVecsPerWarp);
     const unsigned blocks = (unsigned)(want < max_blocks ? want : max_blocks);
     cudaStream_t st = (cudaStream_t)stream;
+    if (head_dim <= 128 && bc_aligned(src, 16)) return encode_planes_lpv(src, out, n, seq_len, kv_stride, head_dim,
+                                                                         residual_mode, sms, st);
     switch (residual_mode) {
         case BC_RES_NONE:
             BC_DISPATCH_NW(head_dim, (k_encode_planes<NW, BC_RES_NONE><<<blocks, kEncWarps * 32, 0, st>>>(

@@ -165,3 +165,32 @@ def test_record_plane_converters_roundtrip(cuda, d):
     for f in (0, 1):
         assert np.array_equal(fields_bin(b2, d)[f], fields_bin(b, d)[f])
         assert np.array_equal(fields_res(r2, d)[f], fields_res(r, d)[f])
+
+
+@pytest.mark.parametrize("d", D_ALL)
+@pytest.mark.parametrize("mode", [planes.RES_FP16_SCALE, planes.RES_FP32_SCALE, planes.RES_NONE])
+def test_plane_encode_edge_vectors_bit_exact(cuda, d, mode):
+    """Zero, -0, subnormal, huge, inf and NaN vectors through the prefill encoder
+    (the lane-per-vector kernel at head_dim <= 128) against the reference kernels
+    (FP16 scale: residual.cu) or the online encoder (FP32 scale: online_encode.cu)."""
+    x = with_edges(src(61, d, 900 + d)).to(cuda)
+    n = x.shape[0]
+    P = planes.Planes.empty(1, planes.round_stride(n), d, mode != planes.RES_NONE, cuda)
+    planes.encode_planes(x.view(1, n, d), P, mode)
+    rb = refgpu.binary_encode(x)
+    wr, sr = fields_bin(rb, d)
+    torch.cuda.synchronize()
+    assert np.array_equal(P.sign[0, :n].cpu().numpy().view(np.uint32), wr)
+    assert np.array_equal(P.bscale[0, :n].cpu().numpy().view(np.uint16), sr)
+    if mode == planes.RES_FP16_SCALE:
+        nr, rsr = fields_res(refgpu.residual_encode(x, rb), d)
+    elif mode == planes.RES_FP32_SCALE:
+        bb = torch.zeros(n * 36, dtype=torch.uint8, device=cuda)
+        rr = torch.zeros(n * 130, dtype=torch.uint8, device=cuda)
+        refgpu.online_encode_token(x, bb, rr, 1, n, d, 0, 1)  # n slots of a 1-position ring
+        nr, rsr = fields_res(rr, d)
+    else:
+        return
+    torch.cuda.synchronize()
+    assert np.array_equal(P.nib_rows()[0, :n].cpu().numpy(), nr)
+    assert np.array_equal(P.rscale[0, :n].cpu().numpy().view(np.uint16), rsr)
