@@ -47,7 +47,9 @@ def parse():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", default="C3", choices=["C1", "C2", "C3", "C4", "C5"])
-    ap.add_argument("--split", default="heads", choices=["heads", "seq"])
+    ap.add_argument("--split", default="heads", choices=["heads", "seq", "seqx"],
+                    help="N>1: shard heads, split the sequence with an NCCL all-gather + merge (seq), or split "
+                         "the sequence with the kernel's own peer-memory exchange (seqx)")
     ap.add_argument("--binary", action="store_true", help="binary-only attention instead of compensated")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-ref-gpu", action="store_true")
@@ -299,11 +301,14 @@ def main():
     out = torch.empty((my_slots * G, d), dtype=torch.float16, device=dev)
     part = torch.empty((my_slots * G, d + 2), dtype=torch.float32, device=dev)
     seq_split = world > 1 and args.split == "seq"
+    xchg = bdist.PeerExchange(my_slots * G, d) if (world > 1 and args.split == "seqx") else None
 
     def step(i):
         K, V = Ks[i % copies], Vs[i % copies]
         if adaptive:
             planes.decode_attention_adaptive(q_all, K, V, my_S, n_keep, out=out)
+        elif xchg is not None:
+            xchg.decode(q_all, K, V, my_S, mode, out=out)
         elif seq_split:
             planes.decode_attention(q_all, K, V, my_S, mode, partial=part, want_out=False)
         else:
@@ -502,6 +507,8 @@ def main():
         line["cpu_baseline"] = cpu_baseline(args, comp, bytes_total)
     if rank == 0:
         print(json.dumps(line), flush=True)
+    if xchg is not None:
+        xchg.close()
     if pg is not None:
         pg.barrier()
         pg.destroy_process_group()

@@ -43,6 +43,13 @@ class PageTable(ctypes.Structure):
                 ("n_pages", ctypes.c_int32)]
 
 
+class Xchg(ctypes.Structure):
+    """bc_xchg: every rank's exchange buffer as mapped here, world, rank, epoch."""
+
+    _fields_ = [("bufs", c_void_p * 8), ("world", ctypes.c_int32), ("rank", ctypes.c_int32),
+                ("epoch", ctypes.c_uint32)]
+
+
 _SIGS = {
     "bc_status_string": (ctypes.c_char_p, [c_int]),
     "bc_get_device_error": (ctypes.c_uint, [c_int]),
@@ -78,6 +85,14 @@ _SIGS = {
     "bc_decode_adaptive_workspace_bytes": (c_size_t, [c_int, c_int, c_int, c_int, c_int]),
     "bc_decode_attention_adaptive": (c_int, [c_void_p, KVPlanes, KVPlanes, c_void_p, c_void_p, c_int, c_int, c_int,
                                              c_int, c_int64, c_int64, c_int, c_void_p, c_size_t, c_void_p]),
+    "bc_xchg_bytes": (c_size_t, [c_int, c_int, c_int]),
+    "bc_xchg_alloc": (c_int, [c_size_t, ctypes.POINTER(c_void_p)]),
+    "bc_xchg_free": (c_int, [c_void_p]),
+    "bc_ipc_handle": (c_int, [c_void_p, c_void_p]),
+    "bc_ipc_open": (c_int, [c_void_p, ctypes.POINTER(c_void_p)]),
+    "bc_ipc_close": (c_int, [c_void_p]),
+    "bc_decode_attention_xchg": (c_int, [c_void_p, KVPlanes, KVPlanes, c_void_p, c_int, c_int, c_int, c_int64, c_int,
+                                         c_int, Xchg, c_void_p, c_size_t, c_void_p]),
     "bc_decode_step_paged": (c_int, [c_void_p, c_void_p, c_void_p, KVPlanes, KVPlanes, c_void_p, c_void_p, PageTable,
                                      c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_void_p, c_size_t, c_void_p]),
     "bc_append_kv_paged": (c_int, [c_void_p, c_void_p, KVPlanes, KVPlanes, PageTable, c_int, c_int, c_int64, c_int,

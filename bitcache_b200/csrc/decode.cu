@@ -34,6 +34,7 @@
 // (pattern * 2^-149) of packed fma.rn.f32x2 with one coefficient per key;
 // each accumulator carries the fixed power-of-two scale of its bit position,
 // removed once per CTA together with the constant parts sum_s (a_s + 8 c_s).
+#include <cstring>
 #include <mutex>
 
 #include "encode_core.cuh"
@@ -138,6 +139,13 @@ struct DecodeArgs {
     // remaining splits the second with kps_bin keys each.
     int n_keep, nc, kps_bin, b0;
     int64_t res_stride;
+    // sequence split over peer memory (xw > 0): the final (m, l, o) of every
+    // head goes straight into every rank's exchange buffer, a flag per
+    // (rank, unit) says it landed, and each rank merges the xw partials itself
+    float* xparts[8];   // rank j's buffer as mapped here: [2 parities][xw][n_heads][d+2]
+    unsigned* xflags[8];  // rank j's flags: [xw][n_heads] (unit index < n_heads)
+    int xw, xrank;
+    unsigned xepoch;
 };
 
 // Plane row of logical position `pos` of `slot`, or -1 for a page id outside
@@ -571,6 +579,101 @@ __device__ __forceinline__ EntPart ent_merge(EntPart a, EntPart b) {
 
 __device__ __forceinline__ float ent_value(EntPart t) { return logf(t.z) + t.m - t.w / fmaxf(t.z, 1e-12f); }
 
+// Final (m in log2 units, l, o) of head h, dim i: to the outputs, or in an
+// exchange to this rank's slot of every rank's buffer (natural-log m).
+template <int D>
+__device__ __forceinline__ void emit_final(const DecodeArgs& a, int64_t h, int i, float M, float L, float O) {
+    if (a.xw > 0) {
+        const int64_t n_heads = (int64_t)a.n_slots * a.group;
+        const int64_t off = (((int64_t)(a.xepoch & 1u) * a.xw + a.xrank) * n_heads + h) * (D + 2);
+        for (int j = 0; j < a.xw; ++j) {
+            float* p = a.xparts[j] + off;
+            if (i == 0) {
+                p[0] = M * kLn2;
+                p[1] = L;
+            }
+            p[2 + i] = O;
+        }
+        return;
+    }
+    if (a.out) a.out[h * D + i] = __float2half((L > 0.0f) ? O * (1.0f / L) : 0.0f);
+    if (a.partial) {
+        float* p = a.partial + h * (D + 2);
+        if (i == 0) {
+            p[0] = M * kLn2;
+            p[1] = L;
+        }
+        p[2 + i] = O;
+    }
+}
+
+__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Exchange epilogue of a (slot, head group): publish this rank's flag on every
+// rank, wait (bounded) for every rank's flag here, then merge the xw partials
+// of the CTA's heads from this rank's buffer and write the output.  Flags
+// carry the call's epoch and are compared as "at least", so a rank that is a
+// step ahead never hides the current step's arrival; partials alternate
+// between two parity halves, so that rank cannot overwrite data still read.
+constexpr uint32_t kXchgSpinLimit = 1u << 22;  // x ~100 ns sleeps: well under a second
+
+template <int D, int GC>
+__device__ __forceinline__ void xchg_finish(const DecodeArgs& a, int slot, int hg) {
+    const int tid = threadIdx.x;
+    const int64_t n_heads = (int64_t)a.n_slots * a.group;
+    const int unit = slot * a.n_hgroups + hg;
+    __threadfence_system();  // this thread's partial stores precede the flags
+    __syncthreads();
+    if (tid < a.xw) st_release_sys(a.xflags[tid] + (int64_t)a.xrank * n_heads + unit, a.xepoch);
+    __shared__ int s_timeout;
+    if (tid == 0) s_timeout = 0;
+    __syncthreads();
+    if (tid < a.xw) {
+        const unsigned* f = a.xflags[a.xrank] + (int64_t)tid * n_heads + unit;
+        for (uint32_t it = 0; (int)(ld_acquire_sys(f) - a.xepoch) < 0; ++it) {
+            if (it >= kXchgSpinLimit) {
+                s_timeout = 1;
+                break;
+            }
+            __nanosleep(100);
+        }
+    }
+    __syncthreads();
+    const int64_t head0 = (int64_t)slot * a.group + (int64_t)hg * GC;
+    if (s_timeout) {
+        if (tid == 0) raise_device_error(&g_bc_device_error, BC_DEVERR_TIMEOUT);
+        return;
+    }
+    const float* base = a.xparts[a.xrank] + (int64_t)(a.xepoch & 1u) * a.xw * n_heads * (D + 2);
+    for (int idx = tid; idx < GC * D; idx += kDecThreads) {
+        const int g = idx / D, i = idx % D;
+        const int64_t h = head0 + g;
+        float M = -INFINITY;
+        for (int j = 0; j < a.xw; ++j) {
+            const float* r = base + ((int64_t)j * n_heads + h) * (D + 2);
+            if (__ldcg(r + 1) > 0.0f) M = fmaxf(M, __ldcg(r));
+        }
+        float L = 0.0f, O = 0.0f;
+        for (int j = 0; j < a.xw; ++j) {
+            const float* r = base + ((int64_t)j * n_heads + h) * (D + 2);
+            const float l = __ldcg(r + 1);
+            if (l > 0.0f) {
+                const float f = __expf(__ldcg(r) - M);
+                L += l * f;
+                O += __ldcg(r + 2 + i) * f;
+            }
+        }
+        if (a.out) a.out[h * D + i] = __float2half((L > 0.0f) ? O * (1.0f / L) : 0.0f);
+    }
+}
+
 // ---------------------------------------------------------------------------
 // End of a CTA: reduce each warp, merge the warps (log-sum-exp), then either
 // write the outputs (single split) or publish a partial and let the last CTA
@@ -660,15 +763,7 @@ __device__ __forceinline__ void finish_cta(const DecodeArgs& a, int slot, int hg
         }
         const int64_t h = head0 + g;
         if (single) {
-            if (a.out) a.out[h * D + i] = __float2half((L > 0.0f) ? O * (1.0f / L) : 0.0f);
-            if (a.partial) {
-                float* p = a.partial + h * (D + 2);
-                if (i == 0) {
-                    p[0] = M * kLn2;
-                    p[1] = L;
-                }
-                p[2 + i] = O;
-            }
+            emit_final<D>(a, h, i, M, L, O);
         } else {
             float* p = a.ws_part + (h * a.n_splits + split) * (D + 2);
             if (i == 0) {
@@ -678,7 +773,10 @@ __device__ __forceinline__ void finish_cta(const DecodeArgs& a, int slot, int hg
             p[2 + i] = O;
         }
     }
-    if (single) return;
+    if (single) {
+        if (a.xw > 0) xchg_finish<D, GC>(a, slot, hg);
+        return;
+    }
     __shared__ unsigned s_last;
     __syncthreads();
     if (tid == 0) {
@@ -723,15 +821,7 @@ __device__ __forceinline__ void finish_cta(const DecodeArgs& a, int slot, int hg
             }
             M = Mn;
         }
-        if (a.out) a.out[h * D + i] = __float2half((L > 0.0f) ? O * (1.0f / L) : 0.0f);
-        if (a.partial) {
-            float* p = a.partial + h * (D + 2);
-            if (i == 0) {
-                p[0] = M * kLn2;
-                p[1] = L;
-            }
-            p[2 + i] = O;
-        }
+        emit_final<D>(a, h, i, M, L, O);
     }
     if constexpr (ENT) {
         if (tid < GC) {
@@ -744,6 +834,7 @@ __device__ __forceinline__ void finish_cta(const DecodeArgs& a, int slot, int hg
         }
     }
     if (tid == 0) a.ws_cnt[(int64_t)slot * a.n_hgroups + hg] = 0u;  // leave the counter zeroed
+    if (a.xw > 0) xchg_finish<D, GC>(a, slot, hg);
 }
 
 __device__ __forceinline__ void cta_coords(const DecodeArgs& a, int& slot, int& hg, int& split) {
@@ -1441,6 +1532,75 @@ int bc_decode_attention(const void* q, bc_kv_planes K, bc_kv_planes V, void* out
     const int rc = check_decode_args(q, K, V, out, partial, n_slots, group, seq_len, kv_stride, head_dim, mode);
     if (rc != BC_OK || n_slots == 0) return rc;
     const DecodeArgs a = decode_args(q, K, V, out, partial, n_slots, group, seq_len, kv_stride, head_dim);
+    return run_decode(a, mode == BC_MODE_COMPENSATED, kVarPlanes, workspace, workspace_bytes, (cudaStream_t)stream);
+}
+
+size_t bc_xchg_bytes(int n_heads, int head_dim, int world) {
+    if (n_heads <= 0 || world <= 0 || world > 8 || !bc_valid_head_dim(head_dim)) return 0;
+    const size_t parts = (size_t)2 * world * n_heads * (head_dim + 2) * sizeof(float);
+    const size_t flags = (size_t)world * n_heads * sizeof(unsigned);
+    return ((parts + 255) & ~(size_t)255) + ((flags + 255) & ~(size_t)255);
+}
+
+int bc_xchg_alloc(size_t bytes, void** buf) {
+    if (!buf || bytes == 0) return BC_ERR_ARG;
+    void* p = nullptr;
+    cudaError_t e = cudaMalloc(&p, bytes);
+    if (e != cudaSuccess) return BC_ERR_CUDA_BASE + (int)e;
+    e = cudaMemset(p, 0, bytes);
+    if (e != cudaSuccess) {
+        cudaFree(p);
+        return BC_ERR_CUDA_BASE + (int)e;
+    }
+    *buf = p;
+    return BC_OK;
+}
+
+int bc_xchg_free(void* buf) {
+    const cudaError_t e = cudaFree(buf);
+    return e == cudaSuccess ? BC_OK : BC_ERR_CUDA_BASE + (int)e;
+}
+
+int bc_ipc_handle(const void* buf, void* handle) {
+    if (!buf || !handle) return BC_ERR_ARG;
+    cudaIpcMemHandle_t h;
+    const cudaError_t e = cudaIpcGetMemHandle(&h, const_cast<void*>(buf));
+    if (e != cudaSuccess) return BC_ERR_CUDA_BASE + (int)e;
+    static_assert(sizeof(h) == 64, "cudaIpcMemHandle_t is 64 bytes");
+    memcpy(handle, &h, sizeof(h));
+    return BC_OK;
+}
+
+int bc_ipc_open(const void* handle, void** buf) {
+    if (!handle || !buf) return BC_ERR_ARG;
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handle, sizeof(h));
+    const cudaError_t e = cudaIpcOpenMemHandle(buf, h, cudaIpcMemLazyEnablePeerAccess);
+    return e == cudaSuccess ? BC_OK : BC_ERR_CUDA_BASE + (int)e;
+}
+
+int bc_ipc_close(void* buf) {
+    const cudaError_t e = cudaIpcCloseMemHandle(buf);
+    return e == cudaSuccess ? BC_OK : BC_ERR_CUDA_BASE + (int)e;
+}
+
+int bc_decode_attention_xchg(const void* q, bc_kv_planes K, bc_kv_planes V, void* out, int n_slots, int group,
+                             int seq_len, int64_t kv_stride, int head_dim, int mode, bc_xchg x, void* workspace,
+                             size_t workspace_bytes, void* stream) {
+    const int rc = check_decode_args(q, K, V, out, nullptr, n_slots, group, seq_len, kv_stride, head_dim, mode);
+    if (rc != BC_OK || n_slots == 0) return rc;
+    if (!out || x.world < 1 || x.world > 8 || x.rank < 0 || x.rank >= x.world || x.epoch == 0) return BC_ERR_ARG;
+    const int64_t n_heads = (int64_t)n_slots * group;
+    const size_t parts = (size_t)2 * x.world * n_heads * (head_dim + 2) * sizeof(float);
+    DecodeArgs a = decode_args(q, K, V, out, nullptr, n_slots, group, seq_len, kv_stride, head_dim);
+    for (int j = 0; j < x.world; ++j) {
+        if (!x.bufs[j] || !bc_aligned(x.bufs[j], 256)) return BC_ERR_ARG;
+        a.xparts[j] = reinterpret_cast<float*>(x.bufs[j]);
+        a.xflags[j] = reinterpret_cast<unsigned*>(reinterpret_cast<uint8_t*>(x.bufs[j]) + ((parts + 255) & ~(size_t)255));
+    }
+    a.xw = x.world;
+    a.xrank = x.rank;
+    a.xepoch = x.epoch;
     return run_decode(a, mode == BC_MODE_COMPENSATED, kVarPlanes, workspace, workspace_bytes, (cudaStream_t)stream);
 }
 

@@ -11,6 +11,11 @@ NCCL (NVLink) and merged with the log-sum-exp rule on every rank.
 
 The collective and the merge are passed in, so the host logic here runs
 unchanged over NCCL on GPUs and over gloo on CPU in the tests.
+
+PeerExchange is the fused alternative for the sequence split: the decode
+kernel itself stores each head's triple into every rank's buffer over
+NVLink, raises a flag there and merges on arrival (bc_decode_attention_xchg),
+so a step is one launch per rank with no separate collective or merge.
 """
 from __future__ import annotations
 
@@ -87,3 +92,84 @@ def nccl_all_gather(group=None) -> Callable[[torch.Tensor], torch.Tensor]:
         return out
 
     return fn
+
+
+class PeerExchange:
+    """Exchange buffers for bc_decode_attention_xchg (one process per GPU).
+
+    Construction is collective over `group` (torch.distributed): every rank
+    allocates its buffer (bc_xchg_alloc), the 64-byte CUDA IPC handles are
+    all-gathered, and the peers' buffers are mapped (bc_ipc_open).  With
+    world size 1 (no process group) the buffer is only this rank's own.
+    """
+
+    def __init__(self, n_heads: int, head_dim: int, group=None) -> None:
+        import ctypes
+
+        from . import _lib
+
+        dist = torch.distributed
+        self._lib = _lib
+        lib = _lib.load()
+        on = dist.is_available() and dist.is_initialized()
+        self.world = dist.get_world_size(group) if on else 1
+        self.rank = dist.get_rank(group) if on else 0
+        if self.world > 8:
+            raise RuntimeError("PeerExchange supports up to 8 ranks")
+        self.n_heads, self.head_dim = n_heads, head_dim
+        nbytes = lib.bc_xchg_bytes(n_heads, head_dim, self.world)
+        own = ctypes.c_void_p()
+        _lib.check(lib.bc_xchg_alloc(nbytes, ctypes.byref(own)), "xchg_alloc")
+        self._own = own.value
+        self._opened: list[int] = []
+        bufs = [0] * self.world
+        bufs[self.rank] = self._own
+        if self.world > 1:
+            handle = (ctypes.c_char * 64)()
+            _lib.check(lib.bc_ipc_handle(self._own, handle), "ipc_handle")
+            handles: list = [None] * self.world
+            dist.all_gather_object(handles, bytes(handle), group=group)
+            for j in range(self.world):
+                if j == self.rank:
+                    continue
+                p = ctypes.c_void_p()
+                hb = (ctypes.c_char * 64).from_buffer_copy(handles[j])
+                _lib.check(lib.bc_ipc_open(hb, ctypes.byref(p)), "ipc_open")
+                bufs[j] = p.value
+                self._opened.append(p.value)
+        self._x = _lib.Xchg()
+        for j, b in enumerate(bufs):
+            self._x.bufs[j] = b
+        self._x.world, self._x.rank, self._x.epoch = self.world, self.rank, 0
+
+    def decode(self, q: torch.Tensor, K, V, seq_len: int, mode: int, out: torch.Tensor | None = None) -> torch.Tensor:
+        """One sequence-split decode step: this rank's slice [K, V] of every slot,
+        the merged output of all heads on every rank."""
+        lib = self._lib.load()
+        d = q.shape[-1]
+        n_heads = q.numel() // d
+        n_slots = K.n_slots
+        group = n_heads // n_slots
+        if out is None:
+            out = torch.empty((n_heads, d), dtype=torch.float16, device=q.device)
+        st = self._lib.stream_of(q.device)
+        wsb = lib.bc_decode_workspace_bytes(n_slots, group, seq_len, d)
+        ws = self._lib.workspace(q.device, st, wsb, ("decode", n_slots, group))
+        self._x.epoch += 1
+        self._lib.check(lib.bc_decode_attention_xchg(q.data_ptr(), K.c(), V.c(), out.data_ptr(), n_slots, group,
+                                                     seq_len, K.kv_stride, d, mode, self._x, self._lib.ptr(ws),
+                                                     ws.numel() if ws is not None else 0, st), "decode_attention_xchg")
+        return out
+
+    def close(self) -> None:
+        """Unmap the peers' buffers and free this rank's (after all ranks are done with it)."""
+        lib = self._lib.load()
+        torch.cuda.synchronize()
+        if self.world > 1 and torch.distributed.is_initialized():
+            torch.distributed.barrier()
+        for p in self._opened:
+            lib.bc_ipc_close(p)
+        self._opened = []
+        if self._own:
+            lib.bc_xchg_free(self._own)
+            self._own = None

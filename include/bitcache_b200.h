@@ -241,6 +241,35 @@ int bc_decode_attention_adaptive(const void* q, bc_kv_planes K, bc_kv_planes V, 
                                  int64_t res_stride, int head_dim, void* workspace, size_t workspace_bytes,
                                  void* stream);
 
+/* ---- sequence split over peer memory (one process per GPU) ------------
+ * Each rank holds a contiguous slice of every slot's positions.  Instead of
+ * an NCCL all-gather of the (m, l, o) triples followed by bc_lse_merge, the
+ * last CTA of every (slot, head group) stores its triple directly into every
+ * rank's exchange buffer over NVLink (plain peer stores), raises a flag there
+ * (st.release.sys), waits for the flags of all ranks in its own buffer (a
+ * bounded spin: BC_DEVERR_TIMEOUT after about a second) and merges the world
+ * triples itself, so one launch per rank yields the full output on every
+ * rank.  Setup (allocates, outside the decode loop): bc_xchg_alloc on every
+ * rank, share the 64-byte bc_ipc_handle of each buffer, bc_ipc_open the
+ * peers' handles.  Every rank calls bc_decode_attention_xchg with the same
+ * n_slots, group, head_dim and epoch (1, 2, 3, ...: one per call); ranks run
+ * on different GPUs.  No counterpart in the reference. */
+typedef struct bc_xchg {
+    void* bufs[8];  /* rank j's exchange buffer as mapped in this process (bufs[rank] = own) */
+    int32_t world;  /* 1..8 */
+    int32_t rank;
+    uint32_t epoch; /* call number, from 1, equal on every rank */
+} bc_xchg;
+size_t bc_xchg_bytes(int n_heads, int head_dim, int world);
+int bc_xchg_alloc(size_t bytes, void** buf);          /* cudaMalloc + zero fill */
+int bc_xchg_free(void* buf);
+int bc_ipc_handle(const void* buf, void* handle_64_bytes);
+int bc_ipc_open(const void* handle_64_bytes, void** buf);
+int bc_ipc_close(void* buf);
+int bc_decode_attention_xchg(const void* q, bc_kv_planes K, bc_kv_planes V, void* out, int n_slots, int group,
+                             int seq_len, int64_t kv_stride, int head_dim, int mode, bc_xchg x, void* workspace,
+                             size_t workspace_bytes, void* stream);
+
 /* Allocation-free bc_decode_attention, for callers that cannot allocate
  * device memory where they run attention (an engine that reserves all of its
  * GPU memory at start-up and forbids allocation in the decode loop, or a

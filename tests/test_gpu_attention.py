@@ -328,3 +328,28 @@ def test_fused_entropy_matches_reference(cuda, slots, group, S, d, comp):
     torch.cuda.synchronize()
     torch.testing.assert_close(ent, ref, rtol=1e-4, atol=1e-4)
     close(out, plain, f"entropy variant output slots={slots} g={group}")
+
+
+@pytest.mark.parametrize("slots,group,S", [(32, 1, 4096), (3, 4, 700), (2, 1, 100)])
+def test_peer_exchange_single_rank_equals_decode(cuda, slots, group, S):
+    """The fused exchange path on one rank (the buffer is its own; flags go to
+    itself) gives the plain decode's output, step after step."""
+    from bitcache_b200 import dist as bdist
+
+    d = 128
+    g = torch.Generator().manual_seed(S + group)
+    K = planes.Planes.empty(slots, planes.round_stride(S), d, True, cuda)
+    V = planes.Planes.empty(slots, planes.round_stride(S), d, True, cuda)
+    planes.encode_planes((torch.randn(slots, S, d, generator=g) * 0.5).half().to(cuda), K)
+    planes.encode_planes((torch.randn(slots, S, d, generator=g) * 0.5).half().to(cuda), V)
+    x = bdist.PeerExchange(slots * group, d)
+    try:
+        for step in range(4):
+            q = (torch.randn(slots * group, d, generator=g) * 0.5).half().to(cuda)
+            got = x.decode(q, K, V, S, planes.MODE_COMPENSATED)
+            want = planes.decode_attention(q, K, V, S)
+            torch.cuda.synchronize()
+            close(got, want, f"xchg step {step}")
+        assert _lib.device_error() == 0
+    finally:
+        x.close()

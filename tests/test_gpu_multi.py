@@ -52,6 +52,17 @@ def _worker(rank, world, port, mode, out_q):
             pieces = [torch.empty(e - s_, d, dtype=torch.float16, device=dev) for s_, e in sizes]
             dist.all_gather(pieces, mine)
             full = torch.cat(pieces)
+        elif mode == "xchg":
+            a, b = bdist.seq_range(S, world, rank)
+            K = planes.Planes.empty(n, planes.round_stride(b - a), d, True, dev)
+            V = planes.Planes.empty(n, planes.round_stride(b - a), d, True, dev)
+            planes.encode_planes(w.k.reshape(n, S, d)[:, a:b].contiguous(), K)
+            planes.encode_planes(w.v.reshape(n, S, d)[:, a:b].contiguous(), V)
+            x = bdist.PeerExchange(q.shape[0], d)
+            for _ in range(3):  # several epochs through the same buffers
+                full = x.decode(q, K, V, b - a, planes.MODE_COMPENSATED)
+            torch.cuda.synchronize()
+            x.close()
         else:
             a, b = bdist.seq_range(S, world, rank)
             K = planes.Planes.empty(n, planes.round_stride(b - a), d, True, dev)
@@ -79,7 +90,7 @@ def _worker(rank, world, port, mode, out_q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("mode", ["heads", "seq"])
+@pytest.mark.parametrize("mode", ["heads", "seq", "xchg"])
 def test_two_gpu_split_matches_single(mode):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
