@@ -248,6 +248,7 @@ def main():
 
         import torch.distributed as tdist
 
+        os.environ.setdefault("NCCL_DEBUG", "WARN")  # keep rank 0's stdout to the one JSON line
         tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
         pg = tdist
     comp = not args.binary

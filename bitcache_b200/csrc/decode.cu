@@ -140,10 +140,10 @@ struct DecodeArgs {
     int n_keep, nc, kps_bin, b0;
     int64_t res_stride;
     // sequence split over peer memory (xw > 0): the final (m, l, o) of every
-    // head goes straight into every rank's exchange buffer, a flag per
-    // (rank, unit) says it landed, and each rank merges the xw partials itself
-    float* xparts[8];   // rank j's buffer as mapped here: [2 parities][xw][n_heads][d+2]
-    unsigned* xflags[8];  // rank j's flags: [xw][n_heads] (unit index < n_heads)
+    // head goes straight into every rank's exchange buffer as 64-bit words
+    // (value, epoch), and each rank merges the xw partials itself once every
+    // word it needs carries the call's epoch
+    unsigned long long* xparts[8];  // rank j's buffer as mapped here: [2 parities][xw][n_heads][d+2]
     int xw, xrank;
     unsigned xepoch;
 };
@@ -581,18 +581,36 @@ __device__ __forceinline__ float ent_value(EntPart t) { return logf(t.z) + t.m -
 
 // Final (m in log2 units, l, o) of head h, dim i: to the outputs, or in an
 // exchange to this rank's slot of every rank's buffer (natural-log m).
+__device__ __forceinline__ void st_relaxed_sys_u64(unsigned long long* p, unsigned long long v) {
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_relaxed_sys_u64(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+// One exchange word: the value's bits low, the call epoch high.  A single
+// aligned 64-bit access is indivisible, so a reader that sees the epoch sees
+// the value with it: no fence or separate flag is needed.
+__device__ __forceinline__ unsigned long long xword(float v, unsigned epoch) {
+    return ((unsigned long long)epoch << 32) | __float_as_uint(v);
+}
+
 template <int D>
 __device__ __forceinline__ void emit_final(const DecodeArgs& a, int64_t h, int i, float M, float L, float O) {
     if (a.xw > 0) {
         const int64_t n_heads = (int64_t)a.n_slots * a.group;
         const int64_t off = (((int64_t)(a.xepoch & 1u) * a.xw + a.xrank) * n_heads + h) * (D + 2);
-        for (int j = 0; j < a.xw; ++j) {
-            float* p = a.xparts[j] + off;
+        const unsigned long long wo = xword(O, a.xepoch), wm = xword(M * kLn2, a.xepoch), wl = xword(L, a.xepoch);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            if (j >= a.xw) break;
+            unsigned long long* p = a.xparts[j] + off;
             if (i == 0) {
-                p[0] = M * kLn2;
-                p[1] = L;
+                st_relaxed_sys_u64(p, wm);
+                st_relaxed_sys_u64(p + 1, wl);
             }
-            p[2 + i] = O;
+            st_relaxed_sys_u64(p + 2 + i, wo);
         }
         return;
     }
@@ -607,71 +625,62 @@ __device__ __forceinline__ void emit_final(const DecodeArgs& a, int64_t h, int i
     }
 }
 
-__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
-    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
-    unsigned v;
-    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
-
-// Exchange epilogue of a (slot, head group): publish this rank's flag on every
-// rank, wait (bounded) for every rank's flag here, then merge the xw partials
-// of the CTA's heads from this rank's buffer and write the output.  Flags
-// carry the call's epoch and are compared as "at least", so a rank that is a
-// step ahead never hides the current step's arrival; partials alternate
-// between two parity halves, so that rank cannot overwrite data still read.
-constexpr uint32_t kXchgSpinLimit = 1u << 22;  // x ~100 ns sleeps: well under a second
+// Exchange epilogue of a (slot, head group): every thread waits (bounded) for
+// the words of its dims from every rank in this rank's buffer, then merges
+// the xw partials.  Words carry the call's epoch and are compared as "at
+// least"; partials alternate between two parity halves, so a rank that is a
+// step ahead writes the other half and never overwrites data still read.
+constexpr uint32_t kXchgSpinLimit = 1u << 22;  // polls (then 256 ns sleeps): about a second
 
 template <int D, int GC>
 __device__ __forceinline__ void xchg_finish(const DecodeArgs& a, int slot, int hg) {
     const int tid = threadIdx.x;
     const int64_t n_heads = (int64_t)a.n_slots * a.group;
-    const int unit = slot * a.n_hgroups + hg;
-    __threadfence_system();  // this thread's partial stores precede the flags
-    __syncthreads();
-    if (tid < a.xw) st_release_sys(a.xflags[tid] + (int64_t)a.xrank * n_heads + unit, a.xepoch);
+    const int64_t head0 = (int64_t)slot * a.group + (int64_t)hg * GC;
+    const unsigned long long* base = a.xparts[a.xrank] + (int64_t)(a.xepoch & 1u) * a.xw * n_heads * (D + 2);
     __shared__ int s_timeout;
     if (tid == 0) s_timeout = 0;
     __syncthreads();
-    if (tid < a.xw) {
-        const unsigned* f = a.xflags[a.xrank] + (int64_t)tid * n_heads + unit;
-        for (uint32_t it = 0; (int)(ld_acquire_sys(f) - a.xepoch) < 0; ++it) {
+    auto wait_word = [&](const unsigned long long* p) -> float {
+        unsigned long long v = ld_relaxed_sys_u64(p);
+        for (uint32_t it = 0; (int)((unsigned)(v >> 32) - a.xepoch) < 0; ++it) {
             if (it >= kXchgSpinLimit) {
                 s_timeout = 1;
-                break;
+                return 0.0f;
             }
-            __nanosleep(100);
+            if (it >= 4096) __nanosleep(256);  // back off only after a few microseconds
+            v = ld_relaxed_sys_u64(p);
         }
-    }
-    __syncthreads();
-    const int64_t head0 = (int64_t)slot * a.group + (int64_t)hg * GC;
-    if (s_timeout) {
-        if (tid == 0) raise_device_error(&g_bc_device_error, BC_DEVERR_TIMEOUT);
-        return;
-    }
-    const float* base = a.xparts[a.xrank] + (int64_t)(a.xepoch & 1u) * a.xw * n_heads * (D + 2);
+        return __uint_as_float((unsigned)v);
+    };
     for (int idx = tid; idx < GC * D; idx += kDecThreads) {
         const int g = idx / D, i = idx % D;
         const int64_t h = head0 + g;
+        float mj[8], lj[8], oj[8];
         float M = -INFINITY;
-        for (int j = 0; j < a.xw; ++j) {
-            const float* r = base + ((int64_t)j * n_heads + h) * (D + 2);
-            if (__ldcg(r + 1) > 0.0f) M = fmaxf(M, __ldcg(r));
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            if (j >= a.xw) break;
+            const unsigned long long* r = base + ((int64_t)j * n_heads + h) * (D + 2);
+            mj[j] = wait_word(r);
+            lj[j] = wait_word(r + 1);
+            oj[j] = wait_word(r + 2 + i);
+            if (lj[j] > 0.0f) M = fmaxf(M, mj[j]);
         }
         float L = 0.0f, O = 0.0f;
-        for (int j = 0; j < a.xw; ++j) {
-            const float* r = base + ((int64_t)j * n_heads + h) * (D + 2);
-            const float l = __ldcg(r + 1);
-            if (l > 0.0f) {
-                const float f = __expf(__ldcg(r) - M);
-                L += l * f;
-                O += __ldcg(r + 2 + i) * f;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            if (j >= a.xw) break;
+            if (lj[j] > 0.0f) {
+                const float f = __expf(mj[j] - M);
+                L += lj[j] * f;
+                O += oj[j] * f;
             }
         }
         if (a.out) a.out[h * D + i] = __float2half((L > 0.0f) ? O * (1.0f / L) : 0.0f);
     }
+    __syncthreads();
+    if (tid == 0 && s_timeout) raise_device_error(&g_bc_device_error, BC_DEVERR_TIMEOUT);
 }
 
 // ---------------------------------------------------------------------------
@@ -1537,9 +1546,8 @@ int bc_decode_attention(const void* q, bc_kv_planes K, bc_kv_planes V, void* out
 
 size_t bc_xchg_bytes(int n_heads, int head_dim, int world) {
     if (n_heads <= 0 || world <= 0 || world > 8 || !bc_valid_head_dim(head_dim)) return 0;
-    const size_t parts = (size_t)2 * world * n_heads * (head_dim + 2) * sizeof(float);
-    const size_t flags = (size_t)world * n_heads * sizeof(unsigned);
-    return ((parts + 255) & ~(size_t)255) + ((flags + 255) & ~(size_t)255);
+    const size_t words = (size_t)2 * world * n_heads * (head_dim + 2) * sizeof(unsigned long long);
+    return (words + 255) & ~(size_t)255;
 }
 
 int bc_xchg_alloc(size_t bytes, void** buf) {
@@ -1590,13 +1598,10 @@ int bc_decode_attention_xchg(const void* q, bc_kv_planes K, bc_kv_planes V, void
     const int rc = check_decode_args(q, K, V, out, nullptr, n_slots, group, seq_len, kv_stride, head_dim, mode);
     if (rc != BC_OK || n_slots == 0) return rc;
     if (!out || x.world < 1 || x.world > 8 || x.rank < 0 || x.rank >= x.world || x.epoch == 0) return BC_ERR_ARG;
-    const int64_t n_heads = (int64_t)n_slots * group;
-    const size_t parts = (size_t)2 * x.world * n_heads * (head_dim + 2) * sizeof(float);
     DecodeArgs a = decode_args(q, K, V, out, nullptr, n_slots, group, seq_len, kv_stride, head_dim);
     for (int j = 0; j < x.world; ++j) {
         if (!x.bufs[j] || !bc_aligned(x.bufs[j], 256)) return BC_ERR_ARG;
-        a.xparts[j] = reinterpret_cast<float*>(x.bufs[j]);
-        a.xflags[j] = reinterpret_cast<unsigned*>(reinterpret_cast<uint8_t*>(x.bufs[j]) + ((parts + 255) & ~(size_t)255));
+        a.xparts[j] = reinterpret_cast<unsigned long long*>(x.bufs[j]);
     }
     a.xw = x.world;
     a.xrank = x.rank;

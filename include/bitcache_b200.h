@@ -245,11 +245,11 @@ int bc_decode_attention_adaptive(const void* q, bc_kv_planes K, bc_kv_planes V, 
  * Each rank holds a contiguous slice of every slot's positions.  Instead of
  * an NCCL all-gather of the (m, l, o) triples followed by bc_lse_merge, the
  * last CTA of every (slot, head group) stores its triple directly into every
- * rank's exchange buffer over NVLink (plain peer stores), raises a flag there
- * (st.release.sys), waits for the flags of all ranks in its own buffer (a
- * bounded spin: BC_DEVERR_TIMEOUT after about a second) and merges the world
- * triples itself, so one launch per rank yields the full output on every
- * rank.  Setup (allocates, outside the decode loop): bc_xchg_alloc on every
+ * rank's exchange buffer over NVLink (plain peer stores of 64-bit words that
+ * carry the value and the call's epoch, so no fence or flag is needed), waits
+ * until every word it needs in its own buffer carries the epoch (a bounded
+ * spin: BC_DEVERR_TIMEOUT after about a second) and merges the world triples
+ * itself, so one launch per rank yields the full output on every rank.  Setup (allocates, outside the decode loop): bc_xchg_alloc on every
  * rank, share the 64-byte bc_ipc_handle of each buffer, bc_ipc_open the
  * peers' handles.  Every rank calls bc_decode_attention_xchg with the same
  * n_slots, group, head_dim and epoch (1, 2, 3, ...: one per call); ranks run
