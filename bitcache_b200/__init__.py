@@ -98,22 +98,34 @@ class BitCache:
         out = _planes.decode_attention(Q.view(-1, self.head_dim), self._K, self._V, self._filled, mode)
         return out.view(self.batch, self.n_heads, self.head_dim)
 
-    def step(self, Q: Tensor, K: Tensor, V: Tensor) -> Tensor:
+    def step(self, Q: Tensor, K: Tensor, V: Tensor, out: Tensor | None = None) -> Tensor:
         """One decode step in one launch: ``append(K, V)`` followed by ``attend(Q)``
         (reference bitcache/__init__.py:95-148), with identical results and cache
         contents.  The new token is encoded inside the attention kernel and
-        attended from the encoder's output."""
-        self._validate_kv(K, V)
-        assert Q.shape == (self.batch, self.n_heads, self.head_dim), "Q shape mismatch"
-        assert Q.dtype == torch.float16 and Q.is_cuda and Q.is_contiguous(), "Q must be contiguous fp16 CUDA"
+        attended from the encoder's output.
+
+        Q, K, V (and ``out``) may also be pinned host tensors: the kernel then
+        reads the step's inputs and writes the output over the host link
+        itself, so a host-driven decode loop needs no separate copies."""
+        pinned = not Q.is_cuda
+        for t, name, shape in ((K, "K", (self.batch, self.n_kv_heads, self.head_dim)),
+                               (V, "V", (self.batch, self.n_kv_heads, self.head_dim)),
+                               (Q, "Q", (self.batch, self.n_heads, self.head_dim))):
+            assert t.shape == torch.Size(shape), f"{name} shape {tuple(t.shape)} != {shape}"
+            assert t.dtype == torch.float16, f"{name} must be float16"
+            assert t.is_contiguous(), f"{name} must be contiguous"
+            assert (t.is_pinned() if pinned else t.is_cuda), f"{name}: all of Q, K, V on CUDA, or all pinned host"
+        if out is not None:
+            assert out.shape == Q.shape and out.dtype == torch.float16 and out.is_contiguous(), "out mismatch"
         pos = self._write_pos
         filled = min(self._filled + 1, self.max_seq)
         mode = _planes.MODE_COMPENSATED if self.compensated else _planes.MODE_BINARY
-        out = _planes.decode_step(Q.view(-1, self.head_dim), K.view(-1, self.head_dim), V.view(-1, self.head_dim),
-                                  self._K, self._V, filled, pos, mode, self._res_mode)
+        res = _planes.decode_step(Q.view(-1, self.head_dim), K.view(-1, self.head_dim), V.view(-1, self.head_dim),
+                                  self._K, self._V, filled, pos, mode, self._res_mode,
+                                  out=None if out is None else out.view(-1, self.head_dim))
         self._write_pos = (pos + 1) % self.max_seq
         self._filled = filled
-        return out.view(self.batch, self.n_heads, self.head_dim)
+        return res.view(self.batch, self.n_heads, self.head_dim)
 
     def keep_residuals(self, fraction: float = 0.25) -> None:
         """Per-vector adaptive precision: keep the INT4 residual only for the given fraction

@@ -118,6 +118,17 @@ def _check_half(x: torch.Tensor, name: str) -> None:
         raise RuntimeError(f"{name} must be float16")
 
 
+def _check_half_dev_or_pinned(x: torch.Tensor, name: str) -> None:
+    """fp16, contiguous, and either on the GPU or in pinned (page-locked) host memory,
+    which kernels read and write directly through unified addressing."""
+    if not (x.is_cuda or x.is_pinned()):
+        raise RuntimeError(f"{name} must be a CUDA tensor or a pinned host tensor")
+    if not x.is_contiguous():
+        raise RuntimeError(f"{name} must be contiguous")
+    if x.dtype != torch.float16:
+        raise RuntimeError(f"{name} must be float16")
+
+
 def encode_planes(src: torch.Tensor, out: Planes, residual_mode: int = RES_FP16_SCALE) -> None:
     """Prefill: encode src fp16 [n_slots, seq_len, head_dim] into rows [slot, 0:seq_len] of out."""
     _check_half(src, "src")
@@ -173,11 +184,13 @@ def decode_step(q: torch.Tensor, k: torch.Tensor | None, v: torch.Tensor | None,
                 want_out: bool = True) -> torch.Tensor | None:
     """Fused decode step: append k, v ([n_slots, head_dim]) at append_pos with residual_mode
     arithmetic, then attend q over keys [0, seq_len), in one launch (bc_decode_step).
-    append_pos = -1 (k, v None) attends only.  Results equal append_kv + decode_attention."""
-    _check_half(q, "Q")
+    append_pos = -1 (k, v None) attends only.  Results equal append_kv + decode_attention.
+    q, k, v and out may be pinned host tensors: the kernel then reads the step's inputs
+    and writes its output over the host link itself, with no separate copies."""
+    _check_half_dev_or_pinned(q, "Q")
     if append_pos >= 0:
-        _check_half(k, "K")
-        _check_half(v, "V")
+        _check_half_dev_or_pinned(k, "K")
+        _check_half_dev_or_pinned(v, "V")
     d = q.shape[-1]
     n_heads = q.numel() // d
     n_slots = K.n_slots
@@ -187,11 +200,15 @@ def decode_step(q: torch.Tensor, k: torch.Tensor | None, v: torch.Tensor | None,
     if append_pos >= 0 and (k.numel() != n_slots * d or v.numel() != n_slots * d):
         raise RuntimeError("k and v must hold one head_dim row per KV slot")
     if want_out and out is None:
-        out = torch.empty((n_heads, d), dtype=torch.float16, device=q.device)
+        out = (torch.empty((n_heads, d), dtype=torch.float16, device=q.device) if q.is_cuda
+               else torch.empty((n_heads, d), dtype=torch.float16).pin_memory())
+    if want_out:
+        _check_half_dev_or_pinned(out, "out")
+    dev = K.sign.device
     lib = _lib.load()
-    st = _stream(q)
+    st = _lib.stream_of(dev)
     wsb = lib.bc_decode_workspace_bytes(n_slots, group, seq_len, d)
-    ws = _lib.workspace(q.device, st, wsb, ("decode", n_slots, group))
+    ws = _lib.workspace(dev, st, wsb, ("decode", n_slots, group))
     _lib.check(lib.bc_decode_step(q.data_ptr(), _lib.ptr(k) if append_pos >= 0 else None,
                                   _lib.ptr(v) if append_pos >= 0 else None, K.c(), V.c(),
                                   _lib.ptr(out) if want_out else None, _lib.ptr(partial), n_slots, group, seq_len,

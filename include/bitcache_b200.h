@@ -174,6 +174,9 @@ int bc_decode_attention_entropy(const void* q, bc_kv_planes K, bc_kv_planes V, v
  * planes receive the same bytes, and the appended row is attended from the encoder's
  * output, not re-read.  append_pos = -1 appends nothing (plain decode); otherwise
  * 0 <= append_pos < seq_len, and compensated attention needs append_res != BC_RES_NONE.
+ * q, new_k, new_v and out may point to pinned (page-locked) host memory: with unified
+ * addressing the kernel reads the step's inputs and writes its output over the host link
+ * itself, so a host-driven decode loop needs no separate copies.
  * Workspace as bc_decode_workspace_bytes. */
 int bc_decode_step(const void* q, const void* new_k, const void* new_v, bc_kv_planes K, bc_kv_planes V, void* out,
                    float* partial, int n_slots, int group, int seq_len, int64_t kv_stride, int head_dim, int mode,

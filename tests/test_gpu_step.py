@@ -178,3 +178,31 @@ def test_bitcache_step_matches_append_attend_and_oracle(cuda):
           "nib": vnb.reshape(n, max_seq, -1), "rscale": vrs.reshape(n, max_seq)}
     want = O.attention(qs[-1].reshape(-1, d).numpy(), Kp, Vp, H // Hkv, max_seq, max_seq, True)
     close(got.view(-1, d), want.view(np.float16).astype(np.float32), "BitCache.step vs oracle")
+
+
+def test_bitcache_step_with_pinned_host_operands(cuda):
+    """Q, K, V and the output in pinned host memory (read and written by the
+    kernel directly) give the same result and cache as device tensors."""
+    B, H, Hkv, d, max_seq = 2, 8, 4, 128, 300
+    g = torch.Generator().manual_seed(23)
+    a = BitCache(B, H, d, max_seq=max_seq, n_kv_heads=Hkv)
+    b = BitCache(B, H, d, max_seq=max_seq, n_kv_heads=Hkv)
+    pre_k = (torch.randn(B, Hkv, 200, d, generator=g) * 0.5).half().to(cuda)
+    pre_v = (torch.randn(B, Hkv, 200, d, generator=g) * 0.5).half().to(cuda)
+    a.prefill(pre_k, pre_v)
+    b.prefill(pre_k, pre_v)
+    qh = torch.empty(B, H, d, dtype=torch.float16).pin_memory()
+    kh = torch.empty(B, Hkv, d, dtype=torch.float16).pin_memory()
+    vh = torch.empty(B, Hkv, d, dtype=torch.float16).pin_memory()
+    oh = torch.empty(B, H, d, dtype=torch.float16).pin_memory()
+    for t in range(5):
+        qh.copy_((torch.randn(B, H, d, generator=g) * 0.5).half())
+        kh.copy_((torch.randn(B, Hkv, d, generator=g) * 0.5).half())
+        vh.copy_((torch.randn(B, Hkv, d, generator=g) * 0.5).half())
+        got = a.step(qh, kh, vh, out=oh)
+        want = b.step(qh.to(cuda), kh.to(cuda), vh.to(cuda))
+        torch.cuda.synchronize()
+        assert got.data_ptr() == oh.data_ptr() and not got.is_cuda
+        assert torch.equal(got, want.cpu())
+    for X, Y in zip(a.planes, b.planes):
+        planes_equal(X, Y, 205, True)
