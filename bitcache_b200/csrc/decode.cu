@@ -47,16 +47,22 @@ __device__ unsigned int g_bc_device_error = 0;
 #ifndef BC_DEC_STAGES
 #define BC_DEC_STAGES 2        // ring stages at head_dim <= 128 (2: 4 CTAs, 16 warps per SM)
 #endif
-#ifndef BC_DEC_QPACK_SMEM
-#define BC_DEC_QPACK_SMEM 1    // 1: the score phase reads the query packs from shared memory
-#endif
 #ifndef BC_DEC_WAVES
 #define BC_DEC_WAVES 1         // resident waves of CTAs the split plan aims for
 #endif
 
-constexpr int kDecThreads = 128;  // 4 warps
+#ifndef BC_DEC_THREADS
+#define BC_DEC_THREADS 128     // threads per CTA (4 warps; each warp owns 32 keys of a tile)
+#endif
+#ifndef BC_DEC_DL1
+#define BC_DEC_DL1 32          // value-phase dims per lane with one head per CTA
+#endif
+#ifndef BC_DEC_MIN_CTAS_C1
+#define BC_DEC_MIN_CTAS_C1 4   // resident CTAs per SM the compensated one-head kernel is held to
+#endif
+constexpr int kDecThreads = BC_DEC_THREADS;
 constexpr int kWarps = kDecThreads / 32;
-constexpr int kTile = 128;        // keys per tile: 32 per warp
+constexpr int kTile = kDecThreads;  // keys per tile: 32 per warp
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 constexpr float kLazy = 8.0f;     // rescale only when the running max grows by > 2^8
@@ -67,7 +73,7 @@ struct DecCfg {
     static constexpr int NWD = D / 32;       // sign words (and 16-byte nibble chunks) per key
     // Value phase: each lane accumulates DL dims of a key, 32 with one head per
     // CTA, 16 with several (so GC heads' accumulators fit the register budget).
-    static constexpr int DL = (GC == 1) ? 32 : 16;
+    static constexpr int DL = (GC == 1) ? BC_DEC_DL1 : 16;
     static constexpr int NP = DL / 2;        // f32x2 accumulator pairs per lane and head part
     static constexpr int QPK = D / DL;       // value-phase lanes per key
     static constexpr int KPW = 32 / QPK;     // value-phase keys in parallel per warp
@@ -94,7 +100,7 @@ struct DecCfg {
     static constexpr int QSIGN_OFF = Q16_OFF + GC * D * 4;      // uint32 [GC][8]
     static constexpr int QCONST_OFF = QSIGN_OFF + GC * 8 * 4;   // [GC][4]: bco, rco, off8, eco
     static constexpr int QPK_OFF = QCONST_OFF + GC * 4 * 4;     // uint32 [GC][D/8][4] query packs
-    static constexpr int FULL_OFF = QPK_OFF + (BC_DEC_QPACK_SMEM ? GC * (D / 8) * 16 : 0);  // mbarriers
+    static constexpr int FULL_OFF = QPK_OFF + GC * (D / 8) * 16;  // mbarriers
     static constexpr int EMPTY_OFF = FULL_OFF + NS * 8;         // mbarriers: all warps done with a stage
     static constexpr int FLAG_OFF = EMPTY_OFF + NS * 8;         // abort flag
     // Fused decode step: the appended K and V rows, staged once per CTA in
@@ -106,7 +112,8 @@ struct DecCfg {
     static constexpr int SMEM_B = NEWRAW_OFF + 4 * D + 128;     // + slack to align the base to 128 B
     // Resident CTAs per SM that shared memory allows at head_dim <= 128 with one
     // head per CTA; the register budget is held to it (0: no bound).
-    static constexpr int MIN_CTAS = (D > 128) ? 0 : (GC == 1 && !COMP) ? 8 : 4;
+    static constexpr int MIN_CTAS =
+        (D > 128) ? 0 : ((GC == 1 && !COMP) ? 8 : (GC == 1 ? BC_DEC_MIN_CTAS_C1 : 4)) * 128 / kDecThreads;
 };
 
 struct DecodeArgs {
@@ -163,11 +170,7 @@ __device__ __forceinline__ int64_t plane_row(const DecodeArgs& a, int slot, int 
 template <int D, int GC>
 struct QState {
     uint32_t sign[GC][D / 32];
-#if BC_DEC_QPACK_SMEM
     const uint4* pk;  // shared memory, [GC][D/8]
-#else
-    uint32_t pk[GC][D / 8][4];
-#endif
     float bco[GC], rco[GC];
     int off8[GC];
     float eco[GC];  // entropy variant: the query's tree-order mean |q| (adaptive_precision.cu:46-59)
@@ -290,7 +293,6 @@ __device__ __forceinline__ void prepare_query(const DecodeArgs& a, int slot, int
         qs.rco[g] = qc[g * 4 + 1];
         qs.off8[g] = reinterpret_cast<const int*>(qc)[g * 4 + 2];
         qs.eco[g] = qc[g * 4 + 3];
-#if BC_DEC_QPACK_SMEM
         qs.pk = reinterpret_cast<const uint4*>(smem + Cfg::QPK_OFF);
         if (COMP) {
             uint4* dst = reinterpret_cast<uint4*>(smem + Cfg::QPK_OFF);
@@ -307,30 +309,8 @@ __device__ __forceinline__ void prepare_query(const DecodeArgs& a, int slot, int
                 dst[g * (D / 8) + w] = make_uint4(eh, el, oh, ol);
             }
         }
-#else
-        if (COMP) {
-#pragma unroll
-            for (int w = 0; w < D / 8; ++w) {
-                uint32_t eh = 0, el = 0, oh = 0, ol = 0;
-#pragma unroll
-                for (int b = 0; b < 4; ++b) {
-                    const int ve = q16[g * D + 8 * w + 2 * b], vo = q16[g * D + 8 * w + 2 * b + 1];
-                    eh |= ((uint32_t)(ve >> 8) & 0xFFu) << (8 * b);
-                    el |= ((uint32_t)ve & 0xFFu) << (8 * b);
-                    oh |= ((uint32_t)(vo >> 8) & 0xFFu) << (8 * b);
-                    ol |= ((uint32_t)vo & 0xFFu) << (8 * b);
-                }
-                qs.pk[g][w][0] = eh;
-                qs.pk[g][w][1] = el;
-                qs.pk[g][w][2] = oh;
-                qs.pk[g][w][3] = ol;
-            }
-        }
-#endif
     }
-#if BC_DEC_QPACK_SMEM
     __syncthreads();
-#endif
 }
 
 template <int GC, int NP>
@@ -405,12 +385,8 @@ __device__ __forceinline__ void consume_warp_tile(const QState<D, GC>& qs, SoftS
                 const uint32_t uo16 = wds[w] & 0xF0F0F0F0u;  // odd elements, 16u
 #pragma unroll
                 for (int g = 0; g < GC; ++g) {
-#if BC_DEC_QPACK_SMEM
                     const uint4 pv = qs.pk[g * (D / 8) + 4 * c + w];
                     const uint32_t pk[4] = {pv.x, pv.y, pv.z, pv.w};
-#else
-                    const uint32_t* pk = qs.pk[g][4 * c + w];
-#endif
                     eh[g] = dp4a_us(ue, pk[0], eh[g]);
                     el[g] = dp4a_uu(ue, pk[1], el[g]);
                     oh[g] = dp4a_us(uo16, pk[2], oh[g]);
@@ -1262,10 +1238,6 @@ struct Plan {
     int n_splits, keys_per_split, n_hgroups, gc, tile;
 };
 
-int tile_keys(int d) {
-    (void)d;
-    return kTile;
-}
 
 // Query heads handled per CTA: up to two (compensated) or four (binary) of a
 // slot's group, so one read and one bit extraction of every KV key serve
@@ -1283,7 +1255,7 @@ Plan make_plan(int n_slots, int group, int seq_len, int d, bool comp, int capaci
     Plan p;
     p.gc = heads_per_cta(group, d, comp);
     p.n_hgroups = group / p.gc;
-    p.tile = tile_keys(d);
+    p.tile = kTile;
     const int n_tiles = max(1, (seq_len + p.tile - 1) / p.tile);
     const int64_t units = (int64_t)n_slots * p.n_hgroups;
     int splits = 1;
@@ -1685,7 +1657,7 @@ int bc_decode_step_paged(const void* q, const void* new_k, const void* new_v, bc
                          void* out, float* partial, bc_page_table pt, int n_slots, int group, int seq_len,
                          int head_dim, int mode, int append_pos, int append_res, void* workspace,
                          size_t workspace_bytes, void* stream) {
-    if (!pt.pages || pt.page_size <= 0 || pt.page_size % 128 != 0 || pt.n_pages <= 0 || pt.max_pages <= 0)
+    if (!pt.pages || pt.page_size <= 0 || pt.page_size % kTile != 0 || pt.n_pages <= 0 || pt.max_pages <= 0)
         return BC_ERR_ARG;
     if ((int64_t)pt.max_pages * pt.page_size < seq_len) return BC_ERR_ARG;
     if (!bc_aligned(pt.pages, 4)) return BC_ERR_ALIGN;
