@@ -966,6 +966,10 @@ __global__ void __launch_bounds__(kDecThreads, DecCfg<D, GC, COMP>::MIN_CTAS)
     const int n_keys = max(0, s_end - s_begin);
     const int n_tiles = (n_keys + T - 1) / T;
 
+    // Launched with programmatic stream serialisation: everything above ran
+    // while the previous kernel in the stream may still be finishing; wait
+    // for it (and its memory) before the first global access.
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     // Small inputs first: their copies start before the ring's bulk copies.
     const bool staged = prefetch_query<D, GC, Cfg>(a, slot, hg, smem);
     // fused step: does this CTA's key range hold the append position?
@@ -1096,6 +1100,9 @@ __global__ void __launch_bounds__(kDecThreads, DecCfg<D, GC, COMP>::MIN_CTAS)
         if (lane == 0) mbar_arrive(&empty[stage]);
     }
     __syncthreads();
+    // This CTA no longer needs the ring: let the next kernel in the stream be
+    // scheduled as CTAs exit (it waits for this grid before touching memory).
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     if (*abort_flag) {
         // A copy never landed (or a stage was never released): report, drain
         // what is still in flight (bounded), and leave.
@@ -1302,14 +1309,30 @@ int launch_decode(const DecodeArgs& a, int var, cudaStream_t st) {
             return BC_OK;
         }
     }
+    // Programmatic dependent launch: the CTAs of this kernel may be scheduled
+    // while the previous kernel of the stream finishes (each waits in
+    // griddepcontrol.wait before its first global access), which hides the
+    // launch and ramp-up behind the previous kernel's tail.
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kDecThreads);
+    cfg.dynamicSmemBytes = Cfg::SMEM_B;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e = cudaSuccess;
     if (var == kVarStep)
-        k_decode_planes<D, GC, COMP, 1><<<grid, kDecThreads, Cfg::SMEM_B, st>>>(a);
+        e = cudaLaunchKernelEx(&cfg, k_decode_planes<D, GC, COMP, 1>, a);
     else if (var == kVarEntropy)
-        k_decode_planes<D, GC, COMP, 2><<<grid, kDecThreads, Cfg::SMEM_B, st>>>(a);
+        e = cudaLaunchKernelEx(&cfg, k_decode_planes<D, GC, COMP, 2>, a);
     else if (var == kVarAdaptive) {
-        if constexpr (COMP) k_decode_planes<D, GC, COMP, 3><<<grid, kDecThreads, Cfg::SMEM_B, st>>>(a);
+        if constexpr (COMP) e = cudaLaunchKernelEx(&cfg, k_decode_planes<D, GC, COMP, 3>, a);
     } else
-        k_decode_planes<D, GC, COMP, 0><<<grid, kDecThreads, Cfg::SMEM_B, st>>>(a);
+        e = cudaLaunchKernelEx(&cfg, k_decode_planes<D, GC, COMP, 0>, a);
+    if (e != cudaSuccess) return BC_ERR_CUDA_BASE + (int)e;
     BC_LAUNCH_CHECK();
     return BC_OK;
 }
