@@ -873,33 +873,34 @@ struct StagedRowSink {
 };
 
 template <int D, typename Cfg>
-__device__ __noinline__ void encode_append_row(const DecodeArgs& a, int slot, bool store, uint8_t* smem,
-                                               const __half* src) {
+// Arguments by value: a reference to the kernel's parameter block would
+// make the compiler copy that block to the stack of every thread.
+__device__ __noinline__ void encode_append_row(const __half* src, bc_kv_planes P, int64_t row, bool store,
+                                               int append_res, int head_dim, uint8_t* smem) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;  // warp 0: K, warp 1: V
     uint8_t* srow = smem + Cfg::NEW_OFF + warp * Cfg::NEWROW_B;
-    if (a.append_res == BC_RES_NONE) {
+    if (append_res == BC_RES_NONE) {
         // binary append: the staged residual is code 0 (offset-binary 0x8) with scale 0
         if (lane < D / 8) reinterpret_cast<uint32_t*>(srow + Cfg::NEWSIGN_B)[lane] = 0x88888888u;
         if (lane == 0) reinterpret_cast<uint16_t*>(srow + Cfg::NEWSIGN_B + D / 2)[1] = 0;
     }
     float x[D / 32];
     load_vec<D / 32>(src, lane, x);
-    const int64_t row = plane_row(a, slot, a.append_pos);
     if (row < 0) {
         if (store && lane == 0) raise_device_error(&g_bc_device_error, BC_DEVERR_PAGE);
         store = false;  // attend the staged row, store nothing
     }
-    StagedRowSink<D / 32> sink{{warp == 0 ? a.K : a.V, row}, srow, Cfg::NEWSIGN_B, store};
-    switch (a.append_res) {
-        case BC_RES_NONE: encode_row<D / 32, BC_RES_NONE>(x, lane, a.head_dim, sink); break;
-        case BC_RES_FP16_SCALE: encode_row<D / 32, BC_RES_FP16_SCALE>(x, lane, a.head_dim, sink); break;
-        default: encode_row<D / 32, BC_RES_FP32_SCALE>(x, lane, a.head_dim, sink); break;
+    StagedRowSink<D / 32> sink{{P, row}, srow, Cfg::NEWSIGN_B, store};
+    switch (append_res) {
+        case BC_RES_NONE: encode_row<D / 32, BC_RES_NONE>(x, lane, head_dim, sink); break;
+        case BC_RES_FP16_SCALE: encode_row<D / 32, BC_RES_FP16_SCALE>(x, lane, head_dim, sink); break;
+        default: encode_row<D / 32, BC_RES_FP32_SCALE>(x, lane, head_dim, sink); break;
     }
 }
 
 // Overwrite key kk of a landed stage with the staged rows (one warp).
 template <int D, bool COMP, typename Cfg>
-__device__ __noinline__ void patch_stage_row(uint8_t* sb, int kk, const uint8_t* smem) {
+__device__ __forceinline__ void patch_stage_row(uint8_t* sb, int kk, const uint8_t* smem) {
     constexpr int NWD = D / 32;
     const int lane = threadIdx.x & 31;
 #pragma unroll
@@ -1056,7 +1057,9 @@ __global__ void __launch_bounds__(kDecThreads, DecCfg<D, GC, COMP>::MIN_CTAS)
         if (appends) {
             asm volatile("cp.async.wait_all;" ::: "memory");
             __syncthreads();
-            if (warp < 2) encode_append_row<D, Cfg>(a, slot, hg == 0, smem, new_src[warp]);
+            if (warp < 2)
+                encode_append_row<D, Cfg>(new_src[warp], warp == 0 ? a.K : a.V, plane_row(a, slot, a.append_pos),
+                                          hg == 0, a.append_res, a.head_dim, smem);
             __syncthreads();
             const int rel = a.append_pos - s_begin;
             if ((rel % T) / 32 == warp) {
