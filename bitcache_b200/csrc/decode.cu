@@ -121,7 +121,7 @@ struct DecodeArgs {
     bc_kv_planes K, V;  // planes, or record bases in .sign (bin) / .nib (res) for the record kernel
     __half* out;        // [n_slots * group][d] or null
     float* partial;     // [n_slots * group][d + 2] or null
-    float* ws_part;     // [n_slots * group][n_splits][d + 2]
+    float* ws_part;     // [n_slots * group][n_splits][d + 4]: m, l, 2 pad, o[d] (o 16-byte aligned)
     unsigned* ws_cnt;   // [n_slots * n_hgroups]
     int n_slots, group, seq_len, n_splits, keys_per_split, n_hgroups;
     int64_t kv_stride;
@@ -750,12 +750,12 @@ __device__ __forceinline__ void finish_cta(const DecodeArgs& a, int slot, int hg
         if (single) {
             emit_final<D>(a, h, i, M, L, O);
         } else {
-            float* p = a.ws_part + (h * a.n_splits + split) * (D + 2);
+            float* p = a.ws_part + (h * a.n_splits + split) * (D + 4);
             if (i == 0) {
                 p[0] = M;
                 p[1] = L;
             }
-            p[2 + i] = O;
+            p[4 + i] = O;
         }
     }
     if (single) {
@@ -772,41 +772,67 @@ __device__ __forceinline__ void finish_cta(const DecodeArgs& a, int slot, int hg
     __syncthreads();
     if (!s_last) return;
     __threadfence();
-    // Splits are combined in chunks of kComb: the chunk's loads are all in
-    // flight together (one L2 round trip per chunk instead of two per split),
-    // then merged into a running (M, L, O).  With n_splits <= kComb this is
-    // the plain max-then-sum in split order.
-    constexpr int kComb = 16;
-    for (int idx = tid; idx < GC * D; idx += kDecThreads) {
-        const int g = idx / D, i = idx % D;
+    // Split combine.  A task is (head, 4 dims); the threads left over split
+    // the splits into SG interleaved groups, so several L2 round trips run in
+    // parallel.  Each thread loads kComb partials at once (m, l, float4 of o),
+    // merges them into a running (M, L, O), and the SG group results are then
+    // merged through shared memory (the ring, free by now).
+    constexpr int kComb = 8;
+    constexpr int TASKS = GC * D / 4;
+    constexpr int SG = (TASKS >= kDecThreads) ? 1 : kDecThreads / TASKS;
+    float* cmb = reinterpret_cast<float*>(smem);  // [SG][TASKS][6]
+    static_assert(SG * TASKS * 6 * 4 <= Cfg::BODY_B, "combine scratch exceeds the ring");
+    for (int t = tid; t < TASKS * SG; t += kDecThreads) {
+        const int task = t % TASKS, sg = t / TASKS;
+        const int g = task / (D / 4), c = task % (D / 4);
         const int64_t h = head0 + g;
-        const float* base = a.ws_part + h * a.n_splits * (D + 2);
-        float M = -INFINITY, L = 0.0f, O = 0.0f;
-        for (int j0 = 0; j0 < a.n_splits; j0 += kComb) {
-            float mj[kComb], lj[kComb], oj[kComb];
+        const float* base = a.ws_part + h * a.n_splits * (D + 4);
+        float M = -INFINITY, L = 0.0f;
+        float4 O = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        for (int j0 = sg * kComb; j0 < a.n_splits; j0 += SG * kComb) {
+            float mj[kComb], lj[kComb];
+            float4 oj[kComb];
 #pragma unroll
             for (int k = 0; k < kComb; ++k) {
                 const bool in = j0 + k < a.n_splits;
-                const float* r = base + (size_t)(j0 + k) * (D + 2);
+                const float* r = base + (size_t)(j0 + k) * (D + 4);
                 mj[k] = in ? __ldcg(r) : -INFINITY;
                 lj[k] = in ? __ldcg(r + 1) : 0.0f;
-                oj[k] = in ? __ldcg(r + 2 + i) : 0.0f;
+                oj[k] = in ? __ldcg(reinterpret_cast<const float4*>(r + 4) + c) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
             }
             float Mn = M;
 #pragma unroll
             for (int k = 0; k < kComb; ++k) Mn = fmaxf(Mn, mj[k]);
             const float fo = (M == -INFINITY) ? 0.0f : fast_exp2(M - Mn);
             L *= fo;
-            O *= fo;
+            O.x *= fo; O.y *= fo; O.z *= fo; O.w *= fo;
 #pragma unroll
             for (int k = 0; k < kComb; ++k) {
                 const float f = (mj[k] == -INFINITY) ? 0.0f : fast_exp2(mj[k] - Mn);
                 L += lj[k] * f;
-                O += oj[k] * f;
+                O.x += oj[k].x * f; O.y += oj[k].y * f; O.z += oj[k].z * f; O.w += oj[k].w * f;
             }
             M = Mn;
         }
-        emit_final<D>(a, h, i, M, L, O);
+        float* e = cmb + (sg * TASKS + task) * 6;
+        e[0] = M; e[1] = L; e[2] = O.x; e[3] = O.y; e[4] = O.z; e[5] = O.w;
+    }
+    __syncthreads();
+    for (int idx = tid; idx < GC * D; idx += kDecThreads) {
+        const int task = idx >> 2, k = idx & 3;
+        const int64_t h = head0 + task / (D / 4);
+        float M = -INFINITY;
+#pragma unroll
+        for (int sg = 0; sg < SG; ++sg) M = fmaxf(M, cmb[(sg * TASKS + task) * 6]);
+        float L = 0.0f, O = 0.0f;
+#pragma unroll
+        for (int sg = 0; sg < SG; ++sg) {
+            const float* e = cmb + (sg * TASKS + task) * 6;
+            const float f = (e[0] == -INFINITY) ? 0.0f : fast_exp2(e[0] - M);
+            L += e[1] * f;
+            O += e[2 + k] * f;
+        }
+        emit_final<D>(a, h, idx % D, M, L, O);
     }
     if constexpr (ENT) {
         if (tid < GC) {
@@ -1280,7 +1306,7 @@ Plan make_plan(int n_slots, int group, int seq_len, int d, bool comp, int capaci
 // Workspace: ticket counters, then split partials (m, l, o[d]), then the
 // entropy variant's split partials (m, z, w).
 size_t ws_bytes_for(int n_slots, int group, int n_splits, int d, int n_hgroups) {
-    const size_t part = (size_t)n_slots * group * n_splits * (d + 2) * sizeof(float);
+    const size_t part = (size_t)n_slots * group * n_splits * (d + 4) * sizeof(float);
     const size_t ent = (size_t)n_slots * group * n_splits * 3 * sizeof(float);
     const size_t cnt = (size_t)n_slots * n_hgroups * sizeof(unsigned);
     return ((part + 255) & ~(size_t)255) + ((cnt + 255) & ~(size_t)255) + ((ent + 255) & ~(size_t)255);
@@ -1423,7 +1449,7 @@ int run_decode_t(DecodeArgs a, int var, void* ws, size_t ws_bytes, cudaStream_t 
         // zero (every completed call resets its own); partials follow and are
         // always written before they are read.
         const size_t cnt = (size_t)a.n_slots * p.n_hgroups * sizeof(unsigned);
-        const size_t part = (size_t)a.n_slots * a.group * p.n_splits * (D + 2) * sizeof(float);
+        const size_t part = (size_t)a.n_slots * a.group * p.n_splits * (D + 4) * sizeof(float);
         uint8_t* base = reinterpret_cast<uint8_t*>(ws);
         a.ws_cnt = reinterpret_cast<unsigned*>(base);
         a.ws_part = reinterpret_cast<float*>(base + ((cnt + 255) & ~(size_t)255));
