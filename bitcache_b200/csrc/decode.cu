@@ -34,6 +34,7 @@
 // (pattern * 2^-149) of packed fma.rn.f32x2 with one coefficient per key;
 // each accumulator carries the fixed power-of-two scale of its bit position,
 // removed once per CTA together with the constant parts sum_s (a_s + 8 c_s).
+#include <type_traits>
 #include <cstring>
 #include <mutex>
 
@@ -59,6 +60,9 @@ __device__ unsigned int g_bc_device_error = 0;
 #endif
 #ifndef BC_DEC_MIN_CTAS_C1
 #define BC_DEC_MIN_CTAS_C1 4   // resident CTAs per SM the compensated one-head kernel is held to
+#endif
+#ifndef BC_DEC_MMA
+#define BC_DEC_MMA 1           // compensated head_dim-128 value phase on the tensor cores (u8 mma.sync)
 #endif
 constexpr int kDecThreads = BC_DEC_THREADS;
 constexpr int kWarps = kDecThreads / 32;
@@ -95,6 +99,10 @@ struct DecCfg {
     static constexpr int RING_B = NS * STAGE_B;
     static constexpr int MERGE_B = kWarps * GC * (D + 2) * 4;  // reuses the ring after the main loop
     static constexpr int BODY_B = RING_B > MERGE_B ? RING_B : MERGE_B;
+    // tensor-core value phase: the warps' accumulators are dumped after the
+    // merge records ([warp][lane][65] ints) for the final read-out
+    static constexpr int DUMP_OFF = (MERGE_B + 127) & ~127;
+    static constexpr int DUMP_B = kWarps * 32 * 65 * 4;
     static constexpr int QF_OFF = BODY_B;                       // float q[GC][D]
     static constexpr int Q16_OFF = QF_OFF + GC * D * 4;         // int Q16[GC][D]
     static constexpr int QSIGN_OFF = Q16_OFF + GC * D * 4;      // uint32 [GC][8]
@@ -109,7 +117,14 @@ struct DecCfg {
     static constexpr int NEWROW_B = NEWSIGN_B + D / 2 + 16;
     static constexpr int NEW_OFF = FLAG_OFF + 16;               // [2][NEWROW_B]: K row, V row
     static constexpr int NEWRAW_OFF = NEW_OFF + 2 * NEWROW_B;   // fp16 [2][D]: the new K, V rows as given
-    static constexpr int SMEM_B = NEWRAW_OFF + 4 * D + 128;     // + slack to align the base to 128 B
+    // Tensor-core value phase (compensated, head_dim 128, one or two heads per
+    // CTA): per warp, the fixed-point key coefficients as bytes, [part][row][48].
+    static constexpr bool MMA = BC_DEC_MMA && COMP && D == 128 && GC <= 2;
+    static constexpr int WB_ROW = 48;                           // padded: the fragment loads hit distinct banks
+    static constexpr int WB_WARP = 2 * 8 * WB_ROW;
+    static constexpr int WB_OFF = NEWRAW_OFF + 4 * D;
+    static constexpr int SMEM_B = WB_OFF + (MMA ? kWarps * WB_WARP : 0) + 128;  // + slack to align the base to 128 B
+    static_assert(!MMA || DUMP_OFF + DUMP_B <= BODY_B, "accumulator dump exceeds the ring");
     // Resident CTAs per SM that shared memory allows at head_dim <= 128 with one
     // head per CTA; the register budget is held to it (0: no bound).
     static constexpr int MIN_CTAS =
@@ -331,6 +346,45 @@ __device__ __forceinline__ void init_soft(SoftState<GC, NP>& st) {
     }
 }
 
+// State of the tensor-core value phase.  The value sums live in integer MMA
+// accumulators: acc[part][t] is the m16n8 tile t of part 0 (sign) or 1
+// (residual), rows = dims, columns = (head, byte of the key coefficient).
+// A key's coefficient (2 w bscale for the sign bits, w rscale / 7 for the
+// codes, w = 2^(s - m)) enters as a 32-bit fixed-point number in units of
+// 2^U[g] (absolute, log2), split into four byte columns, so the softmax's
+// lazy max m never touches the accumulators; U moves only when a coefficient
+// would reach 2^31 units, and the accumulators are then shifted down exactly.
+constexpr int kUUnset = -0x40000000;
+
+template <int GC>
+struct MmaState {
+    float m[GC];
+    float l[GC], t[GC];
+    int acc[2][8][4];
+    int U[GC];
+    float em[GC], ez[GC], ew[GC];
+};
+
+template <int GC>
+__device__ __forceinline__ void init_soft(MmaState<GC>& st) {
+#pragma unroll
+    for (int g = 0; g < GC; ++g) {
+        st.m[g] = -INFINITY;
+        st.l[g] = 0.0f;
+        st.t[g] = 0.0f;
+        st.U[g] = kUUnset;
+        st.em[g] = -INFINITY;
+        st.ez[g] = 0.0f;
+        st.ew[g] = 0.0f;
+    }
+#pragma unroll
+    for (int p = 0; p < 2; ++p)
+#pragma unroll
+        for (int t = 0; t < 8; ++t)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) st.acc[p][t][i] = 0;
+}
+
 // ---------------------------------------------------------------------------
 // One warp consumes its 32 keys of a tile held in shared memory (canonical
 // layout: sign rows, bscale, interleaved offset-binary nibbles, rscale; K then V).
@@ -343,13 +397,13 @@ __device__ __forceinline__ void init_soft(SoftState<GC, NP>& st) {
 //     score lane by shuffle.
 // Nibbles are stored offset-binary (u = code + 8), so no XOR is needed here.
 // ---------------------------------------------------------------------------
-template <int D, int GC, bool COMP, typename Cfg, bool ENT = false>
-__device__ __forceinline__ void consume_warp_tile(const QState<D, GC>& qs, SoftState<GC, Cfg::NP>& st,
-                                                  const uint8_t* sb, int kw, int nk) {
-    constexpr int NWD = Cfg::NWD, QPK = Cfg::QPK, KPW = Cfg::KPW, NP = Cfg::NP;
-    const int lane = threadIdx.x & 31;
-    const int kk = kw + lane;
-    const bool valid = kk < nk;
+// Score phase of one lane: key kk of the stage for the GC heads (scores in
+// log2 units, -inf for keys past the tile's end); the entropy variant also
+// folds the binary score into the lane's online entropy state.
+template <int D, int GC, bool COMP, typename Cfg, bool ENT, typename St>
+__device__ __forceinline__ void score_keys(const QState<D, GC>& qs, St& st, const uint8_t* sb, int kk, bool valid,
+                                           float (&s2)[GC]) {
+    constexpr int NWD = Cfg::NWD;
     // ---- score phase -------------------------------------------------------
     uint32_t ks[NWD];
     {
@@ -397,7 +451,6 @@ __device__ __forceinline__ void consume_warp_tile(const QState<D, GC>& qs, SoftS
 #pragma unroll
         for (int g = 0; g < GC; ++g) dot[g] = eh[g] * 256 + el[g] + ((oh[g] * 256 + ol[g]) >> 4);
     }
-    float s2[GC];
 #pragma unroll
     for (int g = 0; g < GC; ++g) {
         int pop = 0;
@@ -423,6 +476,17 @@ __device__ __forceinline__ void consume_warp_tile(const QState<D, GC>& qs, SoftS
             }
         }
     }
+}
+
+template <int D, int GC, bool COMP, typename Cfg, bool ENT = false>
+__device__ __forceinline__ void consume_warp_tile(const QState<D, GC>& qs, SoftState<GC, Cfg::NP>& st,
+                                                  const uint8_t* sb, int kw, int nk) {
+    constexpr int NWD = Cfg::NWD, QPK = Cfg::QPK, KPW = Cfg::KPW, NP = Cfg::NP;
+    const int lane = threadIdx.x & 31;
+    const int kk = kw + lane;
+    const bool valid = kk < nk;
+    float s2[GC];
+    score_keys<D, GC, COMP, Cfg, ENT>(qs, st, sb, kk, valid, s2);
     // ---- lazy rescale, weights -------------------------------------------------
     const float vbs = valid ? __half2float(reinterpret_cast<const __half*>(sb + Cfg::OFF_VBS)[kk]) : 0.0f;
     const float vrs = (COMP && valid) ? __half2float(reinterpret_cast<const __half*>(sb + Cfg::OFF_VRS)[kk]) : 0.0f;
@@ -537,6 +601,188 @@ __device__ __forceinline__ void consume_warp_tile(const QState<D, GC>& qs, SoftS
             }
         }
     }
+}
+
+// ---------------------------------------------------------------------------
+// Tensor-core value phase (compensated, head_dim 128, GC <= 2 heads).
+//
+// Per warp and tile: D[dims x (head, byte)] += V[dims x 32 keys] . W[32 keys x
+// (head, byte)] with mma.sync m16n8k32 u8 x u8 -> s32.  Lane = 4 g8 + q.
+//  * Keys: MMA k index 4q + 16G + i is the warp's key 8q + ((2q + 4G + i) & 7),
+//    so the four keys a lane reads per load sit in distinct shared-memory banks.
+//  * Sign part, tile t: rows g8 / g8 + 8 are dims 16 g8 + t / 16 g8 + 8 + t
+//    (sign bytes 2 g8, 2 g8 + 1 of each key, bit t, value 2^t).  A byte
+//    transpose (PRMT) puts the four keys' bytes in one register; a mask per
+//    bit then yields the u8 fragment directly.
+//  * Residual part, tile t: rows g8 / g8 + 8 are dims 16 g8 + 2t / 16 g8 + 2t + 1
+//    (nibble byte 8 g8 + t: low nibble as u, high nibble as 16 u).
+//  * Coefficients: each lane writes its key's fixed-point bytes to the warp's
+//    scratch ([part][head*4 + byte][MMA key slot]); lane reads its B fragment
+//    (column g8 = head g8/4, byte g8%4) as two 32-bit words.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+    uint32_t r;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
+    return r;
+}
+
+__device__ __forceinline__ void mma_u8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                       uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.u8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// r[t] = byte t of w0..w3, in that order (a 4x4 byte transpose).
+__device__ __forceinline__ void transpose4(uint32_t w0, uint32_t w1, uint32_t w2, uint32_t w3, uint32_t (&r)[4]) {
+    const uint32_t x0 = prmt(w0, w1, 0x5140), x1 = prmt(w0, w1, 0x7362);
+    const uint32_t y0 = prmt(w2, w3, 0x5140), y1 = prmt(w2, w3, 0x7362);
+    r[0] = prmt(x0, y0, 0x5410);
+    r[1] = prmt(x0, y0, 0x7632);
+    r[2] = prmt(x1, y1, 0x5410);
+    r[3] = prmt(x1, y1, 0x7632);
+}
+
+// Divide head g's accumulators by 2^delta (delta >= 1), exactly up to the
+// dropped low bits: each (row, part, tile) value is rebuilt from its four byte
+// columns (lanes 2g and 2g + 1), shifted, and split back into byte columns.
+template <int GC>
+__device__ __forceinline__ void mma_shift_down(MmaState<GC>& st, int g, int delta) {
+    const int q = threadIdx.x & 3;
+    const bool mine = (q >> 1) == g, upper = q & 1;
+#pragma unroll
+    for (int p = 0; p < 2; ++p)
+#pragma unroll
+        for (int t = 0; t < 8; ++t)
+#pragma unroll
+            for (int r = 0; r < 2; ++r) {
+                const uint64_t P = (uint64_t)(uint32_t)st.acc[p][t][2 * r] + ((uint64_t)(uint32_t)st.acc[p][t][2 * r + 1] << 8);
+                const uint64_t Pn = __shfl_xor_sync(0xffffffffu, P, 1);
+                const uint64_t lo = upper ? Pn : P, hi = upper ? P : Pn;
+                const uint64_t T = delta >= 63 ? 0 : (lo + (hi << 16)) >> delta;
+                if (mine) {
+                    st.acc[p][t][2 * r] = (int)(upper ? (T >> 16) & 0xFFu : T & 0xFFu);
+                    st.acc[p][t][2 * r + 1] = (int)(upper ? (T >> 24) : (T >> 8) & 0xFFu);
+                }
+            }
+}
+
+template <int D, int GC, typename Cfg, bool ENT = false>
+__device__ __forceinline__ void consume_warp_tile_mma(const QState<D, GC>& qs, MmaState<GC>& st, const uint8_t* sb,
+                                                      int kw, int nk, uint8_t* wb) {
+    static_assert(D == 128 && GC <= 2, "tensor-core value phase: head_dim 128, at most two heads per CTA");
+    const int lane = threadIdx.x & 31;
+    const int kk = kw + lane;
+    const bool valid = kk < nk;
+    float s2[GC];
+    score_keys<D, GC, true, Cfg, ENT>(qs, st, sb, kk, valid, s2);
+    const float vbs = valid ? __half2float(reinterpret_cast<const __half*>(sb + Cfg::OFF_VBS)[kk]) : 0.0f;
+    const float vrs = valid ? __half2float(reinterpret_cast<const __half*>(sb + Cfg::OFF_VRS)[kk]) : 0.0f;
+    // this lane's key in MMA k order
+    const int ip = ((lane & 7) - 2 * (lane >> 3)) & 7;
+    const int kpos = 4 * (lane >> 3) + 16 * (ip >> 2) + (ip & 3);
+#pragma unroll
+    for (int g = 0; g < GC; ++g) {
+        if (__any_sync(0xffffffffu, s2[g] > st.m[g] + kLazy)) {  // warp-uniform, rare after the first tile
+            float M = s2[g];
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+            const float alpha = fast_exp2(st.m[g] - M);
+            st.m[g] = M;
+            st.l[g] *= alpha;
+            st.t[g] *= alpha;
+        }
+        const float wt = valid ? fast_exp2(s2[g] - st.m[g]) : 0.0f;
+        st.l[g] += wt;
+        const float ca = 2.0f * wt * vbs;            // sign bit coefficient
+        const float cr = wt * vrs * (1.0f / 7.0f);   // code coefficient
+        st.t[g] += wt * vbs + 8.0f * cr;
+        float f = fast_exp2(st.m[g] - (float)st.U[g]);
+        float xa = ca * f, xr = cr * f;
+        const float cmax = fmaxf(ca, cr);
+        if (__any_sync(0xffffffffu, st.U[g] == kUUnset || fmaxf(xa, xr) >= 2147483648.0f)) {
+            // new unit: the warp's largest coefficient lands in (2^21, 2^22]
+            float lg = cmax > 0.0f ? log2f(cmax) + st.m[g] : -INFINITY;
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) lg = fmaxf(lg, __shfl_xor_sync(0xffffffffu, lg, off));
+            if (lg > -INFINITY) {
+                const int Un = (int)ceilf(lg) - 22;
+                if (st.U[g] != kUUnset && Un > st.U[g]) mma_shift_down(st, g, Un - st.U[g]);
+                if (st.U[g] == kUUnset || Un > st.U[g]) st.U[g] = Un;
+                f = fast_exp2(st.m[g] - (float)st.U[g]);
+                xa = ca * f;
+                xr = cr * f;
+            }
+        }
+        const bool have = st.U[g] != kUUnset;
+        const uint32_t A = have ? __float2uint_rn(xa) : 0u, R = have ? __float2uint_rn(xr) : 0u;
+#pragma unroll
+        for (int n = 0; n < 4; ++n) {
+            wb[(4 * g + n) * Cfg::WB_ROW + kpos] = (uint8_t)(A >> (8 * n));
+            wb[(8 + 4 * g + n) * Cfg::WB_ROW + kpos] = (uint8_t)(R >> (8 * n));
+        }
+    }
+    __syncwarp();
+    const int g8 = lane >> 2, q = lane & 3;
+    uint32_t bs0 = 0, bs1 = 0, br0 = 0, br1 = 0;
+    if (g8 < 4 * GC) {
+        const uint8_t* rs = wb + g8 * Cfg::WB_ROW + 4 * q;
+        const uint8_t* rr = wb + (8 + g8) * Cfg::WB_ROW + 4 * q;
+        bs0 = *reinterpret_cast<const uint32_t*>(rs);
+        bs1 = *reinterpret_cast<const uint32_t*>(rs + 16);
+        br0 = *reinterpret_cast<const uint32_t*>(rr);
+        br1 = *reinterpret_cast<const uint32_t*>(rr + 16);
+    }
+    // ---- sign part -------------------------------------------------------------
+    {
+        const uint8_t* vs = sb + Cfg::OFF_VSIGN + 4 * (g8 >> 1);
+        const uint32_t sel = 0x5140u + (uint32_t)(g8 & 1) * 0x2222u;
+        uint32_t ra[2], rb[2];
+#pragma unroll
+        for (int G = 0; G < 2; ++G) {
+            uint32_t w[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+                w[i] = *reinterpret_cast<const uint32_t*>(vs + (kw + 8 * q + ((2 * q + 4 * G + i) & 7)) * 16);
+            const uint32_t x = prmt(w[0], w[1], sel), y = prmt(w[2], w[3], sel);
+            ra[G] = prmt(x, y, 0x5410);
+            rb[G] = prmt(x, y, 0x7632);
+        }
+#pragma unroll
+        for (int t = 0; t < 8; ++t) {
+            const uint32_t mk = 0x01010101u << t;
+            mma_u8(st.acc[0][t], ra[0] & mk, rb[0] & mk, ra[1] & mk, rb[1] & mk, bs0, bs1);
+        }
+    }
+    // ---- residual part ---------------------------------------------------------
+    {
+        const uint8_t* vn = sb + Cfg::OFF_VNIB + 128 * (g8 >> 1) + 8 * (g8 & 1);
+        uint32_t r[2][8];
+#pragma unroll
+        for (int G = 0; G < 2; ++G) {
+            uint32_t lo[4], hi[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const int key = kw + 8 * q + ((2 * q + 4 * G + i) & 7);
+                const uint2 v = *reinterpret_cast<const uint2*>(vn + (key >> 3) * (4 * D) + 16 * (key & 7));
+                lo[i] = v.x;
+                hi[i] = v.y;
+            }
+            uint32_t t0[4], t1[4];
+            transpose4(lo[0], lo[1], lo[2], lo[3], t0);
+            transpose4(hi[0], hi[1], hi[2], hi[3], t1);
+#pragma unroll
+            for (int t = 0; t < 4; ++t) {
+                r[G][t] = t0[t];
+                r[G][4 + t] = t1[t];
+            }
+        }
+#pragma unroll
+        for (int t = 0; t < 8; ++t)
+            mma_u8(st.acc[1][t], r[0][t] & 0x0F0F0F0Fu, r[0][t] & 0xF0F0F0F0u, r[1][t] & 0x0F0F0F0Fu,
+                   r[1][t] & 0xF0F0F0F0u, br0, br1);
+    }
+    __syncwarp();  // the scratch is rewritten by the next tile
 }
 
 // Entropy partials (max, sum e^(s-max), sum e^(s-max) s) merge by the
@@ -664,13 +910,12 @@ __device__ __forceinline__ void xchg_finish(const DecodeArgs& a, int slot, int h
 // write the outputs (single split) or publish a partial and let the last CTA
 // of the (slot, head group) combine all splits.
 // ---------------------------------------------------------------------------
-template <int D, int GC, typename Cfg, bool ENT = false>
-__device__ __forceinline__ void finish_cta(const DecodeArgs& a, int slot, int hg, int split, uint8_t* smem,
-                                           SoftState<GC, Cfg::NP>& st) {
+// Per-warp record (m, l, o[d] - t) of each head into mg[warp][g][d + 2]:
+// f32x2 accumulators, reduced over the lanes holding the same dims.
+template <int D, int GC, typename Cfg>
+__device__ __forceinline__ void warp_records(float* mg, SoftState<GC, Cfg::NP>& st) {
     constexpr int KPW = Cfg::KPW, DL = Cfg::DL, NP = Cfg::NP;
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, qt = lane / KPW;
-    __syncthreads();  // ring no longer in use
-    float* mg = reinterpret_cast<float*>(smem);  // [warps][GC][D+2]
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, qt = lane / KPW;
 #pragma unroll
     for (int g = 0; g < GC; ++g) {
         float l = st.l[g], t = st.t[g];
@@ -702,6 +947,63 @@ __device__ __forceinline__ void finish_cta(const DecodeArgs& a, int slot, int hg
             rec[1] = l;
         }
     }
+}
+
+// The same record from the tensor-core accumulators.  Each lane dumps its
+// fragments to shared memory (the ring is free by now); lane 2g of each quad
+// then rebuilds head g's values from its byte columns (0, 1) and those of
+// lane 2g + 1 (2, 3), rows g8 and g8 + 8, and owns the quad's 16 dims.
+template <int D, int GC, typename Cfg>
+__device__ __forceinline__ void warp_records(float* mg, MmaState<GC>& st) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, g8 = lane >> 2, q = lane & 3;
+    int* dump = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(mg) + Cfg::DUMP_OFF) + warp * 32 * 65;
+#pragma unroll
+    for (int p = 0; p < 2; ++p)
+#pragma unroll
+        for (int t = 0; t < 8; ++t)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) dump[lane * 65 + 32 * p + 4 * t + i] = st.acc[p][t][i];
+    __syncwarp();
+#pragma unroll
+    for (int g = 0; g < GC; ++g) {
+        float l = st.l[g], t = st.t[g];
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) {
+            l += __shfl_xor_sync(0xffffffffu, l, off);
+            t += __shfl_xor_sync(0xffffffffu, t, off);
+        }
+        float* rec = mg + ((size_t)warp * GC + g) * (D + 2);
+        if (lane == 0) {
+            rec[0] = st.m[g];
+            rec[1] = l;
+        }
+        // accumulator unit relative to the warp's max: 2^(U - m)
+        const float sc = (st.U[g] != kUUnset && st.m[g] > -INFINITY) ? exp2f((float)st.U[g] - st.m[g]) : 0.0f;
+        // lane takes dims 4 lane .. 4 lane + 3: quad g8 = lane / 4, in-quad dims j
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const int j = 4 * q + e;
+            const int* lo = dump + (4 * g8 + 2 * g) * 65;
+            const int* hi = lo + 65;
+            // sign: tile j % 8, row j / 8; residual: tile j / 2, row j % 2
+            const int cs = 4 * (j & 7) + 2 * (j >> 3), cr = 32 + 4 * (j >> 1) + 2 * (j & 1);
+            const uint64_t s0 = (uint64_t)(uint32_t)lo[cs] + ((uint64_t)(uint32_t)lo[cs + 1] << 8);
+            const uint64_t s1 = (uint64_t)(uint32_t)hi[cs] + ((uint64_t)(uint32_t)hi[cs + 1] << 8);
+            const uint64_t r0 = (uint64_t)(uint32_t)lo[cr] + ((uint64_t)(uint32_t)lo[cr + 1] << 8);
+            const uint64_t r1 = (uint64_t)(uint32_t)hi[cr] + ((uint64_t)(uint32_t)hi[cr + 1] << 8);
+            const float vs = ((float)s0 + 65536.0f * (float)s1) * exp2i(-(j & 7));
+            const float vr = ((float)r0 + 65536.0f * (float)r1) * ((j & 1) ? (1.0f / 16.0f) : 1.0f);
+            rec[2 + 4 * lane + e] = (vs + vr) * sc - t;
+        }
+    }
+}
+
+template <int D, int GC, typename Cfg, bool ENT = false, typename St>
+__device__ __forceinline__ void finish_cta(const DecodeArgs& a, int slot, int hg, int split, uint8_t* smem, St& st) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    __syncthreads();  // ring no longer in use
+    float* mg = reinterpret_cast<float*>(smem);  // [warps][GC][D+2]
+    warp_records<D, GC, Cfg>(mg, st);
     __shared__ EntPart s_ent[ENT ? kWarps : 1][ENT ? GC : 1];
     if constexpr (ENT) {
 #pragma unroll
@@ -1094,7 +1396,10 @@ __global__ void __launch_bounds__(kDecThreads, DecCfg<D, GC, COMP>::MIN_CTAS)
             }
         }
     }
-    SoftState<GC, Cfg::NP> st;
+    // the tensor-core value phase (not in adaptive caches, whose binary-only
+    // segments keep the f32x2 path)
+    constexpr bool MMA = Cfg::MMA && !ADA;
+    std::conditional_t<MMA, MmaState<GC>, SoftState<GC, Cfg::NP>> st;
     init_soft(st);
 
     int it = 0;
@@ -1121,10 +1426,15 @@ __global__ void __launch_bounds__(kDecThreads, DecCfg<D, GC, COMP>::MIN_CTAS)
         if constexpr (STEP) {
             if (it == patch_it) patch_stage_row<D, COMP, Cfg>(smem + stage * Cfg::STAGE_B, patch_kk, smem);
         }
-        if (ADA && seg_bin)
-            consume_warp_tile<D, GC, false, Cfg>(qs, st, smem + stage * Cfg::STAGE_B, warp * 32, nk);
-        else
-            consume_warp_tile<D, GC, COMP, Cfg, ENT>(qs, st, smem + stage * Cfg::STAGE_B, warp * 32, nk);
+        if constexpr (MMA) {
+            consume_warp_tile_mma<D, GC, Cfg, ENT>(qs, st, smem + stage * Cfg::STAGE_B, warp * 32, nk,
+                                                   smem + Cfg::WB_OFF + warp * Cfg::WB_WARP);
+        } else {
+            if (ADA && seg_bin)
+                consume_warp_tile<D, GC, false, Cfg>(qs, st, smem + stage * Cfg::STAGE_B, warp * 32, nk);
+            else
+                consume_warp_tile<D, GC, COMP, Cfg, ENT>(qs, st, smem + stage * Cfg::STAGE_B, warp * 32, nk);
+        }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[stage]);
     }
@@ -1287,6 +1597,8 @@ int heads_per_cta(int group, int d, bool comp) {
 
 // Choose the split count so that all CTAs fit in one resident wave when the
 // slots alone cannot fill the GPU (avoids a ragged second wave).
+constexpr int kMaxKeysPerSplit = 32768 * kWarps;
+
 Plan make_plan(int n_slots, int group, int seq_len, int d, bool comp, int capacity) {
     Plan p;
     p.gc = heads_per_cta(group, d, comp);
@@ -1297,6 +1609,9 @@ Plan make_plan(int n_slots, int group, int seq_len, int d, bool comp, int capaci
     int splits = 1;
     if (units < capacity) splits = (int)((int64_t)capacity * BC_DEC_WAVES / units);
     splits = max(1, min(splits, n_tiles));
+    // at most kMaxKeysPerSplit keys per CTA: the tensor-core value phase's
+    // 32-bit accumulators take up to 32768 keys per warp
+    splits = max(splits, (n_tiles * p.tile + kMaxKeysPerSplit - 1) / kMaxKeysPerSplit);
     const int tiles_per_split = (n_tiles + splits - 1) / splits;
     p.keys_per_split = tiles_per_split * p.tile;
     p.n_splits = max(1, (max(seq_len, 1) + p.keys_per_split - 1) / p.keys_per_split);
