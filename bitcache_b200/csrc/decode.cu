@@ -607,25 +607,18 @@ __device__ __forceinline__ void consume_warp_tile(const QState<D, GC>& qs, SoftS
 // Tensor-core value phase (compensated, head_dim 128, GC <= 2 heads).
 //
 // Per warp and tile: D[dims x (head, byte)] += V[dims x 32 keys] . W[32 keys x
-// (head, byte)] with mma.sync m16n8k32 u8 x u8 -> s32.  Lane = 4 g8 + q.
-//  * Keys: MMA k index 4q + 16G + i is the warp's key 8q + ((2q + 4G + i) & 7),
-//    so the four keys a lane reads per load sit in distinct shared-memory banks.
-//  * Sign part, tile t: rows g8 / g8 + 8 are dims 16 g8 + t / 16 g8 + 8 + t
-//    (sign bytes 2 g8, 2 g8 + 1 of each key, bit t, value 2^t).  A byte
-//    transpose (PRMT) puts the four keys' bytes in one register; a mask per
-//    bit then yields the u8 fragment directly.
-//  * Residual part, tile t: rows g8 / g8 + 8 are dims 16 g8 + 2t / 16 g8 + 2t + 1
-//    (nibble byte 8 g8 + t: low nibble as u, high nibble as 16 u).
+// (head, byte)] with mma.sync m16n8k32 u8 x u8 -> s32.  Lane = 4 g8 + q; MMA
+// k index = the warp's key.  ldmatrix .m16n16 .trans .b8 on 16 keys x 16
+// bytes hands lane (g8, q) byte g8 (and g8 + 8) of keys 4q .. 4q + 3: the u8
+// A fragment of one byte position, so one mask per fragment remains.
+//  * Sign part, tile t: rows g8 / g8 + 8 are dims 8 g8 + t / 64 + 8 g8 + t
+//    (sign bytes g8, g8 + 8; bit t, value 2^t).
+//  * Residual part, tile 2c + h: rows g8 / g8 + 8 are dims 32c + 16h + 2 g8
+//    (low nibble, u) / the next dim (high nibble, 16 u), from 16-byte chunk c.
 //  * Coefficients: each lane writes its key's fixed-point bytes to the warp's
-//    scratch ([part][head*4 + byte][MMA key slot]); lane reads its B fragment
-//    (column g8 = head g8/4, byte g8%4) as two 32-bit words.
+//    scratch ([part][head*4 + byte][key]); lane reads its B fragment (column
+//    g8 = head g8/4, byte g8%4; keys 4q.., 4q + 16..) as two 32-bit words.
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
-    uint32_t r;
-    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
-    return r;
-}
-
 __device__ __forceinline__ void mma_u8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
                                        uint32_t b1) {
     asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.u8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
@@ -633,14 +626,13 @@ __device__ __forceinline__ void mma_u8(int (&d)[4], uint32_t a0, uint32_t a1, ui
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-// r[t] = byte t of w0..w3, in that order (a 4x4 byte transpose).
-__device__ __forceinline__ void transpose4(uint32_t w0, uint32_t w1, uint32_t w2, uint32_t w3, uint32_t (&r)[4]) {
-    const uint32_t x0 = prmt(w0, w1, 0x5140), x1 = prmt(w0, w1, 0x7362);
-    const uint32_t y0 = prmt(w2, w3, 0x5140), y1 = prmt(w2, w3, 0x7362);
-    r[0] = prmt(x0, y0, 0x5410);
-    r[1] = prmt(x0, y0, 0x7632);
-    r[2] = prmt(x1, y1, 0x5410);
-    r[3] = prmt(x1, y1, 0x7632);
+// Two 16x16 byte matrices, transposed: lanes 0-15 give the rows of the first,
+// lanes 16-31 those of the second; r0, r1 come from the first.
+__device__ __forceinline__ void ldsm_x2_trans_b8(const uint8_t* row, uint32_t& r0, uint32_t& r1, uint32_t& r2,
+                                                 uint32_t& r3) {
+    asm volatile("ldmatrix.sync.aligned.m16n16.x2.trans.shared.b8 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(smem_u32(row)));
 }
 
 // Divide head g's accumulators by 2^delta (delta >= 1), exactly up to the
@@ -678,9 +670,6 @@ __device__ __forceinline__ void consume_warp_tile_mma(const QState<D, GC>& qs, M
     score_keys<D, GC, true, Cfg, ENT>(qs, st, sb, kk, valid, s2);
     const float vbs = valid ? __half2float(reinterpret_cast<const __half*>(sb + Cfg::OFF_VBS)[kk]) : 0.0f;
     const float vrs = valid ? __half2float(reinterpret_cast<const __half*>(sb + Cfg::OFF_VRS)[kk]) : 0.0f;
-    // this lane's key in MMA k order
-    const int ip = ((lane & 7) - 2 * (lane >> 3)) & 7;
-    const int kpos = 4 * (lane >> 3) + 16 * (ip >> 2) + (ip & 3);
 #pragma unroll
     for (int g = 0; g < GC; ++g) {
         if (__any_sync(0xffffffffu, s2[g] > st.m[g] + kLazy)) {  // warp-uniform, rare after the first tile
@@ -718,8 +707,8 @@ __device__ __forceinline__ void consume_warp_tile_mma(const QState<D, GC>& qs, M
         const uint32_t A = have ? __float2uint_rn(xa) : 0u, R = have ? __float2uint_rn(xr) : 0u;
 #pragma unroll
         for (int n = 0; n < 4; ++n) {
-            wb[(4 * g + n) * Cfg::WB_ROW + kpos] = (uint8_t)(A >> (8 * n));
-            wb[(8 + 4 * g + n) * Cfg::WB_ROW + kpos] = (uint8_t)(R >> (8 * n));
+            wb[(4 * g + n) * Cfg::WB_ROW + lane] = (uint8_t)(A >> (8 * n));
+            wb[(8 + 4 * g + n) * Cfg::WB_ROW + lane] = (uint8_t)(R >> (8 * n));
         }
     }
     __syncwarp();
@@ -735,52 +724,25 @@ __device__ __forceinline__ void consume_warp_tile_mma(const QState<D, GC>& qs, M
     }
     // ---- sign part -------------------------------------------------------------
     {
-        const uint8_t* vs = sb + Cfg::OFF_VSIGN + 4 * (g8 >> 1);
-        const uint32_t sel = 0x5140u + (uint32_t)(g8 & 1) * 0x2222u;
-        uint32_t ra[2], rb[2];
-#pragma unroll
-        for (int G = 0; G < 2; ++G) {
-            uint32_t w[4];
-#pragma unroll
-            for (int i = 0; i < 4; ++i)
-                w[i] = *reinterpret_cast<const uint32_t*>(vs + (kw + 8 * q + ((2 * q + 4 * G + i) & 7)) * 16);
-            const uint32_t x = prmt(w[0], w[1], sel), y = prmt(w[2], w[3], sel);
-            ra[G] = prmt(x, y, 0x5410);
-            rb[G] = prmt(x, y, 0x7632);
-        }
+        uint32_t r0, r1, r2, r3;
+        ldsm_x2_trans_b8(sb + Cfg::OFF_VSIGN + (kw + lane) * (D / 8), r0, r1, r2, r3);
 #pragma unroll
         for (int t = 0; t < 8; ++t) {
             const uint32_t mk = 0x01010101u << t;
-            mma_u8(st.acc[0][t], ra[0] & mk, rb[0] & mk, ra[1] & mk, rb[1] & mk, bs0, bs1);
+            mma_u8(st.acc[0][t], r0 & mk, r1 & mk, r2 & mk, r3 & mk, bs0, bs1);
         }
     }
     // ---- residual part ---------------------------------------------------------
     {
-        const uint8_t* vn = sb + Cfg::OFF_VNIB + 128 * (g8 >> 1) + 8 * (g8 & 1);
-        uint32_t r[2][8];
+        const uint8_t* vn = sb + Cfg::OFF_VNIB + ((kw + lane) >> 3) * (4 * D) + 16 * ((kw + lane) & 7);
 #pragma unroll
-        for (int G = 0; G < 2; ++G) {
-            uint32_t lo[4], hi[4];
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const int key = kw + 8 * q + ((2 * q + 4 * G + i) & 7);
-                const uint2 v = *reinterpret_cast<const uint2*>(vn + (key >> 3) * (4 * D) + 16 * (key & 7));
-                lo[i] = v.x;
-                hi[i] = v.y;
-            }
-            uint32_t t0[4], t1[4];
-            transpose4(lo[0], lo[1], lo[2], lo[3], t0);
-            transpose4(hi[0], hi[1], hi[2], hi[3], t1);
-#pragma unroll
-            for (int t = 0; t < 4; ++t) {
-                r[G][t] = t0[t];
-                r[G][4 + t] = t1[t];
-            }
+        for (int c = 0; c < 4; ++c) {
+            uint32_t r0, r1, r2, r3;
+            ldsm_x2_trans_b8(vn + 128 * c, r0, r1, r2, r3);
+            mma_u8(st.acc[1][2 * c], r0 & 0x0F0F0F0Fu, r0 & 0xF0F0F0F0u, r2 & 0x0F0F0F0Fu, r2 & 0xF0F0F0F0u, br0, br1);
+            mma_u8(st.acc[1][2 * c + 1], r1 & 0x0F0F0F0Fu, r1 & 0xF0F0F0F0u, r3 & 0x0F0F0F0Fu, r3 & 0xF0F0F0F0u, br0,
+                   br1);
         }
-#pragma unroll
-        for (int t = 0; t < 8; ++t)
-            mma_u8(st.acc[1][t], r[0][t] & 0x0F0F0F0Fu, r[0][t] & 0xF0F0F0F0u, r[1][t] & 0x0F0F0F0Fu,
-                   r[1][t] & 0xF0F0F0F0u, br0, br1);
     }
     __syncwarp();  // the scratch is rewritten by the next tile
 }
@@ -979,21 +941,23 @@ __device__ __forceinline__ void warp_records(float* mg, MmaState<GC>& st) {
         }
         // accumulator unit relative to the warp's max: 2^(U - m)
         const float sc = (st.U[g] != kUUnset && st.m[g] > -INFINITY) ? exp2f((float)st.U[g] - st.m[g]) : 0.0f;
-        // lane takes dims 4 lane .. 4 lane + 3: quad g8 = lane / 4, in-quad dims j
+        // lane takes dims 4 lane .. 4 lane + 3
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-            const int j = 4 * q + e;
-            const int* lo = dump + (4 * g8 + 2 * g) * 65;
-            const int* hi = lo + 65;
-            // sign: tile j % 8, row j / 8; residual: tile j / 2, row j % 2
-            const int cs = 4 * (j & 7) + 2 * (j >> 3), cr = 32 + 4 * (j >> 1) + 2 * (j & 1);
-            const uint64_t s0 = (uint64_t)(uint32_t)lo[cs] + ((uint64_t)(uint32_t)lo[cs + 1] << 8);
-            const uint64_t s1 = (uint64_t)(uint32_t)hi[cs] + ((uint64_t)(uint32_t)hi[cs + 1] << 8);
-            const uint64_t r0 = (uint64_t)(uint32_t)lo[cr] + ((uint64_t)(uint32_t)lo[cr + 1] << 8);
-            const uint64_t r1 = (uint64_t)(uint32_t)hi[cr] + ((uint64_t)(uint32_t)hi[cr + 1] << 8);
-            const float vs = ((float)s0 + 65536.0f * (float)s1) * exp2i(-(j & 7));
-            const float vr = ((float)r0 + 65536.0f * (float)r1) * ((j & 1) ? (1.0f / 16.0f) : 1.0f);
-            rec[2 + 4 * lane + e] = (vs + vr) * sc - t;
+            const int dim = 4 * lane + e;
+            // sign: quad (dim % 64) / 8, tile dim % 8, row dim / 64
+            const int* ls = dump + (4 * ((dim & 63) >> 3) + 2 * g) * 65;
+            const int cs = 4 * (dim & 7) + 2 * (dim >> 6);
+            // residual: quad (dim / 2) % 8, tile 2 (dim / 32) + (dim / 16) % 2, row dim % 2
+            const int* lr = dump + (4 * ((dim >> 1) & 7) + 2 * g) * 65;
+            const int cr = 32 + 4 * (2 * (dim >> 5) + ((dim >> 4) & 1)) + 2 * (dim & 1);
+            const uint64_t s0 = (uint64_t)(uint32_t)ls[cs] + ((uint64_t)(uint32_t)ls[cs + 1] << 8);
+            const uint64_t s1 = (uint64_t)(uint32_t)ls[65 + cs] + ((uint64_t)(uint32_t)ls[65 + cs + 1] << 8);
+            const uint64_t r0 = (uint64_t)(uint32_t)lr[cr] + ((uint64_t)(uint32_t)lr[cr + 1] << 8);
+            const uint64_t r1 = (uint64_t)(uint32_t)lr[65 + cr] + ((uint64_t)(uint32_t)lr[65 + cr + 1] << 8);
+            const float vs = ((float)s0 + 65536.0f * (float)s1) * exp2i(-(dim & 7));
+            const float vr = ((float)r0 + 65536.0f * (float)r1) * ((dim & 1) ? (1.0f / 16.0f) : 1.0f);
+            rec[2 + dim] = (vs + vr) * sc - t;
         }
     }
 }

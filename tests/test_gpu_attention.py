@@ -111,6 +111,40 @@ def test_gqa_vs_oracle(cuda, group, d, comp):
     close(mine, want, f"gqa g={group} d={d} comp={comp}")
 
 
+@pytest.mark.parametrize("pattern", ["score_ramp", "value_jump"])
+@pytest.mark.parametrize("group", [1, 2])
+def test_growing_coefficients_vs_oracle(cuda, pattern, group):
+    """Key coefficients that grow within a split: the tensor-core value phase
+    must move its fixed-point unit and shift the accumulators down exactly.
+    score_ramp: scores rise by ~30 log2 units over every 256 positions (a
+    sawtooth, so every period's top keys carry equal weight); value_jump: the
+    first half of every period holds values 2^12 times smaller."""
+    slots, S, d = 32, 8192, 128
+    g = torch.Generator().manual_seed(5 + group)
+    q = (torch.randn(slots * group, d, generator=g) * 0.5).half()
+    pos = torch.arange(S, dtype=torch.float32)
+    phase = (pos % 256) / 256.0
+    k = torch.randn(slots, S, d, generator=g) * 0.3
+    v = torch.randn(slots, S, d, generator=g) * 0.5
+    if pattern == "score_ramp":
+        k += (8.0 * phase)[None, :, None] * q.float().view(slots, group, d)[:, 0][:, None, :]
+    else:
+        v *= torch.where(phase < 0.5, 2.0 ** -12, 1.0)[None, :, None]
+    k, v = k.half(), v.half()
+    K = planes.Planes.empty(slots, S, d, True, cuda)
+    V = planes.Planes.empty(slots, S, d, True, cuda)
+    planes.encode_planes(k.to(cuda), K, planes.RES_FP32_SCALE)
+    planes.encode_planes(v.to(cuda), V, planes.RES_FP32_SCALE)
+    mine = planes.decode_attention(q.to(cuda), K, V, S)
+
+    def host(X):
+        return {"words": X.sign.cpu().numpy().view(np.uint32), "bscale": X.bscale.cpu().numpy().view(np.uint16),
+                "nib": X.nib_rows().cpu().numpy(), "rscale": X.rscale.cpu().numpy().view(np.uint16)}
+
+    want = O.attention(q.numpy(), host(K), host(V), group, S, S, True).view(np.float16).astype(np.float32)
+    close(mine, want, f"{pattern} group={group}")
+
+
 @pytest.mark.parametrize("S", [0, 1, 7, 8, 9, 129, 1000])
 def test_seq_len_edges_and_masking(cuda, S):
     """Positions past seq_len hold garbage and must not contribute; seq_len 0 gives zeros."""
