@@ -659,7 +659,9 @@ __device__ __forceinline__ void mma_shift_down(MmaState<GC>& st, int g, int delt
             }
 }
 
-template <int D, int GC, typename Cfg, bool ENT = false>
+// RES = false: binary-only keys (the adaptive cache's second segment), the
+// sign part alone; the residual accumulators are left untouched.
+template <int D, int GC, typename Cfg, bool ENT = false, bool RES = true>
 __device__ __forceinline__ void consume_warp_tile_mma(const QState<D, GC>& qs, MmaState<GC>& st, const uint8_t* sb,
                                                       int kw, int nk, uint8_t* wb) {
     static_assert(D == 128 && GC <= 2, "tensor-core value phase: head_dim 128, at most two heads per CTA");
@@ -667,9 +669,9 @@ __device__ __forceinline__ void consume_warp_tile_mma(const QState<D, GC>& qs, M
     const int kk = kw + lane;
     const bool valid = kk < nk;
     float s2[GC];
-    score_keys<D, GC, true, Cfg, ENT>(qs, st, sb, kk, valid, s2);
+    score_keys<D, GC, RES, Cfg, ENT>(qs, st, sb, kk, valid, s2);
     const float vbs = valid ? __half2float(reinterpret_cast<const __half*>(sb + Cfg::OFF_VBS)[kk]) : 0.0f;
-    const float vrs = valid ? __half2float(reinterpret_cast<const __half*>(sb + Cfg::OFF_VRS)[kk]) : 0.0f;
+    const float vrs = (RES && valid) ? __half2float(reinterpret_cast<const __half*>(sb + Cfg::OFF_VRS)[kk]) : 0.0f;
 #pragma unroll
     for (int g = 0; g < GC; ++g) {
         if (__any_sync(0xffffffffu, s2[g] > st.m[g] + kLazy)) {  // warp-uniform, rare after the first tile
@@ -708,7 +710,7 @@ __device__ __forceinline__ void consume_warp_tile_mma(const QState<D, GC>& qs, M
 #pragma unroll
         for (int n = 0; n < 4; ++n) {
             wb[(4 * g + n) * Cfg::WB_ROW + lane] = (uint8_t)(A >> (8 * n));
-            wb[(8 + 4 * g + n) * Cfg::WB_ROW + lane] = (uint8_t)(R >> (8 * n));
+            if (RES) wb[(8 + 4 * g + n) * Cfg::WB_ROW + lane] = (uint8_t)(R >> (8 * n));
         }
     }
     __syncwarp();
@@ -719,8 +721,10 @@ __device__ __forceinline__ void consume_warp_tile_mma(const QState<D, GC>& qs, M
         const uint8_t* rr = wb + (8 + g8) * Cfg::WB_ROW + 4 * q;
         bs0 = *reinterpret_cast<const uint32_t*>(rs);
         bs1 = *reinterpret_cast<const uint32_t*>(rs + 16);
-        br0 = *reinterpret_cast<const uint32_t*>(rr);
-        br1 = *reinterpret_cast<const uint32_t*>(rr + 16);
+        if (RES) {
+            br0 = *reinterpret_cast<const uint32_t*>(rr);
+            br1 = *reinterpret_cast<const uint32_t*>(rr + 16);
+        }
     }
     // ---- sign part -------------------------------------------------------------
     {
@@ -733,7 +737,7 @@ __device__ __forceinline__ void consume_warp_tile_mma(const QState<D, GC>& qs, M
         }
     }
     // ---- residual part ---------------------------------------------------------
-    {
+    if constexpr (RES) {
         const uint8_t* vn = sb + Cfg::OFF_VNIB + ((kw + lane) >> 3) * (4 * D) + 16 * ((kw + lane) & 7);
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
@@ -917,7 +921,7 @@ __device__ __forceinline__ void warp_records(float* mg, SoftState<GC, Cfg::NP>& 
 // lane 2g + 1 (2, 3), rows g8 and g8 + 8, and owns the quad's 16 dims.
 template <int D, int GC, typename Cfg>
 __device__ __forceinline__ void warp_records(float* mg, MmaState<GC>& st) {
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, g8 = lane >> 2, q = lane & 3;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     int* dump = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(mg) + Cfg::DUMP_OFF) + warp * 32 * 65;
 #pragma unroll
     for (int p = 0; p < 2; ++p)
@@ -1360,9 +1364,9 @@ __global__ void __launch_bounds__(kDecThreads, DecCfg<D, GC, COMP>::MIN_CTAS)
             }
         }
     }
-    // the tensor-core value phase (not in adaptive caches, whose binary-only
-    // segments keep the f32x2 path)
-    constexpr bool MMA = Cfg::MMA && !ADA;
+    // the tensor-core value phase (in adaptive caches the binary-only
+    // segment runs its sign part alone)
+    constexpr bool MMA = Cfg::MMA;
     std::conditional_t<MMA, MmaState<GC>, SoftState<GC, Cfg::NP>> st;
     init_soft(st);
 
@@ -1391,8 +1395,11 @@ __global__ void __launch_bounds__(kDecThreads, DecCfg<D, GC, COMP>::MIN_CTAS)
             if (it == patch_it) patch_stage_row<D, COMP, Cfg>(smem + stage * Cfg::STAGE_B, patch_kk, smem);
         }
         if constexpr (MMA) {
-            consume_warp_tile_mma<D, GC, Cfg, ENT>(qs, st, smem + stage * Cfg::STAGE_B, warp * 32, nk,
-                                                   smem + Cfg::WB_OFF + warp * Cfg::WB_WARP);
+            uint8_t* wb = smem + Cfg::WB_OFF + warp * Cfg::WB_WARP;
+            if (ADA && seg_bin)
+                consume_warp_tile_mma<D, GC, Cfg, false, false>(qs, st, smem + stage * Cfg::STAGE_B, warp * 32, nk, wb);
+            else
+                consume_warp_tile_mma<D, GC, Cfg, ENT>(qs, st, smem + stage * Cfg::STAGE_B, warp * 32, nk, wb);
         } else {
             if (ADA && seg_bin)
                 consume_warp_tile<D, GC, false, Cfg>(qs, st, smem + stage * Cfg::STAGE_B, warp * 32, nk);
@@ -1691,7 +1698,10 @@ int capacity_of(int var) {
 // binary one (seq_len - n_keep) so that one resident wave covers both, giving
 // a binary split kBinKeysPerComp times the keys of a compensated split (a
 // binary key costs about 40% of a compensated one).
-constexpr int kBinKeysPerComp = 5;  // in halves: 2.5x
+#ifndef BC_DEC_BIN_HALVES
+#define BC_DEC_BIN_HALVES 5
+#endif
+constexpr int kBinKeysPerComp = BC_DEC_BIN_HALVES;  // in halves: 2.5x
 void plan_adaptive(DecodeArgs& a, int gc, int capacity) {
     const int n_hgroups = a.group / gc;
     const int64_t units = (int64_t)a.n_slots * n_hgroups;
