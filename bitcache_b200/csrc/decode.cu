@@ -146,6 +146,7 @@ struct DecodeArgs {
     const __half* new_k;
     const __half* new_v;
     int append_pos, append_res;
+    int host_in;        // fused step: bit 0 q, bit 1 new_k / new_v are in pinned host memory
     // paged caches (pages != null): logical position s of slot j lives in plane
     // row pages[j * max_pages + s / page_size] * page_size + s % page_size
     const int* pages;
@@ -1263,28 +1264,37 @@ __global__ void __launch_bounds__(kDecThreads, DecCfg<D, GC, COMP>::MIN_CTAS)
     const int n_keys = max(0, s_end - s_begin);
     const int n_tiles = (n_keys + T - 1) / T;
 
-    // Launched with programmatic stream serialisation: everything above ran
-    // while the previous kernel in the stream may still be finishing; wait
-    // for it (and its memory) before the first global access.
-    asm volatile("griddepcontrol.wait;" ::: "memory");
-    // Small inputs first: their copies start before the ring's bulk copies.
-    const bool staged = prefetch_query<D, GC, Cfg>(a, slot, hg, smem);
     // fused step: does this CTA's key range hold the append position?
     const bool appends = STEP && a.append_pos >= s_begin && a.append_pos < s_end;
     const __half* new_src[2] = {nullptr, nullptr};
-    if constexpr (STEP) {
-        if (appends) {
-            const __half* g[2] = {a.new_k + (int64_t)slot * D, a.new_v + (int64_t)slot * D};
-            const bool aligned = ((reinterpret_cast<uintptr_t>(g[0]) | reinterpret_cast<uintptr_t>(g[1])) & 15) == 0;
-            __half* raw = reinterpret_cast<__half*>(smem + Cfg::NEWRAW_OFF);
-            for (int j = 0; j < 2; ++j) {
-                new_src[j] = aligned ? raw + j * D : g[j];
-                if (aligned)
-                    for (int c = tid; c < D / 8; c += kDecThreads) cp_async16(raw + j * D + 8 * c, g[j] + 8 * c);
+    auto fetch_new_rows = [&]() {
+        if constexpr (STEP) {
+            if (appends) {
+                const __half* g[2] = {a.new_k + (int64_t)slot * D, a.new_v + (int64_t)slot * D};
+                const bool aligned = ((reinterpret_cast<uintptr_t>(g[0]) | reinterpret_cast<uintptr_t>(g[1])) & 15) == 0;
+                __half* raw = reinterpret_cast<__half*>(smem + Cfg::NEWRAW_OFF);
+                for (int j = 0; j < 2; ++j) {
+                    new_src[j] = aligned ? raw + j * D : g[j];
+                    if (aligned)
+                        for (int c = tid; c < D / 8; c += kDecThreads) cp_async16(raw + j * D + 8 * c, g[j] + 8 * c);
+                }
+                asm volatile("cp.async.commit_group;" ::: "memory");
             }
-            asm volatile("cp.async.commit_group;" ::: "memory");
         }
-    }
+    };
+    // Inputs in pinned host memory cannot be written by the previous kernel in
+    // the stream: their (slow, host-link) reads start before waiting for it.
+    const bool q_host = STEP && (a.host_in & 1), kv_host = STEP && (a.host_in & 2);
+    bool staged = false;
+    if (q_host) staged = prefetch_query<D, GC, Cfg>(a, slot, hg, smem);
+    if (kv_host) fetch_new_rows();
+    // Launched with programmatic stream serialisation: everything above ran
+    // while the previous kernel in the stream may still be finishing; wait
+    // for it (and its memory) before the first access to device memory.
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    // Small inputs first: their copies start before the ring's bulk copies.
+    if (!q_host) staged = prefetch_query<D, GC, Cfg>(a, slot, hg, smem);
+    if (!kv_host) fetch_new_rows();
 
     if (tid == 0) {
         for (int s = 0; s < NS; ++s) {
@@ -1970,6 +1980,31 @@ int bc_decode_attention_entropy(const void* q, bc_kv_planes K, bc_kv_planes V, v
     return run_decode(a, mode == BC_MODE_COMPENSATED, kVarEntropy, workspace, workspace_bytes, (cudaStream_t)stream);
 }
 
+}  // extern "C"
+
+namespace {
+// Where the fused step's host-side operands live: bit 0 q, bit 1 new_k and
+// new_v in pinned (page-locked) host memory, which kernels read through
+// unified addressing; -1 for pageable host memory, which they cannot.
+int host_inputs(const void* q, const void* new_k, const void* new_v, const void* out) {
+    auto kind = [](const void* p) -> int {  // 0 device / managed / null, 1 pinned host, -1 pageable
+        if (!p) return 0;
+        cudaPointerAttributes at;
+        if (cudaPointerGetAttributes(&at, p) != cudaSuccess) {
+            cudaGetLastError();
+            return -1;
+        }
+        if (at.type == cudaMemoryTypeHost) return 1;
+        return at.type == cudaMemoryTypeUnregistered ? -1 : 0;
+    };
+    const int kq = kind(q), kk = kind(new_k), kv = kind(new_v), ko = kind(out);
+    if (kq < 0 || kk < 0 || kv < 0 || ko < 0) return -1;
+    return (kq ? 1 : 0) | ((kk || kv) ? 2 : 0);
+}
+}  // namespace
+
+extern "C" {
+
 int bc_decode_step(const void* q, const void* new_k, const void* new_v, bc_kv_planes K, bc_kv_planes V, void* out,
                    float* partial, int n_slots, int group, int seq_len, int64_t kv_stride, int head_dim, int mode,
                    int append_pos, int append_res, void* workspace, size_t workspace_bytes, void* stream) {
@@ -1991,6 +2026,9 @@ int bc_decode_step(const void* q, const void* new_k, const void* new_v, bc_kv_pl
         a.append_pos = append_pos;
         a.append_res = append_res;
     }
+    const int hi = host_inputs(q, a.new_k, a.new_v, out);
+    if (hi < 0) return BC_ERR_ARG;
+    a.host_in = hi;
     return run_decode(a, mode == BC_MODE_COMPENSATED, kVarStep, workspace, workspace_bytes, (cudaStream_t)stream);
 }
 
@@ -2024,6 +2062,9 @@ int bc_decode_step_paged(const void* q, const void* new_k, const void* new_v, bc
         a.append_pos = append_pos;
         a.append_res = append_res;
     }
+    const int hi = host_inputs(q, a.new_k, a.new_v, out);
+    if (hi < 0) return BC_ERR_ARG;
+    a.host_in = hi;
     return run_decode(a, mode == BC_MODE_COMPENSATED, kVarStep, workspace, workspace_bytes, (cudaStream_t)stream);
 }
 

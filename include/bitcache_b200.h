@@ -176,7 +176,10 @@ int bc_decode_attention_entropy(const void* q, bc_kv_planes K, bc_kv_planes V, v
  * 0 <= append_pos < seq_len, and compensated attention needs append_res != BC_RES_NONE.
  * q, new_k, new_v and out may point to pinned (page-locked) host memory: with unified
  * addressing the kernel reads the step's inputs and writes its output over the host link
- * itself, so a host-driven decode loop needs no separate copies.
+ * itself, so a host-driven decode loop needs no separate copies.  Host inputs are read
+ * before the kernel waits for the previous one in the stream (programmatic dependent
+ * launch), so they must not be written by work queued ahead of this call.  Pageable
+ * host pointers are rejected with BC_ERR_ARG.
  * Workspace as bc_decode_workspace_bytes. */
 int bc_decode_step(const void* q, const void* new_k, const void* new_v, bc_kv_planes K, bc_kv_planes V, void* out,
                    float* partial, int n_slots, int group, int seq_len, int64_t kv_stride, int head_dim, int mode,

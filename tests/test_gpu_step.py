@@ -138,6 +138,28 @@ def test_step_rejects_bad_arguments(cuda):
         planes.decode_step(q, k, k, K, V, 10, 3, residual_mode=planes.RES_NONE)
 
 
+def test_step_rejects_pageable_host_operands(cuda):
+    """The kernel reads host operands through unified addressing, which only
+    pinned memory has: the C ABI refuses pageable pointers (status, no launch)."""
+    from bitcache_b200 import _lib
+    lib = _lib.load()
+    K = planes.Planes.empty(1, 64, 128, True, cuda)
+    V = planes.Planes.empty(1, 64, 128, True, cuda)
+    out = torch.empty(1, 128, dtype=torch.float16, device=cuda)
+    qd = torch.zeros(1, 128, dtype=torch.float16, device=cuda)
+    pageable = torch.zeros(1, 128, dtype=torch.float16)  # ordinary host memory
+    assert not pageable.is_pinned()
+    ws = torch.empty(1 << 20, dtype=torch.uint8, device=cuda)
+    st = _lib.stream_of(cuda)
+    for q, k in ((pageable, qd), (qd, pageable)):
+        rc = lib.bc_decode_step(q.data_ptr(), k.data_ptr(), k.data_ptr(), K.c(), V.c(), out.data_ptr(), None, 1, 1,
+                                10, K.kv_stride, 128, planes.MODE_COMPENSATED, 3, _lib.BC_RES_FP32_SCALE,
+                                ws.data_ptr(), ws.numel(), st)
+        assert rc == 2, f"pageable operand accepted (status {rc})"  # BC_ERR_ARG
+    torch.cuda.synchronize()
+    assert _lib.device_error() == 0
+
+
 def test_bitcache_step_matches_append_attend_and_oracle(cuda):
     """BitCache.step over a ring that wraps, against append+attend on a twin
     cache (bit-identical planes) and the oracle on the final contents."""
