@@ -61,6 +61,9 @@ __device__ unsigned int g_bc_device_error = 0;
 #ifndef BC_DEC_MIN_CTAS_C1
 #define BC_DEC_MIN_CTAS_C1 4   // resident CTAs per SM the compensated one-head kernel is held to
 #endif
+#ifndef BC_DEC_MIN_TILES
+#define BC_DEC_MIN_TILES 1     // fewest 128-key tiles a split is planned with
+#endif
 #ifndef BC_DEC_MMA
 #define BC_DEC_MMA 1           // compensated head_dim-128 value phase on the tensor cores (u8 mma.sync)
 #endif
@@ -1589,7 +1592,7 @@ Plan make_plan(int n_slots, int group, int seq_len, int d, bool comp, int capaci
     const int64_t units = (int64_t)n_slots * p.n_hgroups;
     int splits = 1;
     if (units < capacity) splits = (int)((int64_t)capacity * BC_DEC_WAVES / units);
-    splits = max(1, min(splits, n_tiles));
+    splits = max(1, min(splits, n_tiles / BC_DEC_MIN_TILES));
     // at most kMaxKeysPerSplit keys per CTA: the tensor-core value phase's
     // 32-bit accumulators take up to 32768 keys per warp
     splits = max(splits, (n_tiles * p.tile + kMaxKeysPerSplit - 1) / kMaxKeysPerSplit);
