@@ -61,6 +61,9 @@ __device__ unsigned int g_bc_device_error = 0;
 #ifndef BC_DEC_MIN_CTAS_C1
 #define BC_DEC_MIN_CTAS_C1 4   // resident CTAs per SM the compensated one-head kernel is held to
 #endif
+#ifndef BC_DEC_MIN_CTAS_B1
+#define BC_DEC_MIN_CTAS_B1 5   // resident CTAs per SM the binary one-head kernel is held to
+#endif
 #ifndef BC_DEC_MIN_TILES
 #define BC_DEC_MIN_TILES 1     // fewest 128-key tiles a split is planned with
 #endif
@@ -122,16 +125,16 @@ struct DecCfg {
     static constexpr int NEWRAW_OFF = NEW_OFF + 2 * NEWROW_B;   // fp16 [2][D]: the new K, V rows as given
     // Tensor-core value phase (compensated, head_dim 128, one or two heads per
     // CTA): per warp, the fixed-point key coefficients as bytes, [part][row][48].
-    static constexpr bool MMA = BC_DEC_MMA && COMP && D == 128 && GC <= 2;
+    static constexpr bool MMA = BC_DEC_MMA && D == 128 && GC <= 2;
     static constexpr int WB_ROW = 48;                           // padded: the fragment loads hit distinct banks
     static constexpr int WB_WARP = 2 * 8 * WB_ROW;
     static constexpr int WB_OFF = NEWRAW_OFF + 4 * D;
     static constexpr int SMEM_B = WB_OFF + (MMA ? kWarps * WB_WARP : 0) + 128;  // + slack to align the base to 128 B
-    static_assert(!MMA || DUMP_OFF + DUMP_B <= BODY_B, "accumulator dump exceeds the ring");
+    static_assert(!MMA || !COMP || DUMP_OFF + DUMP_B <= BODY_B, "accumulator dump exceeds the ring");
     // Resident CTAs per SM that shared memory allows at head_dim <= 128 with one
     // head per CTA; the register budget is held to it (0: no bound).
     static constexpr int MIN_CTAS =
-        (D > 128) ? 0 : ((GC == 1 && !COMP) ? 8 : (GC == 1 ? BC_DEC_MIN_CTAS_C1 : 4)) * 128 / kDecThreads;
+        (D > 128) ? 0 : ((GC == 1 && !COMP) ? BC_DEC_MIN_CTAS_B1 : (GC == 1 ? BC_DEC_MIN_CTAS_C1 : 4)) * 128 / kDecThreads;
 };
 
 struct DecodeArgs {
@@ -360,17 +363,18 @@ __device__ __forceinline__ void init_soft(SoftState<GC, NP>& st) {
 // would reach 2^31 units, and the accumulators are then shifted down exactly.
 constexpr int kUUnset = -0x40000000;
 
-template <int GC>
+template <int GC, int P = 2>
 struct MmaState {
+    static constexpr int PARTS = P;  // 2: sign and residual; 1: binary-only cache
     float m[GC];
     float l[GC], t[GC];
-    int acc[2][8][4];
+    int acc[P][8][4];
     int U[GC];
     float em[GC], ez[GC], ew[GC];
 };
 
-template <int GC>
-__device__ __forceinline__ void init_soft(MmaState<GC>& st) {
+template <int GC, int P>
+__device__ __forceinline__ void init_soft(MmaState<GC, P>& st) {
 #pragma unroll
     for (int g = 0; g < GC; ++g) {
         st.m[g] = -INFINITY;
@@ -382,7 +386,7 @@ __device__ __forceinline__ void init_soft(MmaState<GC>& st) {
         st.ew[g] = 0.0f;
     }
 #pragma unroll
-    for (int p = 0; p < 2; ++p)
+    for (int p = 0; p < P; ++p)
 #pragma unroll
         for (int t = 0; t < 8; ++t)
 #pragma unroll
@@ -642,12 +646,12 @@ __device__ __forceinline__ void ldsm_x2_trans_b8(const uint8_t* row, uint32_t& r
 // Divide head g's accumulators by 2^delta (delta >= 1), exactly up to the
 // dropped low bits: each (row, part, tile) value is rebuilt from its four byte
 // columns (lanes 2g and 2g + 1), shifted, and split back into byte columns.
-template <int GC>
-__device__ __forceinline__ void mma_shift_down(MmaState<GC>& st, int g, int delta) {
+template <int GC, int P>
+__device__ __forceinline__ void mma_shift_down(MmaState<GC, P>& st, int g, int delta) {
     const int q = threadIdx.x & 3;
     const bool mine = (q >> 1) == g, upper = q & 1;
 #pragma unroll
-    for (int p = 0; p < 2; ++p)
+    for (int p = 0; p < P; ++p)
 #pragma unroll
         for (int t = 0; t < 8; ++t)
 #pragma unroll
@@ -665,10 +669,11 @@ __device__ __forceinline__ void mma_shift_down(MmaState<GC>& st, int g, int delt
 
 // RES = false: binary-only keys (the adaptive cache's second segment), the
 // sign part alone; the residual accumulators are left untouched.
-template <int D, int GC, typename Cfg, bool ENT = false, bool RES = true>
-__device__ __forceinline__ void consume_warp_tile_mma(const QState<D, GC>& qs, MmaState<GC>& st, const uint8_t* sb,
+template <int D, int GC, typename Cfg, bool ENT = false, bool RES = true, int P>
+__device__ __forceinline__ void consume_warp_tile_mma(const QState<D, GC>& qs, MmaState<GC, P>& st, const uint8_t* sb,
                                                       int kw, int nk, uint8_t* wb) {
     static_assert(D == 128 && GC <= 2, "tensor-core value phase: head_dim 128, at most two heads per CTA");
+    static_assert(!RES || P == 2, "the residual part needs its accumulators");
     const int lane = threadIdx.x & 31;
     const int kk = kw + lane;
     const bool valid = kk < nk;
@@ -741,7 +746,7 @@ __device__ __forceinline__ void consume_warp_tile_mma(const QState<D, GC>& qs, M
         }
     }
     // ---- residual part ---------------------------------------------------------
-    if constexpr (RES) {
+    if constexpr (RES && P == 2) {
         const uint8_t* vn = sb + Cfg::OFF_VNIB + ((kw + lane) >> 3) * (4 * D) + 16 * ((kw + lane) & 7);
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
@@ -924,7 +929,39 @@ __device__ __forceinline__ void warp_records(float* mg, SoftState<GC, Cfg::NP>& 
 // then rebuilds head g's values from its byte columns (0, 1) and those of
 // lane 2g + 1 (2, 3), rows g8 and g8 + 8, and owns the quad's 16 dims.
 template <int D, int GC, typename Cfg>
-__device__ __forceinline__ void warp_records(float* mg, MmaState<GC>& st) {
+__device__ __forceinline__ void warp_records(float* mg, MmaState<GC, 1>& st) {
+    // sign part only: read out from registers (lane 2g of each quad owns
+    // rows g8 / g8 + 8, i.e. dims 8 g8 + t / 64 + 8 g8 + t)
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, g8 = lane >> 2, q = lane & 3;
+#pragma unroll
+    for (int g = 0; g < GC; ++g) {
+        float l = st.l[g], t = st.t[g];
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) {
+            l += __shfl_xor_sync(0xffffffffu, l, off);
+            t += __shfl_xor_sync(0xffffffffu, t, off);
+        }
+        float* rec = mg + ((size_t)warp * GC + g) * (D + 2);
+        if (lane == 0) {
+            rec[0] = st.m[g];
+            rec[1] = l;
+        }
+        const float sc = (st.U[g] != kUUnset && st.m[g] > -INFINITY) ? exp2f((float)st.U[g] - st.m[g]) : 0.0f;
+#pragma unroll
+        for (int tt = 0; tt < 8; ++tt)
+#pragma unroll
+            for (int r = 0; r < 2; ++r) {
+                const uint64_t P0 = (uint64_t)(uint32_t)st.acc[0][tt][2 * r] +
+                                    ((uint64_t)(uint32_t)st.acc[0][tt][2 * r + 1] << 8);
+                const uint64_t P1 = __shfl_xor_sync(0xffffffffu, P0, 1);
+                if (q == 2 * g)
+                    rec[2 + 64 * r + 8 * g8 + tt] = ((float)P0 + 65536.0f * (float)P1) * sc * exp2i(-tt) - t;
+            }
+    }
+}
+
+template <int D, int GC, typename Cfg>
+__device__ __forceinline__ void warp_records(float* mg, MmaState<GC, 2>& st) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     int* dump = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(mg) + Cfg::DUMP_OFF) + warp * 32 * 65;
 #pragma unroll
@@ -1380,7 +1417,7 @@ __global__ void __launch_bounds__(kDecThreads, DecCfg<D, GC, COMP>::MIN_CTAS)
     // the tensor-core value phase (in adaptive caches the binary-only
     // segment runs its sign part alone)
     constexpr bool MMA = Cfg::MMA;
-    std::conditional_t<MMA, MmaState<GC>, SoftState<GC, Cfg::NP>> st;
+    std::conditional_t<MMA, MmaState<GC, COMP ? 2 : 1>, SoftState<GC, Cfg::NP>> st;
     init_soft(st);
 
     int it = 0;
@@ -1412,7 +1449,7 @@ __global__ void __launch_bounds__(kDecThreads, DecCfg<D, GC, COMP>::MIN_CTAS)
             if (ADA && seg_bin)
                 consume_warp_tile_mma<D, GC, Cfg, false, false>(qs, st, smem + stage * Cfg::STAGE_B, warp * 32, nk, wb);
             else
-                consume_warp_tile_mma<D, GC, Cfg, ENT>(qs, st, smem + stage * Cfg::STAGE_B, warp * 32, nk, wb);
+                consume_warp_tile_mma<D, GC, Cfg, ENT, COMP>(qs, st, smem + stage * Cfg::STAGE_B, warp * 32, nk, wb);
         } else {
             if (ADA && seg_bin)
                 consume_warp_tile<D, GC, false, Cfg>(qs, st, smem + stage * Cfg::STAGE_B, warp * 32, nk);
