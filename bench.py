@@ -492,7 +492,8 @@ def main():
 
     hbm, peak_kind = peaks()
     achieved = bytes_rank / (kern_ms * 1e-3) / 1e9
-    traffic = traffic_from_profiles(args.config, world)
+    # the committed summaries profile the compensated kernel of each workload
+    traffic = traffic_from_profiles(args.config, world) if comp else None
     value = bytes_total / (step_ms * 1e-3) / 1e9
 
     line = {

@@ -64,6 +64,9 @@ __device__ unsigned int g_bc_device_error = 0;
 #ifndef BC_DEC_MIN_CTAS_B1
 #define BC_DEC_MIN_CTAS_B1 5   // resident CTAs per SM the binary one-head kernel is held to
 #endif
+#ifndef BC_DEC_BIN_GC
+#define BC_DEC_BIN_GC 2        // most query heads per CTA in binary grouped-query caches (2: tensor-core value phase)
+#endif
 #ifndef BC_DEC_MIN_TILES
 #define BC_DEC_MIN_TILES 1     // fewest 128-key tiles a split is planned with
 #endif
@@ -1612,7 +1615,8 @@ struct Plan {
 // grid, share the KV tiles through L2.
 int heads_per_cta(int group, int d, bool comp) {
     (void)d;
-    const int cap = comp ? 2 : 4;  // accumulator registers: 32 per head (compensated), 16 (binary)
+    // accumulator registers: 32 per head (compensated), 16 (binary, f32x2)
+    const int cap = comp ? 2 : BC_DEC_BIN_GC;
     return group < cap ? group : cap;
 }
 

@@ -89,7 +89,8 @@ def test_c1_golden_vs_kernels(cuda):
 @pytest.mark.parametrize("d", [32, 64, 128, 256])
 @pytest.mark.parametrize("comp", [True, False])
 def test_gqa_vs_oracle(cuda, group, d, comp):
-    """Grouped-query heads: 2 (compensated) or 4 (binary) heads per CTA on 16-dim value lanes."""
+    """Grouped-query heads, two per CTA: the tensor-core value phase at d = 128
+    (heads as MMA columns), 16-dim f32x2 value lanes at the other head dims."""
     slots, S = 3, 700
     g = torch.Generator().manual_seed(group * 10 + d)
     q = (torch.randn(slots * group, d, generator=g) * 0.5).half()
