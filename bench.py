@@ -255,11 +255,18 @@ def main():
     mode = planes.MODE_COMPENSATED if comp else planes.MODE_BINARY
     res_mode = planes.RES_FP16_SCALE if comp else planes.RES_NONE
 
-    w = workloads.make(args.config, device=dev)
+    # Head sharding (the default) is weak scaling: heads are independent, so
+    # every rank holds a full config-sized shard of a global batch N times the
+    # config's (rank 0's data is the single-GPU workload) and no collective
+    # runs on the data path.  The sequence splits divide one config-sized
+    # workload across the ranks (strong scaling) and merge across GPUs.
+    weak = args.split == "heads"
+    w = workloads.make(args.config, device=dev,
+                       seed=None if (rank == 0 or not weak) else 1000 * rank + 7)
     S, d, G = w.seq_len, w.head_dim, w.group
     n_slots = w.n_slots
     if world > 1 and args.split == "heads":
-        a, b = bdist.slot_range(n_slots, world, rank)
+        a, b = 0, n_slots
         s_a, s_b = 0, S
     elif world > 1:
         a, b = 0, n_slots
@@ -282,6 +289,8 @@ def main():
     else:
         bytes_rank = workloads.step_cache_bytes(1, my_slots, my_S, d, comp)
         bytes_total = workloads.step_cache_bytes(w.batch, w.n_kv_heads, S, d, comp)
+    if weak:
+        bytes_total *= world
     # Inputs larger than L2: rotate through enough cache copies that one step's
     # data is evicted before it is read again.
     copies = max(1, math.ceil(3 * L2_BYTES / max(1, bytes_rank)))
@@ -499,13 +508,15 @@ def main():
     line = {
         "metric": "decode-attention cache GB/s", "value": value, "unit": "GB/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_ms, "us_per_step": step_ms * 1e3,
-        "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "higher_is_better": True, "scaling": "weak" if weak else "strong", "vs_baseline": None,
         "dtype": "u32 sign words, u8 INT4 codes, f32 accumulate (fp16 in/out)",
         "data": "synthetic (seeded torch generator, BASELINE config shapes)",
         "config": {"workload": f"{args.config}: B={w.batch} H={w.n_heads} Hkv={w.n_kv_heads} S={S} d={d} "
                                + (f"adaptive, residual kept for {keep_frac:.0%} of positions (compact layout)"
                                   if adaptive else ('compensated' if comp else 'binary')),
-                   "parallelism": (f"{args.split}-split x{world}" if world > 1 else "single GPU"),
+                   "parallelism": ((f"heads sharded x{world}: each rank a full {args.config} shard, "
+                                    f"global batch {world}x the config's" if weak else f"{args.split}-split x{world}")
+                                   if world > 1 else "single GPU"),
                    "l2": f"inputs larger than L2: {copies} rotating cache copies of {bytes_rank / 1e6:.1f} MB per rank",
                    "timing": "K steps back to back between two CUDA events (host queued ahead); "
                              "roofline kernel time = the timed region per launch (one launch per step), "

@@ -67,6 +67,9 @@ __device__ unsigned int g_bc_device_error = 0;
 #ifndef BC_DEC_BIN_GC
 #define BC_DEC_BIN_GC 2        // most query heads per CTA in binary grouped-query caches (2: tensor-core value phase)
 #endif
+#ifndef BC_DEC_KCOMB
+#define BC_DEC_KCOMB 8         // split partials each combining thread loads per L2 round trip
+#endif
 #ifndef BC_DEC_MIN_TILES
 #define BC_DEC_MIN_TILES 1     // fewest 128-key tiles a split is planned with
 #endif
@@ -1091,7 +1094,7 @@ __device__ __forceinline__ void finish_cta(const DecodeArgs& a, int slot, int hg
     // parallel.  Each thread loads kComb partials at once (m, l, float4 of o),
     // merges them into a running (M, L, O), and the SG group results are then
     // merged through shared memory (the ring, free by now).
-    constexpr int kComb = 8;
+    constexpr int kComb = BC_DEC_KCOMB;
     constexpr int TASKS = GC * D / 4;
     constexpr int SG = (TASKS >= kDecThreads) ? 1 : kDecThreads / TASKS;
     float* cmb = reinterpret_cast<float*>(smem);  // [SG][TASKS][6]
