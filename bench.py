@@ -184,7 +184,8 @@ def run_reference(args):
     line = {
         "impl": "reference", "metric": "decode-attention cache GB/s", "value": gbs, "unit": "GB/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
-        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "u32/u8 codes, f32 accumulate",
+        "higher_is_better": True, "scaling": "weak" if args.split == "heads" else "strong", "vs_baseline": None,
+        "dtype": "u32/u8 codes, f32 accumulate",
         "data": "synthetic (seeded torch generator)",
         "config": {"workload": f"{args.config}: B={w.batch} H={w.n_heads} Hkv={w.n_kv_heads} S={S} d={d} "
                                f"{'compensated' if comp else 'binary'}", "layout": "planes (host arrays)"},
