@@ -1082,13 +1082,19 @@ __device__ __forceinline__ void finish_cta(const DecodeArgs& a, int slot, int hg
     __shared__ unsigned s_last;
     __syncthreads();
     if (tid == 0) {
-        __threadfence();
-        const unsigned prev = atomicAdd(&a.ws_cnt[(int64_t)slot * a.n_hgroups + hg], 1u);
+        // acq_rel at GPU scope, instead of fences around a plain atomic: it
+        // releases this CTA's partial (written by all threads, ordered before
+        // this one by the barrier above) and, in the last CTA, acquires every
+        // other CTA's; the barrier below extends that to all its threads.
+        unsigned prev;
+        asm volatile("atom.add.acq_rel.gpu.u32 %0, [%1], 1;"
+                     : "=r"(prev)
+                     : "l"(&a.ws_cnt[(int64_t)slot * a.n_hgroups + hg])
+                     : "memory");
         s_last = (prev == (unsigned)(a.n_splits - 1)) ? 1u : 0u;
     }
     __syncthreads();
     if (!s_last) return;
-    __threadfence();
     // Split combine.  A task is (head, 4 dims); the threads left over split
     // the splits into SG interleaved groups, so several L2 round trips run in
     // parallel.  Each thread loads kComb partials at once (m, l, float4 of o),
