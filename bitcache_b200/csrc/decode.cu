@@ -1273,6 +1273,23 @@ __device__ __forceinline__ void patch_stage_row(uint8_t* sb, int kk, const uint8
     __syncwarp();
 }
 
+// Stage layout of the adaptive kernel's binary-only segment on the tensor-core
+// path: four 128-key tiles per ring stage (sign words and scales only, 18 KB
+// at head_dim 128), so a binary CTA keeps four times the bytes in flight.
+template <int D>
+struct BinStageCfg {
+    static constexpr int NWD = D / 32;
+    static constexpr int TILES = 4;
+    static constexpr int KEYS = TILES * kTile;
+    static constexpr int OFF_KSIGN = 0;
+    static constexpr int OFF_KBS = OFF_KSIGN + KEYS * D / 8;
+    static constexpr int OFF_VSIGN = OFF_KBS + KEYS * 2;
+    static constexpr int OFF_VBS = OFF_VSIGN + KEYS * D / 8;
+    static constexpr int BYTES = OFF_VBS + KEYS * 2;
+    static constexpr int OFF_KNIB = 0, OFF_KRS = 0, OFF_VNIB = 0, OFF_VRS = 0;  // no residual planes
+    static constexpr int WB_ROW = DecCfg<D, 1, true>::WB_ROW;
+};
+
 // ---------------------------------------------------------------------------
 // Plane-layout kernel.  Thread 0 keeps the ring full: at iteration `it` it
 // refills the stage consumed at iteration it-LAG once all four warps have
@@ -1314,7 +1331,13 @@ __global__ void __launch_bounds__(kDecThreads, DecCfg<D, GC, COMP>::MIN_CTAS)
         s_end = min(a.seq_len, s_begin + a.keys_per_split);
     }
     const int n_keys = max(0, s_end - s_begin);
-    const int n_tiles = (n_keys + T - 1) / T;
+    // keys per ring stage: one tile, or four in the binary segment of the
+    // adaptive kernel's tensor-core path
+    constexpr bool BIN4 = ADA && Cfg::MMA && D == 128;
+    if constexpr (BIN4) static_assert(BinStageCfg<D>::BYTES <= Cfg::STAGE_B, "binary stage exceeds the ring stage");
+    const bool wide = BIN4 && seg_bin;
+    const int TS = wide ? BinStageCfg<D>::KEYS : T;
+    const int n_tiles = (n_keys + TS - 1) / TS;
 
     // fused step: does this CTA's key range hold the append position?
     const bool appends = STEP && a.append_pos >= s_begin && a.append_pos < s_end;
@@ -1363,12 +1386,12 @@ __global__ void __launch_bounds__(kDecThreads, DecCfg<D, GC, COMP>::MIN_CTAS)
     // tile boundaries and pages hold a multiple of the tile's 128 positions.
     auto row_of = [&](int tile) -> int64_t {
         if constexpr (STEP) return plane_row(a, slot, s_begin + tile * T);
-        if constexpr (ADA) return (int64_t)slot * a.kv_stride + (seg_bin ? a.b0 : 0) + s_begin + tile * T;
+        if constexpr (ADA) return (int64_t)slot * a.kv_stride + (seg_bin ? a.b0 : 0) + s_begin + (int64_t)tile * TS;
         return (int64_t)slot * a.kv_stride + s_begin + tile * T;
     };
     auto issue = [&](int tile, int stage, int64_t row) {
-        const int k0 = tile * T;
-        const int nk = min(T, n_keys - k0);
+        const int k0 = tile * TS;
+        const int nk = min(TS, n_keys - k0);
         const int nk8 = (nk + 7) & ~7;
         if constexpr (STEP) {
             if (row < 0) {
@@ -1386,10 +1409,13 @@ __global__ void __launch_bounds__(kDecThreads, DecCfg<D, GC, COMP>::MIN_CTAS)
         // residual planes: their own row stride in adaptive caches
         const int64_t rrow = ADA ? (int64_t)slot * a.res_stride + s_begin + k0 : row;
         mbar_arrive_expect_tx(&full[stage], total);
-        bulk_g2s(sbuf + Cfg::OFF_KSIGN, (const uint8_t*)a.K.sign + row * (D / 8), sign_b, &full[stage]);
-        bulk_g2s(sbuf + Cfg::OFF_KBS, (const uint8_t*)a.K.bscale + row * 2, sc_b, &full[stage]);
-        bulk_g2s(sbuf + Cfg::OFF_VSIGN, (const uint8_t*)a.V.sign + row * (D / 8), sign_b, &full[stage]);
-        bulk_g2s(sbuf + Cfg::OFF_VBS, (const uint8_t*)a.V.bscale + row * 2, sc_b, &full[stage]);
+        using BS = BinStageCfg<D>;
+        bulk_g2s(sbuf + (wide ? BS::OFF_KSIGN : Cfg::OFF_KSIGN), (const uint8_t*)a.K.sign + row * (D / 8), sign_b,
+                 &full[stage]);
+        bulk_g2s(sbuf + (wide ? BS::OFF_KBS : Cfg::OFF_KBS), (const uint8_t*)a.K.bscale + row * 2, sc_b, &full[stage]);
+        bulk_g2s(sbuf + (wide ? BS::OFF_VSIGN : Cfg::OFF_VSIGN), (const uint8_t*)a.V.sign + row * (D / 8), sign_b,
+                 &full[stage]);
+        bulk_g2s(sbuf + (wide ? BS::OFF_VBS : Cfg::OFF_VBS), (const uint8_t*)a.V.bscale + row * 2, sc_b, &full[stage]);
         if (res) {
             bulk_g2s(sbuf + Cfg::OFF_KNIB, (const uint8_t*)a.K.nib + rrow * (D / 2), nib_b, &full[stage]);
             bulk_g2s(sbuf + Cfg::OFF_KRS, (const uint8_t*)a.K.rscale + rrow * 2, sc_b, &full[stage]);
@@ -1452,13 +1478,19 @@ __global__ void __launch_bounds__(kDecThreads, DecCfg<D, GC, COMP>::MIN_CTAS)
         bool ok = mbar_wait_bounded(&full[stage], (uint32_t)(it / NS) & 1u);
         if (!ok) *abort_flag = 1;
         if (*abort_flag) break;
-        const int nk = min(T, n_keys - it * T);
+        const int nk = min(TS, n_keys - it * TS);
         if constexpr (STEP) {
             if (it == patch_it) patch_stage_row<D, COMP, Cfg>(smem + stage * Cfg::STAGE_B, patch_kk, smem);
         }
         if constexpr (MMA) {
             uint8_t* wb = smem + Cfg::WB_OFF + warp * Cfg::WB_WARP;
-            if (ADA && seg_bin)
+            if (wide) {
+                if constexpr (BIN4) {
+                    for (int j = 0; j < BinStageCfg<D>::TILES && j * T < nk; ++j)
+                        consume_warp_tile_mma<D, GC, BinStageCfg<D>, false, false>(
+                            qs, st, smem + stage * Cfg::STAGE_B, j * T + warp * 32, nk, wb);
+                }
+            } else if (ADA && seg_bin)
                 consume_warp_tile_mma<D, GC, Cfg, false, false>(qs, st, smem + stage * Cfg::STAGE_B, warp * 32, nk, wb);
             else
                 consume_warp_tile_mma<D, GC, Cfg, ENT, COMP>(qs, st, smem + stage * Cfg::STAGE_B, warp * 32, nk, wb);
