@@ -70,6 +70,9 @@ __device__ unsigned int g_bc_device_error = 0;
 #ifndef BC_DEC_KCOMB
 #define BC_DEC_KCOMB 8         // split partials each combining thread loads per L2 round trip
 #endif
+#ifndef BC_DEC_BIN_TPS
+#define BC_DEC_BIN_TPS 4       // binary caches, tensor-core path: 128-key tiles per ring stage
+#endif
 #ifndef BC_DEC_MIN_TILES
 #define BC_DEC_MIN_TILES 1     // fewest 128-key tiles a split is planned with
 #endif
@@ -96,9 +99,14 @@ struct DecCfg {
     static constexpr int NS = (D == 256) ? 2 : BC_DEC_STAGES;  // ring stages
     static constexpr int LAG = 1;            // refill the stage consumed one tile ago
     static constexpr int T = kTile;
-    static constexpr int SIGN_B = T * D / 8;
+    // Binary caches on the tensor-core path stage TPS tiles per ring slot (a
+    // binary tile is only 4.6 KB at head_dim 128): attention and entropy
+    // stream that many per stage, the step and record kernels one.
+    static constexpr int TPS = (BC_DEC_MMA && D == 128 && GC <= 2 && !COMP) ? BC_DEC_BIN_TPS : 1;
+    static constexpr int KEYS = T * TPS;     // keys a stage can hold
+    static constexpr int SIGN_B = KEYS * D / 8;
     static constexpr int NIB_B = COMP ? T * D / 2 : 0;
-    static constexpr int SC_B = T * 2;
+    static constexpr int SC_B = KEYS * 2;
     static constexpr int OFF_KSIGN = 0;
     static constexpr int OFF_KBS = OFF_KSIGN + SIGN_B;
     static constexpr int OFF_KNIB = OFF_KBS + SC_B;
@@ -1336,7 +1344,7 @@ __global__ void __launch_bounds__(kDecThreads, DecCfg<D, GC, COMP>::MIN_CTAS)
     constexpr bool BIN4 = ADA && Cfg::MMA && D == 128;
     if constexpr (BIN4) static_assert(BinStageCfg<D>::BYTES <= Cfg::STAGE_B, "binary stage exceeds the ring stage");
     const bool wide = BIN4 && seg_bin;
-    const int TS = wide ? BinStageCfg<D>::KEYS : T;
+    const int TS = wide ? BinStageCfg<D>::KEYS : ((VAR == 0 || VAR == 2) ? Cfg::KEYS : T);
     const int n_tiles = (n_keys + TS - 1) / TS;
 
     // fused step: does this CTA's key range hold the append position?
@@ -1490,6 +1498,10 @@ __global__ void __launch_bounds__(kDecThreads, DecCfg<D, GC, COMP>::MIN_CTAS)
                         consume_warp_tile_mma<D, GC, BinStageCfg<D>, false, false>(
                             qs, st, smem + stage * Cfg::STAGE_B, j * T + warp * 32, nk, wb);
                 }
+            } else if (Cfg::TPS > 1 && TS > T) {
+                for (int j = 0; j < Cfg::TPS && j * T < nk; ++j)
+                    consume_warp_tile_mma<D, GC, Cfg, ENT, COMP>(qs, st, smem + stage * Cfg::STAGE_B, j * T + warp * 32,
+                                                                 nk, wb);
             } else if (ADA && seg_bin)
                 consume_warp_tile_mma<D, GC, Cfg, false, false>(qs, st, smem + stage * Cfg::STAGE_B, warp * 32, nk, wb);
             else
