@@ -214,16 +214,29 @@ def run_profile(args):
     planes.encode_planes(w.k.reshape(n, S, d), K, rm)
     planes.encode_planes(w.v.reshape(n, S, d), V, rm)
     q = w.q.reshape(-1, d).contiguous()
+    w_extra = dict(w.extra)
     del w
     torch.cuda.synchronize()
     torch.cuda.empty_cache()
     mode = planes.MODE_COMPENSATED if comp else planes.MODE_BINARY
     out = torch.empty((q.shape[0], d), dtype=torch.float16, device=dev)
-    for _ in range(args.warmup + args.steps):
-        planes.decode_attention(q, K, V, S, mode, out=out)
+    keep_frac = w_extra.get("keep") if (comp and args.config == "C5") else None
+    if keep_frac is not None:  # C5: the compact adaptive cache and its decode
+        n_keep = planes.keep_count(S, keep_frac)
+        keep = planes.select_positions_topk(K, V, S, n_keep)
+        K, V = planes.compact_adaptive(K, V, keep, S, n_keep)
+        del keep
+        torch.cuda.synchronize()
+        torch.cuda.empty_cache()
+        for _ in range(args.warmup + args.steps):
+            planes.decode_attention_adaptive(q, K, V, S, n_keep, out=out)
+        nbytes = workloads.adaptive_step_bytes(1, n, S, d, keep_frac)
+    else:
+        for _ in range(args.warmup + args.steps):
+            planes.decode_attention(q, K, V, S, mode, out=out)
+        nbytes = workloads.step_cache_bytes(1, n, S, d, comp)
     torch.cuda.synchronize()
-    print(json.dumps({"profile": args.config, "launches": args.warmup + args.steps,
-                      "bytes_per_launch": workloads.step_cache_bytes(1, n, S, d, comp)}))
+    print(json.dumps({"profile": args.config, "launches": args.warmup + args.steps, "bytes_per_launch": nbytes}))
 
 
 def main():
