@@ -73,6 +73,9 @@ __device__ unsigned int g_bc_device_error = 0;
 #ifndef BC_DEC_BIN_TPS
 #define BC_DEC_BIN_TPS 4       // binary caches, tensor-core path: 128-key tiles per ring stage
 #endif
+#ifndef BC_DEC_FILL
+#define BC_DEC_FILL 1          // plan several waves when one wave leaves CTA slots idle
+#endif
 #ifndef BC_DEC_MIN_TILES
 #define BC_DEC_MIN_TILES 1     // fewest 128-key tiles a split is planned with
 #endif
@@ -1687,6 +1690,24 @@ Plan make_plan(int n_slots, int group, int seq_len, int d, bool comp, int capaci
     int splits = 1;
     if (units < capacity) splits = (int)((int64_t)capacity * BC_DEC_WAVES / units);
     splits = max(1, min(splits, n_tiles / BC_DEC_MIN_TILES));
+    if (BC_DEC_FILL && comp && units < capacity && splits < n_tiles) {
+        // Compensated caches, where a CTA's split is long: when one wave
+        // leaves many CTA slots idle, take the split count of up to four
+        // waves whose last wave is fullest (C4: 278.6 against 297.5 us).
+        // Binary CTAs are short, and extra waves cost them more than idle
+        // slots (binary C4 105 against 97 us), so their plan stays one wave.
+        auto fill = [&](int sp) {
+            const int64_t ctas = units * sp;
+            const int64_t waves = (ctas + capacity - 1) / capacity;
+            return (double)ctas / (double)(waves * capacity);
+        };
+        if (fill(splits) < 0.93) {
+            int best = splits;
+            for (int sp = splits + 1; sp <= min(n_tiles, (int)(4 * (int64_t)capacity / units)); ++sp)
+                if (fill(sp) > fill(best) + 0.02) best = sp;
+            splits = best;
+        }
+    }
     // at most kMaxKeysPerSplit keys per CTA: the tensor-core value phase's
     // 32-bit accumulators take up to 32768 keys per warp
     splits = max(splits, (n_tiles * p.tile + kMaxKeysPerSplit - 1) / kMaxKeysPerSplit);
@@ -1711,7 +1732,13 @@ size_t ws_bound(int n_slots, int group, int seq_len, int d) {
     size_t best = 0;
     for (int comp = 0; comp < 2; ++comp) {
         const Plan p = make_plan(n_slots, group, seq_len, d, comp != 0, kMaxCtasPlan);
-        const size_t b = ws_bytes_for(n_slots, group, p.n_splits, d, group);
+        int splits = p.n_splits;
+        if (BC_DEC_FILL && comp) {  // the fill search may pick up to four waves of splits at any capacity
+            const int64_t units = (int64_t)n_slots * p.n_hgroups;
+            const int n_tiles = max(1, (seq_len + p.tile - 1) / p.tile);
+            if (units < kMaxCtasPlan) splits = max(splits, (int)std::min<int64_t>(n_tiles, 4 * (int64_t)kMaxCtasPlan / units));
+        }
+        const size_t b = ws_bytes_for(n_slots, group, splits, d, group);
         best = b > best ? b : best;
     }
     return best;
