@@ -8,15 +8,22 @@ algorithmic cache bytes 2*B*Hkv*S*82 (the reference README's 82-byte
 binary+INT4 footprint per vector at d=128), read once per step.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--config C1..C5] [--head-dim D] [--split auto|heads|seq|seqx]
 
-N > 1 (torchrun, one rank per GPU, NCCL): --split heads (default) shards the
-KV heads across ranks with no data-path collective; --split seq splits every
-head's positions across ranks and merges the per-rank log-sum-exp triples
-after an NCCL all-gather.  The total workload is fixed (strong scaling).
+N > 1 (torchrun, one rank per GPU): the configuration's workload is divided
+across the ranks (strong scaling; `value` is the whole job's GB/s, the
+per-GPU figure is `gbs_per_gpu`).  --split auto (the default) splits C3, the
+single-sequence configuration, along the sequence with the decode kernel's
+own peer-memory exchange of the per-rank log-sum-exp triples (seqx); the
+batched configurations shard their KV heads (heads, no data-path
+collective).  --split seq is the sequence split with an NCCL all-gather of
+the triples and a merge launch.
 
 --impl reference runs the reference algorithm on the host cores (the C
-restatement of the reference kernels under oracle/, OpenMP over heads; the
-reference ships no CPU code of its own) on the same workload, rank 0 only.
+restatement of the reference kernels under oracle/, OpenMP over query heads
+on every core of the host; the reference ships no CPU code of its own) on
+the same workload and config, rank 0 only.  It maps no library of the GPU
+path.
 """
 from __future__ import annotations
 
@@ -29,9 +36,6 @@ import statistics
 import subprocess
 import sys
 import time
-
-import numpy as np
-import torch
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
@@ -47,9 +51,11 @@ def parse():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", default="C3", choices=["C1", "C2", "C3", "C4", "C5"])
-    ap.add_argument("--split", default="heads", choices=["heads", "seq", "seqx"],
-                    help="N>1: shard heads, split the sequence with an NCCL all-gather + merge (seq), or split "
-                         "the sequence with the kernel's own peer-memory exchange (seqx)")
+    ap.add_argument("--head-dim", type=int, default=0, help="override the config's head_dim (C5 sweeps 64/128/256)")
+    ap.add_argument("--split", default="auto", choices=["auto", "heads", "seq", "seqx"],
+                    help="N>1: shard the KV heads (heads), split the sequence with an NCCL all-gather + merge (seq), "
+                         "or split the sequence with the kernel's own peer-memory exchange (seqx); auto: seqx for "
+                         "C3, heads otherwise")
     ap.add_argument("--binary", action="store_true", help="binary-only attention instead of compensated")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-ref-gpu", action="store_true")
@@ -61,6 +67,14 @@ def parse():
     return ap.parse_args()
 
 
+def resolve_split(args, world: int) -> str:
+    if world <= 1:
+        return "none"
+    if args.split != "auto":
+        return args.split
+    return "seqx" if args.config == "C3" else "heads"
+
+
 def peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
@@ -70,13 +84,37 @@ def peaks():
     return FALLBACK_HBM_GBS, "fallback"
 
 
-def traffic_from_profiles(workload: str, world: int) -> float | None:
-    """Per-launch DRAM bytes from the committed ncu summary of this workload, if any."""
-    p = os.path.join(ROOT, "profiles", f"decode_planes_{workload}.md")
-    if not os.path.exists(p) or world != 1:
-        return None
-    m = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)", open(p).read())
-    return float(m.group(1)) if m else None
+def workload_overrides(args) -> dict:
+    return {"head_dim": args.head_dim} if args.head_dim else {}
+
+
+def host_threads() -> int:
+    """Every core this process may run on (torchrun sets OMP_NUM_THREADS=1 per rank)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:  # pragma: no cover
+        return os.cpu_count() or 1
+
+
+def traffic_from_profiles(workload: str, head_dim: int, comp: bool, bytes_rank: float) -> tuple[float | None, str]:
+    """Per-launch DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of this
+    workload's kernel from the committed ncu summary, scaled to this run's
+    per-rank cache bytes (the kernel reads each vector once, so traffic grows
+    in proportion).  Returns (bytes or None, where it came from)."""
+    name = f"decode_planes_{workload}" + ("" if comp else "_binary") + ("" if head_dim in (0, 128) else f"_d{head_dim}")
+    p = os.path.join(ROOT, "profiles", name + ".md")
+    if not os.path.exists(p):
+        return None, "no committed ncu summary for this workload"
+    txt = open(p).read()
+    m = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)", txt)
+    mb = re.search(r"profiled_cache_bytes_per_launch:\s*([0-9.eE+]+)", txt)
+    if not m:
+        return None, f"profiles/{name}.md has no traffic line"
+    t = float(m.group(1))
+    if mb:
+        t *= bytes_rank / float(mb.group(1))
+    return t, (f"ncu capture of the same kernel and workload (profiles/{name}.md), not measured by this run"
+               + ("; scaled to this rank's cache bytes" if mb else ""))
 
 
 class ClockSampler:
@@ -126,16 +164,82 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------------------
+# The job: workload shape, per-rank partition, bytes, and the config dict
+# (identical in both arms: built from the arguments and the shape alone)
+# ---------------------------------------------------------------------------
+class Job:
+    def __init__(self, args, world: int, rank: int):
+        from bitcache_b200 import dist as bdist
+        from bitcache_b200 import planes, workloads
+
+        cfg = dict(workloads.CONFIGS[args.config])
+        cfg.update(workload_overrides(args))
+        self.cfg_name = args.config
+        self.batch, self.n_heads, self.n_kv_heads = cfg["batch"], cfg["n_heads"], cfg["n_kv_heads"]
+        self.S, self.d = cfg["seq_len"], cfg["head_dim"]
+        self.G = self.n_heads // self.n_kv_heads
+        self.n_slots = self.batch * self.n_kv_heads
+        self.comp = not args.binary
+        self.world, self.rank = world, rank
+        self.split = resolve_split(args, world)
+        self.keep_frac = cfg.get("keep") if (self.comp and args.config == "C5") else None
+        self.adaptive = self.keep_frac is not None
+        if self.split == "heads":
+            self.a, self.b = bdist.slot_range(self.n_slots, world, rank)
+            self.s_a, self.s_b = 0, self.S
+        elif self.split in ("seq", "seqx"):
+            self.a, self.b = 0, self.n_slots
+            self.s_a, self.s_b = bdist.seq_range(self.S, world, rank)
+        else:
+            self.a, self.b, self.s_a, self.s_b = 0, self.n_slots, 0, self.S
+        self.my_slots, self.my_S = self.b - self.a, self.s_b - self.s_a
+        self.stride = planes.round_stride(self.my_S)
+        self.n_keep = planes.keep_count(self.my_S, self.keep_frac) if self.adaptive else self.my_S
+        d = self.d
+        if self.adaptive:
+            self.bytes_rank = workloads.adaptive_step_bytes(1, self.my_slots, self.my_S, d, self.keep_frac)
+            self.bytes_total = workloads.adaptive_step_bytes(self.batch, self.n_kv_heads, self.S, d, self.keep_frac)
+        else:
+            self.bytes_rank = workloads.step_cache_bytes(1, self.my_slots, self.my_S, d, self.comp)
+            self.bytes_total = workloads.step_cache_bytes(self.batch, self.n_kv_heads, self.S, d, self.comp)
+        # Inputs larger than L2: enough rotating cache copies that one step's
+        # data is evicted before it is read again.
+        self.copies = max(1, math.ceil(3 * L2_BYTES / max(1, self.bytes_rank)))
+        self.bytes_per_vector = ((self.bytes_total / (2 * self.batch * self.n_kv_heads * self.S)) if self.adaptive
+                                 else workloads.vector_footprint(d, self.comp))
+        self.stored_bytes_per_vector = planes.vector_bytes(d, self.comp)
+
+    def workload_str(self) -> str:
+        kind = (f"adaptive, residual kept for {self.keep_frac:.0%} of positions (compact layout)" if self.adaptive
+                else ("compensated" if self.comp else "binary"))
+        return (f"{self.cfg_name}: B={self.batch} H={self.n_heads} Hkv={self.n_kv_heads} S={self.S} d={self.d} "
+                f"{kind}")
+
+    def config(self) -> dict:
+        if self.split == "none":
+            par = "single GPU"
+        elif self.split == "heads":
+            par = f"KV heads sharded across {self.world} GPUs (no data-path collective)"
+        elif self.split == "seqx":
+            par = (f"sequence split across {self.world} GPUs, per-rank (m, l, o) triples exchanged and merged by "
+                   f"the decode kernel over peer memory")
+        else:
+            par = f"sequence split across {self.world} GPUs, NCCL all-gather of (m, l, o) + merge launch"
+        return {"workload": self.workload_str(), "parallelism": par,
+                "l2": f"inputs larger than L2: {self.copies} rotating cache copies of "
+                      f"{self.bytes_rank / 1e6:.1f} MB per rank",
+                "bytes_per_vector": self.bytes_per_vector, "stored_bytes_per_vector": self.stored_bytes_per_vector}
+
+
+# ---------------------------------------------------------------------------
 # Reference arm: the reference algorithm on the host cores
 # ---------------------------------------------------------------------------
-def cpu_workload_planes(cfg: str, heads: int | None = None):
+def cpu_workload_planes(cfg: str, overrides: dict):
     """Workload on the host, encoded by the C oracle (no GPU kernels involved)."""
     from bitcache_b200 import workloads
     from oracle import oracle as O
 
-    w = workloads.make(cfg, device="cpu")
-    if heads is not None:
-        w.k, w.v, w.q = w.k[:, :heads], w.v[:, :heads], w.q[:, :heads]
+    w = workloads.make(cfg, device="cpu", **overrides)
     n_slots = w.k.shape[0] * w.k.shape[1]
     S, d = w.seq_len, w.head_dim
 
@@ -165,32 +269,27 @@ def run_reference(args):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if rank != 0:
         return
-    from bitcache_b200 import workloads
-    from oracle import oracle as O
-
-    comp = not args.binary
-    w, q, K, V = cpu_workload_planes(args.config)
-    threads = O.num_threads()
-    S, d = w.seq_len, w.head_dim
+    job = Job(args, world, 0)
+    comp = job.comp
+    w, q, K, V = cpu_workload_planes(args.config, workload_overrides(args))
+    threads = host_threads()
+    S = w.seq_len
     used = min(threads, q.shape[0])  # the port parallelises over query heads
-    bytes_step = workloads.step_cache_bytes(w.batch, w.n_kv_heads, S, d, comp)
-    if comp and args.config == "C5":  # adaptive config: the same byte model as our arm
-        bytes_step = workloads.adaptive_step_bytes(w.batch, w.n_kv_heads, S, d, w.extra.get("keep", 0.25))
     for _ in range(max(0, args.warmup)):
         time_cpu_steps(q, K, V, w.group, S, comp, 1, threads)
     t = time_cpu_steps(q, K, V, w.group, S, comp, args.steps, threads)
     ms = t * 1e3 / args.steps
-    gbs = bytes_step / (ms * 1e-3) / 1e9
+    gbs = job.bytes_total / (ms * 1e-3) / 1e9
     line = {
         "impl": "reference", "metric": "decode-attention cache GB/s", "value": gbs, "unit": "GB/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
-        "higher_is_better": True, "scaling": "weak" if args.split == "heads" else "strong", "vs_baseline": None,
-        "dtype": "u32/u8 codes, f32 accumulate",
-        "data": "synthetic (seeded torch generator)",
-        "config": {"workload": f"{args.config}: B={w.batch} H={w.n_heads} Hkv={w.n_kv_heads} S={S} d={d} "
-                               f"{'compensated' if comp else 'binary'}", "layout": "planes (host arrays)"},
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "u32 sign words, u8 INT4 codes, f32 accumulate (fp16 in/out)",
+        "data": "synthetic (seeded torch generator, BASELINE config shapes)",
+        "config": job.config(),
         "cpu_baseline": {"value": gbs, "unit": "GB/s", "cores": used, "kind": "port",
-                         "sample": f"{args.steps} full decode steps of {args.config} (all heads, all positions)"},
+                         "sample": f"{args.steps} full decode steps of {args.config} (all heads, all positions) on "
+                                   f"rank 0's host, OpenMP over {q.shape[0]} query heads with {threads} threads"},
         "e2e": {"value": gbs, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -202,11 +301,16 @@ def run_reference(args):
 def run_profile(args):
     """Minimal run for ncu: one cache copy of the workload (> L2), fp16 inputs freed,
     then warmup + steps launches of the decode kernel and nothing else."""
+    import torch
+
     from bitcache_b200 import planes, workloads
 
     dev = torch.device("cuda", 0)
     comp = not args.binary
-    w = workloads.make(args.config, device=dev, **({"seq_len": args.profile_seq} if args.profile_seq else {}))
+    over = workload_overrides(args)
+    if args.profile_seq:
+        over["seq_len"] = args.profile_seq
+    w = workloads.make(args.config, device=dev, **over)
     S, d, n = w.seq_len, w.head_dim, w.n_slots
     K = planes.Planes.empty(n, planes.round_stride(S), d, comp, dev, zero=False)
     V = planes.Planes.empty(n, planes.round_stride(S), d, comp, dev, zero=False)
@@ -248,6 +352,8 @@ def main():
         run_profile(args)
         return
 
+    import torch
+
     from bitcache_b200 import BitCache, _lib, planes, workloads
     from bitcache_b200 import dist as bdist
 
@@ -265,49 +371,19 @@ def main():
         os.environ.setdefault("NCCL_DEBUG", "WARN")  # keep rank 0's stdout to the one JSON line
         tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
         pg = tdist
-    comp = not args.binary
+    job = Job(args, world, rank)
+    comp, d, G, S = job.comp, job.d, job.G, job.S
     mode = planes.MODE_COMPENSATED if comp else planes.MODE_BINARY
     res_mode = planes.RES_FP16_SCALE if comp else planes.RES_NONE
 
-    # Head sharding (the default) is weak scaling: heads are independent, so
-    # every rank holds a full config-sized shard of a global batch N times the
-    # config's (rank 0's data is the single-GPU workload) and no collective
-    # runs on the data path.  The sequence splits divide one config-sized
-    # workload across the ranks (strong scaling) and merge across GPUs.
-    weak = args.split == "heads"
-    w = workloads.make(args.config, device=dev,
-                       seed=None if (rank == 0 or not weak) else 1000 * rank + 7)
-    S, d, G = w.seq_len, w.head_dim, w.group
-    n_slots = w.n_slots
-    if world > 1 and args.split == "heads":
-        a, b = 0, n_slots
-        s_a, s_b = 0, S
-    elif world > 1:
-        a, b = 0, n_slots
-        s_a, s_b = bdist.seq_range(S, world, rank)
-    else:
-        a, b, s_a, s_b = 0, n_slots, 0, S
-    my_slots, my_S = b - a, s_b - s_a
-    k_all = w.k.reshape(n_slots, S, d)[a:b, s_a:s_b].contiguous()
-    v_all = w.v.reshape(n_slots, S, d)[a:b, s_a:s_b].contiguous()
-    q_all = w.q.reshape(n_slots * G, d)[a * G:b * G].contiguous()
-    stride = planes.round_stride(my_S)
-    # C5 is the adaptive-precision config: the residual is kept for a fraction of
-    # the positions (compact layout, unkept residuals neither stored nor read)
-    keep_frac = w.extra.get("keep") if (comp and args.config == "C5") else None
-    adaptive = keep_frac is not None
-    n_keep = planes.keep_count(my_S, keep_frac) if adaptive else my_S
-    if adaptive:
-        bytes_rank = workloads.adaptive_step_bytes(1, my_slots, my_S, d, keep_frac)
-        bytes_total = workloads.adaptive_step_bytes(w.batch, w.n_kv_heads, S, d, keep_frac)
-    else:
-        bytes_rank = workloads.step_cache_bytes(1, my_slots, my_S, d, comp)
-        bytes_total = workloads.step_cache_bytes(w.batch, w.n_kv_heads, S, d, comp)
-    if weak:
-        bytes_total *= world
-    # Inputs larger than L2: rotate through enough cache copies that one step's
-    # data is evicted before it is read again.
-    copies = max(1, math.ceil(3 * L2_BYTES / max(1, bytes_rank)))
+    # One workload (same seed on every rank); each rank keeps its share.
+    w = workloads.make(args.config, device=dev, **workload_overrides(args))
+    a, b, s_a, s_b = job.a, job.b, job.s_a, job.s_b
+    my_slots, my_S, stride = job.my_slots, job.my_S, job.stride
+    k_all = w.k.reshape(job.n_slots, S, d)[a:b, s_a:s_b].contiguous()
+    v_all = w.v.reshape(job.n_slots, S, d)[a:b, s_a:s_b].contiguous()
+    q_all = w.q.reshape(job.n_slots * G, d)[a * G:b * G].contiguous()
+    adaptive, n_keep, copies = job.adaptive, job.n_keep, job.copies
     Ks, Vs = [], []
     for _ in range(copies):
         K = planes.Planes.empty(my_slots, stride, d, comp, dev, zero=False)
@@ -324,49 +400,62 @@ def main():
     torch.cuda.synchronize()
     out = torch.empty((my_slots * G, d), dtype=torch.float16, device=dev)
     part = torch.empty((my_slots * G, d + 2), dtype=torch.float32, device=dev)
-    seq_split = world > 1 and args.split == "seq"
-    xchg = bdist.PeerExchange(my_slots * G, d) if (world > 1 and args.split == "seqx") else None
+    seq_split = job.split == "seq"
+    xchg = bdist.PeerExchange(my_slots * G, d) if job.split == "seqx" else None
 
-    def step(i):
+    def step(i, qq=q_all, o=out):
         K, V = Ks[i % copies], Vs[i % copies]
         if adaptive:
-            planes.decode_attention_adaptive(q_all, K, V, my_S, n_keep, out=out)
+            planes.decode_attention_adaptive(qq, K, V, my_S, n_keep, out=o)
         elif xchg is not None:
-            xchg.decode(q_all, K, V, my_S, mode, out=out)
+            xchg.decode(qq, K, V, my_S, mode, out=o)
         elif seq_split:
-            planes.decode_attention(q_all, K, V, my_S, mode, partial=part, want_out=False)
+            planes.decode_attention(qq, K, V, my_S, mode, partial=part, want_out=False)
         else:
-            planes.decode_attention(q_all, K, V, my_S, mode, out=out)
+            planes.decode_attention(qq, K, V, my_S, mode, out=o)
 
     gather = bdist.nccl_all_gather() if seq_split else None
 
-    def full_step(i):
-        step(i)
+    def full_step(i, qq=q_all, o=out):
+        step(i, qq, o)
         if seq_split:
-            planes.lse_merge(gather(part), out=out)
+            planes.lse_merge(gather(part), out=o)
 
     def barrier():
         if pg is not None:
             pg.barrier()
 
-    for i in range(max(3, args.warmup)):
+    def agreed_max(x: float) -> float:
+        """The largest value of x over the ranks (every rank gets the same)."""
+        if pg is None:
+            return x
+        t = torch.tensor([x], device=dev, dtype=torch.float64)
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        return float(t[0])
+
+    stream = torch.cuda.current_stream(dev)
+    n_warm = max(3, args.warmup)
+    t0 = time.perf_counter()
+    for i in range(n_warm):
         full_step(i)
     torch.cuda.synchronize()
     barrier()
+    # Every rank must run the same number of steps (the sequence splits wait
+    # for all ranks inside each step), so the busy-loop length is agreed once.
+    per_step_s = agreed_max((time.perf_counter() - t0) / n_warm)
+    n_busy = max(50, int(0.6 / max(per_step_s, 1e-6)))
+    n_tail = max(50, int(0.4 / max(per_step_s, 1e-6)))
+    i = n_warm
 
     # clocks sampled over a busy window that contains the timed region
     sampler = ClockSampler(local)
     sampler.start()
-    t_busy = time.perf_counter()
-    i = 0
-    while time.perf_counter() - t_busy < 0.6:
-        for _ in range(50):
-            full_step(i)
-            i += 1
-        torch.cuda.synchronize()
+    for j in range(n_busy):
+        full_step(i + j)
+    i += n_busy
+    torch.cuda.synchronize()
     barrier()
     torch.cuda.synchronize()
-    stream = torch.cuda.current_stream(dev)
     # Timed region: K steps back to back on the stream.  The GPU first runs a
     # short spin (outside the region) so that the host has queued the steps
     # before they start; consecutive decode launches then overlap their
@@ -394,19 +483,14 @@ def main():
     torch.cuda.synchronize()
     barrier()
     i += args.steps
-    t_busy = time.perf_counter()
-    while time.perf_counter() - t_busy < 0.4:
-        for _ in range(50):
-            full_step(i)
-            i += 1
-        torch.cuda.synchronize()
+    for j in range(n_tail):
+        full_step(i + j)
+    i += n_tail
+    torch.cuda.synchronize()
     clocks = sampler.stop()
     iso_ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends)) / args.steps
     step_ms = tot0.elapsed_time(tot1) / args.steps
-    if pg is not None:
-        t = torch.tensor([step_ms, iso_ms], device=dev, dtype=torch.float64)
-        pg.all_reduce(t, op=pg.ReduceOp.MAX)
-        step_ms, iso_ms = float(t[0]), float(t[1])
+    step_ms, iso_ms = agreed_max(step_ms), agreed_max(iso_ms)
     # The kernel's average launch duration: over the timed region when each
     # step is that one launch (its duration there matches ncu's per-launch
     # gpu__time_duration); with a separate merge launch per step, the
@@ -416,43 +500,29 @@ def main():
 
     # ---- end to end through the public API (pinned host buffers) ----------
     e2e = None
-    if adaptive:
-        # adaptive cache (snapshot after selection): pinned host Q in, output out
+    if adaptive or job.split in ("seq", "seqx"):
+        # pinned host Q in, merged output out, the decode on the device
         qh = q_all.cpu().pin_memory()
         oh = torch.empty(q_all.shape, dtype=torch.float16).pin_memory()
         qd = torch.empty_like(q_all)
-        Kc, Vc = Ks[0], Vs[0]
+        od = torch.empty_like(out)
 
-        def e2e_step():
+        def e2e_step(j):
             qd.copy_(qh, non_blocking=True)
-            o = planes.decode_attention_adaptive(qd, Kc, Vc, my_S, n_keep)
-            oh.copy_(o, non_blocking=True)
+            full_step(j, qd, od)
+            oh.copy_(od, non_blocking=True)
 
-        for _ in range(max(3, args.warmup)):
-            e2e_step()
-        torch.cuda.synchronize()
-        barrier()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        for _ in range(args.steps):
-            e2e_step()
-        e1.record(stream)
-        torch.cuda.synchronize()
-        barrier()
-        e2e_ms = e0.elapsed_time(e1) / args.steps
-        if pg is not None:
-            t = torch.tensor([e2e_ms], device=dev, dtype=torch.float64)
-            pg.all_reduce(t, op=pg.ReduceOp.MAX)
-            e2e_ms = float(t[0])
-        e2e = {"value": bytes_total / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s", "ms_per_step": e2e_ms,
-               "h2d_bytes_per_step": qh.numel() * 2 * world, "d2h_bytes_per_step": oh.numel() * 2 * world,
-               "path": "planes.decode_attention_adaptive on the compact cache, pinned host Q in, output out",
-               "gpu_launches_per_step": 1}
-    elif world == 1 or args.split == "heads":
-        cache = BitCache(w.batch if world == 1 else 1, my_slots * G if world > 1 else w.n_heads, d, max_seq=my_S,
-                         device=str(dev), compensated=comp, n_kv_heads=my_slots if world > 1 else w.n_kv_heads)
-        cache.prefill(k_all.view(cache.batch, cache.n_kv_heads, my_S, d), v_all.view(cache.batch, cache.n_kv_heads, my_S, d))
-        del k_all, v_all
+        path = ("planes.decode_attention_adaptive on the compact cache" if adaptive
+                else "dist.PeerExchange.decode (one launch per rank)" if xchg is not None
+                else "planes.decode_attention + NCCL all-gather + planes.lse_merge")
+        path += ", pinned host Q copied in and the output copied out every step"
+        h2d, d2h = qh.numel() * 2 * world, oh.numel() * 2 * world
+    else:
+        cache = BitCache(1 if world > 1 else job.batch, my_slots * G if world > 1 else job.n_heads, d,
+                         max_seq=my_S, device=str(dev), compensated=comp,
+                         n_kv_heads=my_slots if world > 1 else job.n_kv_heads)
+        cache.prefill(k_all.view(cache.batch, cache.n_kv_heads, my_S, d),
+                      v_all.view(cache.batch, cache.n_kv_heads, my_S, d))
         # Pinned host Q, K, V and output: the fused step kernel reads the inputs
         # and writes the output over the host link itself (one launch per step).
         nq, nkv = cache.batch * cache.n_heads * d, cache.batch * cache.n_kv_heads * d
@@ -464,39 +534,37 @@ def main():
         kh = host_in[nq:nq + nkv].view(cache.batch, cache.n_kv_heads, d)
         vh = host_in[nq + nkv:].view(cache.batch, cache.n_kv_heads, d)
 
-        def e2e_step():
+        def e2e_step(j):
             cache.step(qh, kh, vh, out=oh)  # append + attend, one launch, host operands
 
-        for _ in range(max(3, args.warmup)):
-            e2e_step()
-        torch.cuda.synchronize()
-        barrier()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        for _ in range(args.steps):
-            e2e_step()
-        e1.record(stream)
-        torch.cuda.synchronize()
-        barrier()
-        e2e_ms = e0.elapsed_time(e1) / args.steps
-        if pg is not None:
-            t = torch.tensor([e2e_ms], device=dev, dtype=torch.float64)
-            pg.all_reduce(t, op=pg.ReduceOp.MAX)
-            e2e_ms = float(t[0])
-        h2d = host_in.numel() * 2 * world
-        d2h = oh.numel() * 2 * world
-        # the cache in the e2e leg is one copy: its reads may partly hit L2 when it is small
-        e2e = {"value": bytes_total / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s", "ms_per_step": e2e_ms,
-               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-               "path": "BitCache.step (fused append + attend, one launch) on pinned host Q/K/V and output, "
-                       "which the kernel reads and writes over the host link",
-               "gpu_launches_per_step": 1}
+        path = ("BitCache.step (fused append + attend, one launch) on pinned host Q/K/V and output, which the "
+                "kernel reads and writes over the host link")
+        h2d, d2h = host_in.numel() * 2 * world, oh.numel() * 2 * world
+    del k_all, v_all
+    for j in range(n_warm):
+        e2e_step(i + j)
+    i += n_warm
+    torch.cuda.synchronize()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for j in range(args.steps):
+        e2e_step(i + j)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    i += args.steps
+    e2e_ms = agreed_max(e0.elapsed_time(e1) / args.steps)
+    assert _lib.device_error() == 0, "device-side timeout during the end-to-end leg"
+    e2e = {"value": job.bytes_total / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s", "ms_per_step": e2e_ms,
+           "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "path": path,
+           "gpu_launches_per_step": 2 if seq_split else 1}
 
     # ---- prefill encode throughput (fused binary + INT4 residual into planes) ----
     prefill = None
     if rank == 0:
         Kp = planes.Planes.empty(my_slots, stride, d, comp, dev, zero=False)
-        src = w.k.reshape(n_slots, S, d)[a:b, s_a:s_b].contiguous()
+        src = w.k.reshape(job.n_slots, S, d)[a:b, s_a:s_b].contiguous()
         for _ in range(3):
             planes.encode_planes(src, Kp, res_mode)
         p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -509,40 +577,32 @@ def main():
         enc_ms = p0.elapsed_time(p1) / n_enc
         enc_bytes = src.numel() * 2 + my_slots * my_S * planes.vector_bytes(d, comp)
         prefill = {"value": enc_bytes / (enc_ms * 1e-3) / 1e9, "unit": "GB/s", "ms": enc_ms,
-                   "vectors": my_slots * my_S, "bytes": enc_bytes, "kernel": "k_encode_planes",
+                   "vectors": my_slots * my_S, "bytes": enc_bytes, "kernel": "k_encode_planes_lpv",
                    "frac": enc_bytes / (enc_ms * 1e-3) / 1e9 / peaks()[0]}
         del Kp, src
 
     hbm, peak_kind = peaks()
-    achieved = bytes_rank / (kern_ms * 1e-3) / 1e9
-    # the committed summaries profile the compensated kernel of each workload
-    traffic = traffic_from_profiles(args.config, world) if comp else None
-    value = bytes_total / (step_ms * 1e-3) / 1e9
+    achieved = job.bytes_rank / (kern_ms * 1e-3) / 1e9
+    traffic, traffic_src = traffic_from_profiles(args.config, args.head_dim, comp, job.bytes_rank)
+    value = job.bytes_total / (step_ms * 1e-3) / 1e9
 
     line = {
         "metric": "decode-attention cache GB/s", "value": value, "unit": "GB/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_ms, "us_per_step": step_ms * 1e3,
-        "higher_is_better": True, "scaling": "weak" if weak else "strong", "vs_baseline": None,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
         "dtype": "u32 sign words, u8 INT4 codes, f32 accumulate (fp16 in/out)",
         "data": "synthetic (seeded torch generator, BASELINE config shapes)",
-        "config": {"workload": f"{args.config}: B={w.batch} H={w.n_heads} Hkv={w.n_kv_heads} S={S} d={d} "
-                               + (f"adaptive, residual kept for {keep_frac:.0%} of positions (compact layout)"
-                                  if adaptive else ('compensated' if comp else 'binary')),
-                   "parallelism": ((f"heads sharded x{world}: each rank a full {args.config} shard, "
-                                    f"global batch {world}x the config's" if weak else f"{args.split}-split x{world}")
-                                   if world > 1 else "single GPU"),
-                   "l2": f"inputs larger than L2: {copies} rotating cache copies of {bytes_rank / 1e6:.1f} MB per rank",
-                   "timing": "K steps back to back between two CUDA events (host queued ahead); "
-                             "roofline kernel time = the timed region per launch (one launch per step), "
-                             "isolated_launch_us from a second pass with events around each launch",
-                   "bytes_per_vector": (bytes_total / (2 * w.batch * w.n_kv_heads * S)) if adaptive
-                   else workloads.vector_footprint(d, comp),
-                   "stored_bytes_per_vector": planes.vector_bytes(d, comp)},
+        "config": job.config(),
+        "timing": "K steps back to back between two CUDA events on the launching stream (host queued ahead), "
+                  "max over ranks; roofline kernel time = the timed region per launch (one launch per step), "
+                  "isolated_launch_us from a second pass with events around each launch",
+        "gbs_per_gpu": value / world,
         "pct_of_hbm_peak": 100.0 * value / world / hbm,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
-                     "peak_kind": peak_kind, "traffic": traffic, "kernel": "k_decode_planes",
-                     "kernel_us": kern_ms * 1e3, "isolated_launch_us": iso_ms * 1e3, "achieved_84B": achieved * planes.vector_bytes(d, comp) /
-                     workloads.vector_footprint(d, comp)},
+                     "peak_kind": peak_kind, "traffic": traffic, "traffic_source": traffic_src,
+                     "kernel": "k_decode_planes", "kernel_us": kern_ms * 1e3, "isolated_launch_us": iso_ms * 1e3,
+                     "bytes_per_launch": job.bytes_rank,
+                     "achieved_stored_bytes": achieved * job.stored_bytes_per_vector / job.bytes_per_vector},
         "clocks": clocks,
         "gpu_launches": args.steps * (2 if seq_split else 1),
         "e2e": e2e,
@@ -550,9 +610,9 @@ def main():
     }
 
     if rank == 0 and world == 1 and not args.no_ref_gpu:
-        line["ref_gpu"] = reference_gpu(w, comp, dev, bytes_total)
+        line["ref_gpu"] = reference_gpu(w, comp, job.bytes_total)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_baseline(args, comp, bytes_total)
+        line["cpu_baseline"] = cpu_baseline(args, comp, job.bytes_total)
     if rank == 0:
         print(json.dumps(line), flush=True)
     if xchg is not None:
@@ -562,15 +622,18 @@ def main():
         pg.destroy_process_group()
 
 
-def reference_gpu(w, comp, dev, bytes_total):
+def reference_gpu(w, comp, bytes_total):
     """The reference's own CUDA kernel (recompiled for sm_100a) on the same workload, record format."""
+    import torch
+
     try:
-        from bitcache_b200 import _C
         from oracle import refgpu
     except Exception as e:  # pragma: no cover
         return {"unavailable": str(e)}
     if not refgpu.available():
         return {"unavailable": "oracle/_ref not built"}
+    if w.group != 1:
+        return {"unavailable": "the reference kernels have no grouped-query heads"}
     d, H = w.head_dim, w.n_slots
     S = w.seq_len
     k = w.k.reshape(-1, d)
@@ -595,17 +658,16 @@ def reference_gpu(w, comp, dev, bytes_total):
 
 
 def cpu_baseline(args, comp, bytes_total):
-    from oracle import oracle as O
-
-    w, q, K, V = cpu_workload_planes(args.config)
-    threads = O.num_threads()
+    w, q, K, V = cpu_workload_planes(args.config, workload_overrides(args))
+    threads = host_threads()
     t1 = time_cpu_steps(q, K, V, w.group, w.seq_len, comp, 1, threads)
     n = max(1, int(args.cpu_sample_s / max(t1, 1e-3)))
     t = time_cpu_steps(q, K, V, w.group, w.seq_len, comp, n, threads)
     ms = t * 1e3 / n
     return {"value": bytes_total / (ms * 1e-3) / 1e9, "unit": "GB/s", "ms_per_step": ms,
             "cores": min(threads, q.shape[0]),
-            "kind": "port", "sample": f"{n} full decode steps of {args.config} on the host (OpenMP over heads)"}
+            "kind": "port", "sample": f"{n} full decode steps of {args.config} on the host "
+                                      f"(OpenMP over {q.shape[0]} query heads, {threads} threads)"}
 
 
 if __name__ == "__main__":

@@ -162,3 +162,7 @@ def adaptive_select(entropy: torch.Tensor, threshold: float) -> torch.Tensor:
     _lib.check(_lib.load().bc_adaptive_select(entropy.data_ptr(), modes.data_ptr(), 1, n, float(threshold),
                                               _stream(entropy)), "adaptive_select")
     return modes
+
+
+__all__ = ["sizeof_binary_vec", "sizeof_residual_vec", "binary_encode", "residual_encode", "binary_attention",
+           "compensated_attention", "online_encode_token", "compute_head_entropy", "adaptive_select"]

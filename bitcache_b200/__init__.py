@@ -13,7 +13,15 @@ from torch import Tensor
 
 from . import _lib
 
-_HAS_EXTENSION = _lib.available()
+
+def __getattr__(name: str):
+    # _HAS_EXTENSION (reference bitcache/__init__.py:14-19) is evaluated on
+    # first use: importing the package (e.g. for its workload generators) maps
+    # no native code; every operator loads the library and fails loudly when
+    # it is missing.
+    if name == "_HAS_EXTENSION":
+        return _lib.available()
+    raise AttributeError(f"module {__name__!r} has no attribute {name!r}")
 
 
 def _require_extension() -> None:

@@ -44,10 +44,11 @@ class PageTable(ctypes.Structure):
 
 
 class Xchg(ctypes.Structure):
-    """bc_xchg: every rank's exchange buffer as mapped here, world, rank, epoch."""
+    """bc_xchg: every rank's exchange buffer as mapped here, world, rank, epoch, the
+    poll limit of one exchange word (0: the library default) and the buffers' size."""
 
     _fields_ = [("bufs", c_void_p * 8), ("world", ctypes.c_int32), ("rank", ctypes.c_int32),
-                ("epoch", ctypes.c_uint32)]
+                ("epoch", ctypes.c_uint32), ("spin_limit", ctypes.c_uint32), ("buf_bytes", ctypes.c_uint64)]
 
 
 _SIGS = {

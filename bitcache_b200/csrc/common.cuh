@@ -169,6 +169,14 @@ __device__ __forceinline__ uint4 ldg_nc_v4(const void* p) {
 // in decode.cu), for kernels of other translation units.
 unsigned int* bc_device_error_ptr();
 
+// Record-layout attention for the C++ launchers (decode.cu): split-K scratch
+// in a fixed 4 MiB array of the library instead of a caller workspace, with
+// fewer splits when the partials would not fit.  Calls that overlap on the GPU
+// share that array and race.  Allocates nothing.
+int bc_record_attention_fixed_scratch(const void* q, const void* k_bin, const void* k_res, const void* v_bin,
+                                      const void* v_res, void* out, int batch, int n_heads, int seq_len, int head_dim,
+                                      bool compensated, void* stream);
+
 // ---------------------------------------------------------------------------
 // Host-side helpers shared by the entry points.
 // ---------------------------------------------------------------------------

@@ -34,6 +34,8 @@
 // (pattern * 2^-149) of packed fma.rn.f32x2 with one coefficient per key;
 // each accumulator carries the fixed power-of-two scale of its bit position,
 // removed once per CTA together with the constant parts sum_s (a_s + 8 c_s).
+#include <cuda.h>
+
 #include <type_traits>
 #include <cstring>
 #include <mutex>
@@ -192,6 +194,7 @@ struct DecodeArgs {
     unsigned long long* xparts[8];  // rank j's buffer as mapped here: [2 parities][xw][n_heads][d+2]
     int xw, xrank;
     unsigned xepoch;
+    unsigned xspin;  // polls of one exchange word before the CTA gives up
 };
 
 // Plane row of logical position `pos` of `slot`, or -1 for a page id outside
@@ -673,9 +676,9 @@ __device__ __forceinline__ void mma_shift_down(MmaState<GC, P>& st, int g, int d
         for (int t = 0; t < 8; ++t)
 #pragma unroll
             for (int r = 0; r < 2; ++r) {
-                const uint64_t P = (uint64_t)(uint32_t)st.acc[p][t][2 * r] + ((uint64_t)(uint32_t)st.acc[p][t][2 * r + 1] << 8);
-                const uint64_t Pn = __shfl_xor_sync(0xffffffffu, P, 1);
-                const uint64_t lo = upper ? Pn : P, hi = upper ? P : Pn;
+                const uint64_t v = (uint64_t)(uint32_t)st.acc[p][t][2 * r] + ((uint64_t)(uint32_t)st.acc[p][t][2 * r + 1] << 8);
+                const uint64_t vn = __shfl_xor_sync(0xffffffffu, v, 1);
+                const uint64_t lo = upper ? vn : v, hi = upper ? v : vn;
                 const uint64_t T = delta >= 63 ? 0 : (lo + (hi << 16)) >> delta;
                 if (mine) {
                     st.acc[p][t][2 * r] = (int)(upper ? (T >> 16) & 0xFFu : T & 0xFFu);
@@ -844,8 +847,6 @@ __device__ __forceinline__ void emit_final(const DecodeArgs& a, int64_t h, int i
 // the xw partials.  Words carry the call's epoch and are compared as "at
 // least"; partials alternate between two parity halves, so a rank that is a
 // step ahead writes the other half and never overwrites data still read.
-constexpr uint32_t kXchgSpinLimit = 1u << 22;  // polls (then 256 ns sleeps): about a second
-
 template <int D, int GC>
 __device__ __forceinline__ void xchg_finish(const DecodeArgs& a, int slot, int hg) {
     const int tid = threadIdx.x;
@@ -855,11 +856,16 @@ __device__ __forceinline__ void xchg_finish(const DecodeArgs& a, int slot, int h
     __shared__ int s_timeout;
     if (tid == 0) s_timeout = 0;
     __syncthreads();
+    volatile int* gave_up = &s_timeout;
+    // One word, polled at most a.xspin times (after 4096 fast polls with
+    // 256 ns sleeps).  Once any thread of the CTA has given up, every other
+    // poll returns at once, so a missing rank costs one spin limit per CTA,
+    // not one per word.
     auto wait_word = [&](const unsigned long long* p) -> float {
         unsigned long long v = ld_relaxed_sys_u64(p);
         for (uint32_t it = 0; (int)((unsigned)(v >> 32) - a.xepoch) < 0; ++it) {
-            if (it >= kXchgSpinLimit) {
-                s_timeout = 1;
+            if (it >= a.xspin || *gave_up) {
+                *gave_up = 1;
                 return 0.0f;
             }
             if (it >= 4096) __nanosleep(256);  // back off only after a few microseconds
@@ -1368,8 +1374,10 @@ __global__ void __launch_bounds__(kDecThreads, DecCfg<D, GC, COMP>::MIN_CTAS)
             }
         }
     };
-    // Inputs in pinned host memory cannot be written by the previous kernel in
-    // the stream: their (slow, host-link) reads start before waiting for it.
+    // Host-resident inputs are read before this kernel waits for the previous
+    // one in the stream, so no earlier GPU work in the stream may write them
+    // (the host synchronises before it rewrites them).  Their slow host-link
+    // reads then overlap the previous kernel's tail.
     const bool q_host = STEP && (a.host_in & 1), kv_host = STEP && (a.host_in & 2);
     bool staged = false;
     if (q_host) staged = prefetch_query<D, GC, Cfg>(a, slot, hg, smem);
@@ -1853,8 +1861,10 @@ void plan_adaptive(DecodeArgs& a, int gc, int capacity) {
     a.n_hgroups = n_hgroups;
 }
 
+// fit_ws: take fewer splits than planned when their partials would not fit
+// in ws_bytes (the C++ launchers, whose scratch is a fixed array).
 template <int D, int GC, bool COMP>
-int run_decode_t(DecodeArgs a, int var, void* ws, size_t ws_bytes, cudaStream_t st) {
+int run_decode_t(DecodeArgs a, int var, void* ws, size_t ws_bytes, cudaStream_t st, bool fit_ws) {
     const int cap = min(capacity_of<D, GC, COMP>(var), kMaxCtasPlan);
     if (var == kVarAdaptive) {
         plan_adaptive(a, GC, cap);
@@ -1863,6 +1873,18 @@ int run_decode_t(DecodeArgs a, int var, void* ws, size_t ws_bytes, cudaStream_t 
         a.n_splits = p.n_splits;
         a.keys_per_split = p.keys_per_split;
         a.n_hgroups = p.n_hgroups;
+        if (fit_ws) {
+            const int n_tiles = max(1, (a.seq_len + kTile - 1) / kTile);
+            for (int sp = a.n_splits; a.n_splits > 1 && ws_bytes_for(a.n_slots, a.group, a.n_splits, D, a.n_hgroups) >
+                                                          ws_bytes;) {
+                sp = min(sp, a.n_splits) - 1;
+                a.keys_per_split = ((n_tiles + sp - 1) / sp) * kTile;
+                a.n_splits = max(1, (max(a.seq_len, 1) + a.keys_per_split - 1) / a.keys_per_split);
+            }
+            // the tensor-core value phase's accumulators bound the keys per CTA
+            if (var != kVarRecords && DecCfg<D, GC, COMP>::MMA && a.keys_per_split > kMaxKeysPerSplit)
+                return BC_ERR_TOO_LARGE;
+        }
     }
     Plan p{a.n_splits, a.keys_per_split, a.n_hgroups, GC, kTile};
     if (p.n_splits > 1) {
@@ -1886,44 +1908,110 @@ int run_decode_t(DecodeArgs a, int var, void* ws, size_t ws_bytes, cudaStream_t 
 }
 
 template <int D>
-int run_decode_d(const DecodeArgs& a, bool comp, int var, void* ws, size_t wsb, cudaStream_t st) {
+int run_decode_d(const DecodeArgs& a, bool comp, int var, void* ws, size_t wsb, cudaStream_t st, bool fit) {
     switch (heads_per_cta(a.group, D, comp)) {
         case 1:
-            return comp ? run_decode_t<D, 1, true>(a, var, ws, wsb, st) : run_decode_t<D, 1, false>(a, var, ws, wsb, st);
+            return comp ? run_decode_t<D, 1, true>(a, var, ws, wsb, st, fit)
+                        : run_decode_t<D, 1, false>(a, var, ws, wsb, st, fit);
         case 2:
-            return comp ? run_decode_t<D, 2, true>(a, var, ws, wsb, st) : run_decode_t<D, 2, false>(a, var, ws, wsb, st);
+            return comp ? run_decode_t<D, 2, true>(a, var, ws, wsb, st, fit)
+                        : run_decode_t<D, 2, false>(a, var, ws, wsb, st, fit);
         default:
-            return run_decode_t<D, 4, false>(a, var, ws, wsb, st);
+            return run_decode_t<D, 4, false>(a, var, ws, wsb, st, fit);
     }
 }
 
-int run_decode(const DecodeArgs& a, bool comp, int var, void* ws, size_t wsb, cudaStream_t st) {
+int run_decode(const DecodeArgs& a, bool comp, int var, void* ws, size_t wsb, cudaStream_t st, bool fit = false) {
     switch (a.head_dim) {
-        case 32: return run_decode_d<32>(a, comp, var, ws, wsb, st);
-        case 64: return run_decode_d<64>(a, comp, var, ws, wsb, st);
-        case 128: return run_decode_d<128>(a, comp, var, ws, wsb, st);
-        case 256: return run_decode_d<256>(a, comp, var, ws, wsb, st);
+        case 32: return run_decode_d<32>(a, comp, var, ws, wsb, st, fit);
+        case 64: return run_decode_d<64>(a, comp, var, ws, wsb, st, fit);
+        case 128: return run_decode_d<128>(a, comp, var, ws, wsb, st, fit);
+        case 256: return run_decode_d<256>(a, comp, var, ws, wsb, st, fit);
         default: return BC_ERR_UNSUPPORTED;
     }
 }
 
 bool valid_group(int g) { return g == 1 || g == 2 || g == 4 || g == 8; }
 
+// Default poll limit of an exchange word: 4096 fast polls, then 256 ns
+// sleeps, about a second in all.
+constexpr uint32_t kXchgSpinLimit = 1u << 22;
+
+}  // namespace
+
+namespace {
+
+// Identity of the CUDA context current on this thread, unique for the life
+// of the process (cuCtxGetCurrent and cuCtxGetId, reached through the
+// runtime's driver entry points so the library does not link libcuda
+// itself); 0 when no context is current or the entry points are missing.
+unsigned long long current_context_id() {
+    using GetCurrent = CUresult (*)(CUcontext*);
+    using GetId = CUresult (*)(CUcontext, unsigned long long*);
+    static GetCurrent get_current = nullptr;
+    static GetId get_id = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get_current = reinterpret_cast<GetCurrent>(p);
+        p = nullptr;
+        if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get_id = reinterpret_cast<GetId>(p);
+    });
+    if (!get_current || !get_id) return 0;
+    CUcontext c = nullptr;
+    if (get_current(&c) != CUDA_SUCCESS || c == nullptr) return 0;
+    unsigned long long id = 0;
+    return get_id(c, &id) == CUDA_SUCCESS ? id : 0;
+}
+
+// Device address of a __device__ variable of this library on the current
+// device.  In host code the variable's name is only a host-side stand-in, so
+// the address is looked up with cudaGetSymbolAddress (with the device
+// current) and cached per device together with the context it belongs to: a
+// new context on the device (after cudaDeviceReset, say) reloads the module
+// at another address, and the lookup is then made again.
+struct SymbolAddressCache {
+    static constexpr int kMaxDev = 64;
+    std::mutex mu;
+    void* addr[kMaxDev] = {};
+    unsigned long long ctx[kMaxDev] = {};
+};
+
+int cached_symbol_address(SymbolAddressCache& c, const void* symbol, void** out) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return BC_ERR_CUDA_BASE + (int)e;
+    if (dev < 0 || dev >= SymbolAddressCache::kMaxDev) return BC_ERR_UNSUPPORTED;
+    std::lock_guard<std::mutex> lock(c.mu);
+    const unsigned long long id = current_context_id();
+    if (c.addr[dev] != nullptr && id != 0 && c.ctx[dev] == id) {
+        *out = c.addr[dev];
+        return BC_OK;
+    }
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, symbol);  // also makes the device's primary context current
+    if (e != cudaSuccess) return BC_ERR_CUDA_BASE + (int)e;
+    c.addr[dev] = p;
+    c.ctx[dev] = current_context_id();
+    *out = p;
+    return BC_OK;
+}
+
+SymbolAddressCache g_error_word_addr;
+
 }  // namespace
 
 // Device address of the library's error word, for kernels compiled in other
-// translation units (looked up once per device).
+// translation units (null when the lookup fails).
 unsigned int* bc_device_error_ptr() {
-    constexpr int kMaxDev = 64;
-    static unsigned int* ptrs[kMaxDev] = {};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev < 0 || dev >= kMaxDev) return nullptr;
-    if (!ptrs[dev]) {
-        void* p = nullptr;
-        if (cudaGetSymbolAddress(&p, g_bc_device_error) == cudaSuccess) ptrs[dev] = static_cast<unsigned int*>(p);
-    }
-    return ptrs[dev];
+    void* p = nullptr;
+    return cached_symbol_address(g_error_word_addr, &g_bc_device_error, &p) == BC_OK ? static_cast<unsigned int*>(p)
+                                                                                      : nullptr;
 }
 
 extern "C" {
@@ -2045,6 +2133,10 @@ int bc_decode_attention_xchg(const void* q, bc_kv_planes K, bc_kv_planes V, void
     const int rc = check_decode_args(q, K, V, out, nullptr, n_slots, group, seq_len, kv_stride, head_dim, mode);
     if (rc != BC_OK || n_slots == 0) return rc;
     if (!out || x.world < 1 || x.world > 8 || x.rank < 0 || x.rank >= x.world || x.epoch == 0) return BC_ERR_ARG;
+    // Every rank's buffer must hold both parity halves of this call's triples:
+    // the kernel stores into all of them and reads its own.
+    const uint64_t need = (uint64_t)2 * x.world * ((uint64_t)n_slots * group) * (head_dim + 2) * 8;
+    if (x.buf_bytes < need) return BC_ERR_ARG;
     DecodeArgs a = decode_args(q, K, V, out, nullptr, n_slots, group, seq_len, kv_stride, head_dim);
     for (int j = 0; j < x.world; ++j) {
         if (!x.bufs[j] || !bc_aligned(x.bufs[j], 256)) return BC_ERR_ARG;
@@ -2053,6 +2145,7 @@ int bc_decode_attention_xchg(const void* q, bc_kv_planes K, bc_kv_planes V, void
     a.xw = x.world;
     a.xrank = x.rank;
     a.xepoch = x.epoch;
+    a.xspin = x.spin_limit ? x.spin_limit : kXchgSpinLimit;
     return run_decode(a, mode == BC_MODE_COMPENSATED, kVarPlanes, workspace, workspace_bytes, (cudaStream_t)stream);
 }
 
@@ -2123,7 +2216,9 @@ int host_inputs(const void* q, const void* new_k, const void* new_v, const void*
     };
     const int kq = kind(q), kk = kind(new_k), kv = kind(new_v), ko = kind(out);
     if (kq < 0 || kk < 0 || kv < 0 || ko < 0) return -1;
-    return (kq ? 1 : 0) | ((kk || kv) ? 2 : 0);
+    // The new rows are read early only when both are host-resident: a device
+    // row may still be written by the kernel queued ahead of this one.
+    return (kq ? 1 : 0) | ((kk && kv) ? 2 : 0);
 }
 }  // namespace
 
@@ -2192,6 +2287,22 @@ int bc_decode_step_paged(const void* q, const void* new_k, const void* new_v, bc
     return run_decode(a, mode == BC_MODE_COMPENSATED, kVarStep, workspace, workspace_bytes, (cudaStream_t)stream);
 }
 
+}  // extern "C"
+
+// Scratch of the C++ record launchers (launch_binary_attention,
+// launch_compensated_attention).  The reference's launchers take no workspace
+// and allocate nothing (compensated_attention.cu:111-134), so their
+// replacements keep the split-K partials in a fixed array of the library
+// (every GPU that loads the library holds it until exit) and plan fewer
+// splits for shapes whose partials would not fit.
+namespace {
+constexpr size_t kLauncherScratchBytes = size_t(4) << 20;  // 4 MiB
+static __device__ __align__(256) unsigned char g_bc_launcher_scratch[kLauncherScratchBytes];
+SymbolAddressCache g_launcher_scratch_addr;
+}  // namespace
+
+extern "C" {
+
 size_t bc_attention_workspace_bytes(int batch, int n_heads, int seq_len, int head_dim) {
     if (batch <= 0 || n_heads <= 0) return 0;
     return bc_decode_workspace_bytes(batch * n_heads, 1, seq_len, head_dim);
@@ -2199,7 +2310,7 @@ size_t bc_attention_workspace_bytes(int batch, int n_heads, int seq_len, int hea
 
 static int record_attention(const void* q, const void* kb, const void* kr, const void* vb, const void* vr, void* out,
                             int batch, int n_heads, int seq_len, int head_dim, bool comp, void* ws, size_t wsb,
-                            void* stream) {
+                            void* stream, bool fixed_scratch = false) {
     if (!bc_valid_head_dim(head_dim)) return BC_ERR_HEAD_DIM;
     if (head_dim != 32 && head_dim != 64 && head_dim != 128 && head_dim != 256) return BC_ERR_UNSUPPORTED;
     if (batch < 0 || n_heads < 0 || seq_len < 0) return BC_ERR_ARG;
@@ -2221,8 +2332,19 @@ static int record_attention(const void* q, const void* kb, const void* kr, const
     a.seq_len = seq_len;
     a.kv_stride = seq_len;
     a.head_dim = head_dim;
-    return run_decode(a, comp, kVarRecords, ws, wsb, (cudaStream_t)stream);
+    if (fixed_scratch) {
+        const int rc = cached_symbol_address(g_launcher_scratch_addr, g_bc_launcher_scratch, &ws);
+        if (rc != BC_OK) return rc;
+        wsb = kLauncherScratchBytes;
+        // The ticket counters (one per head: one head per CTA here) must start
+        // at zero; the array keeps whatever the previous call left there.
+        const cudaError_t e = cudaMemsetAsync(ws, 0, (size_t)n * sizeof(unsigned), (cudaStream_t)stream);
+        if (e != cudaSuccess) return BC_ERR_CUDA_BASE + (int)e;
+    }
+    return run_decode(a, comp, kVarRecords, ws, wsb, (cudaStream_t)stream, fixed_scratch);
 }
+
+
 
 int bc_binary_attention(const void* q, const void* k_bin, const void* v_bin, void* out, int batch, int n_heads,
                         int seq_len, int head_dim, void* workspace, size_t workspace_bytes, void* stream) {
@@ -2264,6 +2386,13 @@ int bc_xnor_popcount(const void* q, const void* k_sign, int32_t* out, int n_slot
 
 }  // extern "C"
 
+int bc_record_attention_fixed_scratch(const void* q, const void* k_bin, const void* k_res, const void* v_bin,
+                                      const void* v_res, void* out, int batch, int n_heads, int seq_len, int head_dim,
+                                      bool compensated, void* stream) {
+    return record_attention(q, k_bin, k_res, v_bin, v_res, out, batch, n_heads, seq_len, head_dim, compensated,
+                            nullptr, 0, stream, true);
+}
+
 // ===========================================================================
 // Allocation-free decode attention.
 //
@@ -2281,27 +2410,14 @@ namespace {
 constexpr size_t kStaticScratchBytes = size_t(4) << 20;  // 4 MiB
 static __device__ __align__(256) unsigned char g_bc_static_scratch[kStaticScratchBytes];
 
-constexpr int kStaticMaxDevices = 64;
-std::mutex g_static_mu;
-void* g_static_scratch_addr[kStaticMaxDevices] = {};
+SymbolAddressCache g_static_scratch_addr;
 
 // Device address of the array on the current device.  In host code the
-// array's name is only a host-side stand-in, so the address is looked up once
-// per device (with that device current) and cached.
+// array's name is only a host-side stand-in, so the address is looked up
+// (with the device current) on the first call on each device and cached;
+// the lookup is made again when the device has a new context.
 int static_scratch_address(void** addr) {
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
-    if (e != cudaSuccess) return BC_ERR_CUDA_BASE + (int)e;
-    if (dev < 0 || dev >= kStaticMaxDevices) return BC_ERR_UNSUPPORTED;
-    std::lock_guard<std::mutex> lock(g_static_mu);
-    if (g_static_scratch_addr[dev] == nullptr) {
-        void* p = nullptr;
-        e = cudaGetSymbolAddress(&p, g_bc_static_scratch);
-        if (e != cudaSuccess) return BC_ERR_CUDA_BASE + (int)e;
-        g_static_scratch_addr[dev] = p;
-    }
-    *addr = g_static_scratch_addr[dev];
-    return BC_OK;
+    return cached_symbol_address(g_static_scratch_addr, g_bc_static_scratch, addr);
 }
 
 }  // namespace

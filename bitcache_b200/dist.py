@@ -14,8 +14,9 @@ unchanged over NCCL on GPUs and over gloo on CPU in the tests.
 
 PeerExchange is the fused alternative for the sequence split: the decode
 kernel itself stores each head's triple into every rank's buffer over
-NVLink, raises a flag there and merges on arrival (bc_decode_attention_xchg),
-so a step is one launch per rank with no separate collective or merge.
+NVLink as 64-bit (value, epoch) words and merges once every word it needs
+carries the call's epoch (bc_decode_attention_xchg), so a step is one launch
+per rank with no separate collective or merge.
 """
 from __future__ import annotations
 
@@ -103,7 +104,7 @@ class PeerExchange:
     world size 1 (no process group) the buffer is only this rank's own.
     """
 
-    def __init__(self, n_heads: int, head_dim: int, group=None) -> None:
+    def __init__(self, n_heads: int, head_dim: int, group=None, spin_limit: int = 0) -> None:
         import ctypes
 
         from . import _lib
@@ -141,6 +142,9 @@ class PeerExchange:
         for j, b in enumerate(bufs):
             self._x.bufs[j] = b
         self._x.world, self._x.rank, self._x.epoch = self.world, self.rank, 0
+        # polls of one exchange word before the kernel gives up (0: about a second)
+        self._x.spin_limit = spin_limit
+        self._x.buf_bytes = nbytes
 
     def decode(self, q: torch.Tensor, K, V, seq_len: int, mode: int, out: torch.Tensor | None = None) -> torch.Tensor:
         """One sequence-split decode step: this rank's slice [K, V] of every slot,
@@ -150,6 +154,14 @@ class PeerExchange:
         n_heads = q.numel() // d
         n_slots = K.n_slots
         group = n_heads // n_slots
+        # the exchange buffers were sized for (n_heads, head_dim) of __init__;
+        # every rank stores into every other rank's buffer, so a larger call
+        # would write past the end of a peer's buffer
+        if n_heads != self.n_heads or d != self.head_dim:
+            raise RuntimeError(f"PeerExchange built for {self.n_heads} heads of dim {self.head_dim}, "
+                               f"called with {n_heads} heads of dim {d}")
+        if group * n_slots != n_heads:
+            raise RuntimeError("number of query heads must be a multiple of the number of KV slots")
         if out is None:
             out = torch.empty((n_heads, d), dtype=torch.float16, device=q.device)
         st = self._lib.stream_of(q.device)

@@ -60,3 +60,7 @@ def sizeof_residual_vec() -> int:
     """Size in bytes of one ResidualVec record (functional.py:136-139): 130."""
     _require_extension()
     return _C.sizeof_residual_vec()
+
+
+__all__ = ["encode", "compute_residual", "binary_attention", "compensated_attention", "sizeof_binary_vec",
+           "sizeof_residual_vec"]

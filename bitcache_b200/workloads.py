@@ -53,11 +53,15 @@ def _normal(shape, std: float, g: torch.Generator, device) -> torch.Tensor:
 
 
 def _student_t5(shape, g: torch.Generator, device) -> torch.Tensor:
+    # z / sqrt(chi2_5 / 5), in place so that at most three full-size fp32
+    # tensors are alive (C5 at head_dim 256 is 4.3 G elements per tensor)
     z = torch.randn(shape, generator=g, device=device, dtype=torch.float32)
     chi2 = torch.zeros(shape, device=device, dtype=torch.float32)
     for _ in range(5):
-        chi2 += torch.randn(shape, generator=g, device=device, dtype=torch.float32) ** 2
-    return z / torch.sqrt(chi2 / 5.0)
+        t = torch.randn(shape, generator=g, device=device, dtype=torch.float32)
+        chi2 += t.square_()
+        del t
+    return z.div_(chi2.div_(5.0).sqrt_())
 
 
 def make(name: str, device: str | torch.device = "cpu", seed: int | None = None, **over) -> Workload:
@@ -74,8 +78,8 @@ def make(name: str, device: str | torch.device = "cpu", seed: int | None = None,
     if name == "C5":
         q = _normal((b, hq, d), std, g, device)
         scale = math.sqrt(3.0 / (5.0 * d))
-        k = _student_t5((b, hkv, s, d), g, device) * scale
-        v = _student_t5((b, hkv, s, d), g, device) * scale
+        k = _student_t5((b, hkv, s, d), g, device).mul_(scale).half()
+        v = _student_t5((b, hkv, s, d), g, device).mul_(scale).half()
         extra["keep"] = cfg.get("keep", 0.25)
     else:
         q = _normal((b, hq, d), std, g, device)

@@ -254,17 +254,25 @@ int bc_decode_attention_adaptive(const void* q, bc_kv_planes K, bc_kv_planes V, 
  * rank's exchange buffer over NVLink (plain peer stores of 64-bit words that
  * carry the value and the call's epoch, so no fence or flag is needed), waits
  * until every word it needs in its own buffer carries the epoch (a bounded
- * spin: BC_DEVERR_TIMEOUT after about a second) and merges the world triples
- * itself, so one launch per rank yields the full output on every rank.  Setup (allocates, outside the decode loop): bc_xchg_alloc on every
- * rank, share the 64-byte bc_ipc_handle of each buffer, bc_ipc_open the
- * peers' handles.  Every rank calls bc_decode_attention_xchg with the same
- * n_slots, group, head_dim and epoch (1, 2, 3, ...: one per call); ranks run
- * on different GPUs.  No counterpart in the reference. */
+ * spin of spin_limit polls per word: BC_DEVERR_TIMEOUT after about a second
+ * by default) and merges the world triples itself, so one launch per rank
+ * yields the full output on every rank.  Setup (allocates, outside the decode
+ * loop): bc_xchg_alloc on every rank, share the 64-byte bc_ipc_handle of each
+ * buffer, bc_ipc_open the peers' handles.  Every rank calls
+ * bc_decode_attention_xchg with the same n_slots, group, head_dim and epoch
+ * (1, 2, 3, ...: one per call); ranks run on different GPUs.  A call whose
+ * n_slots*group heads of head_dim do not fit buf_bytes returns BC_ERR_ARG.
+ * Recovery after BC_DEVERR_TIMEOUT (a rank that never published): the output
+ * of that call is invalid; clear the error (bc_get_device_error(1)), zero the
+ * workspace, and continue with the next epoch once every rank is back.
+ * No counterpart in the reference. */
 typedef struct bc_xchg {
-    void* bufs[8];  /* rank j's exchange buffer as mapped in this process (bufs[rank] = own) */
-    int32_t world;  /* 1..8 */
+    void* bufs[8];       /* rank j's exchange buffer as mapped in this process (bufs[rank] = own) */
+    int32_t world;       /* 1..8 */
     int32_t rank;
-    uint32_t epoch; /* call number, from 1, equal on every rank */
+    uint32_t epoch;      /* call number, from 1, equal on every rank */
+    uint32_t spin_limit; /* polls of one word before the wait gives up; 0 = default (about a second) */
+    uint64_t buf_bytes;  /* bytes of each rank's buffer (all equal; bc_xchg_bytes at allocation) */
 } bc_xchg;
 size_t bc_xchg_bytes(int n_heads, int head_dim, int world);
 int bc_xchg_alloc(size_t bytes, void** buf);          /* cudaMalloc + zero fill */
@@ -286,7 +294,8 @@ int bc_decode_attention_xchg(const void* q, bc_kv_planes K, bc_kv_planes V, void
  * library, held by every GPU that loads it until the process exits.  Shapes
  * whose bc_decode_workspace_bytes() exceeds that return BC_ERR_TOO_LARGE.
  * The first call on a device looks up the array's device address (with that
- * device current), so make it before any stream capture.  All calls on a
+ * device current), so make it before any stream capture; the lookup is made
+ * again when the device has a new context (after cudaDeviceReset).  All calls on a
  * device share the array: calls that overlap on the GPU (concurrent streams)
  * race and must be serialised by the caller.  Calls nothing that allocates. */
 size_t bc_decode_noalloc_max_scratch_bytes(void);

@@ -11,9 +11,12 @@
 //    a failed launch is reported through bc_last_status() instead of aborting.
 //  - The attention launchers guard batch*n_heads (the reference kernels need
 //    every buffer padded to a multiple of 32 rows).
-//  - The attention launchers draw their split-K scratch from the stream-ordered
-//    allocator (cudaMallocAsync/cudaFreeAsync on the given stream); the C ABI
-//    variants take a caller workspace instead.
+//  - Like the reference's, no launcher allocates.  The attention launchers keep
+//    their split-K partials in a fixed 4 MiB array inside the library (held by
+//    every GPU that loads it until exit) and plan fewer splits for shapes whose
+//    partials would not fit.  Attention launches that overlap on the GPU
+//    (concurrent streams) share that array and race: serialise them, or use
+//    the C ABI variants, which take a caller workspace.
 #pragma once
 
 #include <cuda_fp16.h>

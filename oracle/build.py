@@ -5,12 +5,14 @@
   reference's expressions term by term.
 * ``oracle/_ref/libbitcache_ref.so``: the reference's own CUDA kernels,
   compiled for sm_100a from their sources where they lie (the reference
-  checkout, ``BITCACHE_REF_SRC`` or ``/root/reference/src``) with the
+  checkout's ``src/``, named by ``BITCACHE_REF_SRC`` or, as its root, by
+  ``BITCACHE_REF_ROOT``) with the
   reference's own nvcc flags (setup.py:7-17 of the reference) plus
   ref_shim.cu.  Built only where those sources exist; the prebuilt .so travels
   with the repository snapshot to the GPU box.
 
-Usage: ``python oracle/build.py [--oracle] [--ref]`` (both by default).
+Usage: ``python oracle/build.py [--oracle] [--ref] [--ref-root <reference checkout>]``
+(both by default).
 """
 from __future__ import annotations
 
@@ -35,8 +37,14 @@ REF_SOURCES = [
 ]
 
 
-def ref_src_dir() -> str:
-    return os.environ.get("BITCACHE_REF_SRC", "/root/reference/src")
+def ref_src_dir() -> str | None:
+    """The reference's src/ directory: BITCACHE_REF_SRC, else the `src` folder of
+    a reference checkout named by BITCACHE_REF_ROOT; None when neither is set."""
+    if os.environ.get("BITCACHE_REF_SRC"):
+        return os.environ["BITCACHE_REF_SRC"]
+    if os.environ.get("BITCACHE_REF_ROOT"):
+        return os.path.join(os.environ["BITCACHE_REF_ROOT"], "src")
+    return None
 
 
 def _up_to_date(target: str, deps: list[str]) -> bool:
@@ -64,8 +72,8 @@ def build_ref(force: bool = False) -> str | None:
     """Compile the reference kernels; returns the .so path, or None when the
     reference sources are not present on this machine."""
     sdir = ref_src_dir()
-    srcs = [os.path.join(sdir, s) for s in REF_SOURCES]
-    if not all(os.path.exists(s) for s in srcs):
+    srcs = [os.path.join(sdir, s) for s in REF_SOURCES] if sdir else []
+    if not srcs or not all(os.path.exists(s) for s in srcs):
         return REF_SO if os.path.exists(REF_SO) else None
     shim = os.path.join(HERE, "ref_shim.cu")
     if not force and _up_to_date(REF_SO, srcs + [shim, __file__]):
@@ -84,7 +92,12 @@ def build_ref(force: bool = False) -> str | None:
 
 
 if __name__ == "__main__":
-    want = set(sys.argv[1:]) or {"--oracle", "--ref"}
+    args = sys.argv[1:]
+    if "--ref-root" in args:  # the reference checkout to compile the checker from
+        i = args.index("--ref-root")
+        os.environ["BITCACHE_REF_ROOT"] = args[i + 1]
+        del args[i:i + 2]
+    want = set(args) or {"--oracle", "--ref"}
     if "--oracle" in want:
         print(build_oracle(force=True))
     if "--ref" in want:

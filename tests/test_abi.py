@@ -97,3 +97,49 @@ def test_vector_footprints():
     assert planes.vector_bytes(128, False) == 18
     assert workloads.vector_footprint(128) == 82
     assert workloads.step_cache_bytes(1, 32, 65536, 128) == 343_932_928
+
+
+def test_exchange_struct_and_size_check():
+    """bc_xchg carries the buffers' size; a call whose heads would not fit is
+    refused on the host (BC_ERR_ARG) before anything is launched."""
+    lib = _lib.load()
+    assert ctypes.sizeof(_lib.Xchg) == 88
+    fake = _lib.KVPlanes(16, 16, 16, 16)
+    x = _lib.Xchg()
+    x.bufs[0] = 256
+    x.world, x.rank, x.epoch = 1, 0, 1
+    x.buf_bytes = lib.bc_xchg_bytes(4, 128, 1)  # sized for 4 heads
+    assert lib.bc_decode_attention_xchg(16, fake, fake, 16, 8, 1, 64, 64, 128, 1, x, None, 0, None) == 2
+    x.buf_bytes = 0
+    assert lib.bc_decode_attention_xchg(16, fake, fake, 16, 4, 1, 64, 64, 128, 1, x, None, 0, None) == 2
+
+
+def test_peer_exchange_refuses_other_shapes():
+    """PeerExchange.decode checks the call's heads and head_dim against the
+    sizes its buffers were allocated for, before any device work."""
+    from types import SimpleNamespace
+
+    from bitcache_b200 import dist as bdist
+
+    x = object.__new__(bdist.PeerExchange)
+    x._lib = _lib
+    x.n_heads, x.head_dim = 4, 128
+    K = SimpleNamespace(n_slots=8)
+    with pytest.raises(RuntimeError, match="built for 4 heads of dim 128"):
+        x.decode(torch.zeros(8, 128, dtype=torch.float16), K, K, 64, 1)
+    with pytest.raises(RuntimeError, match="built for 4 heads of dim 128"):
+        x.decode(torch.zeros(4, 64, dtype=torch.float16), SimpleNamespace(n_slots=4), K, 64, 1)
+
+
+def test_bitcache_import_name():
+    """The reference's import name gives this implementation."""
+    import bitcache
+    import bitcache.functional as F
+    from bitcache import _C as C
+
+    import bitcache_b200
+
+    assert bitcache.BitCache is bitcache_b200.BitCache
+    assert F.compensated_attention is functional.compensated_attention
+    assert C.online_encode_token is _C.online_encode_token
+    assert callable(bitcache._require_extension)

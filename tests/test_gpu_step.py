@@ -228,3 +228,35 @@ def test_bitcache_step_with_pinned_host_operands(cuda):
         assert torch.equal(got, want.cpu())
     for X, Y in zip(a.planes, b.planes):
         planes_equal(X, Y, 205, True)
+
+
+def test_step_mixed_host_and_device_rows_wait_for_the_previous_kernel(cuda):
+    """new_k in pinned host memory, new_v a device tensor written by the
+    kernel queued just ahead (a decode whose output is that tensor).  The step
+    may read host-resident rows before it waits for the previous kernel, but
+    only when both rows are host-resident: here new_v must be read after the
+    previous decode has written it.  The result equals the same step run after
+    a full synchronisation."""
+    d, slots, S0 = 128, 8, 3000
+    g = torch.Generator().manual_seed(31)
+    big = [(torch.randn(slots, 32768, d, generator=g) * 0.5).half().to(cuda) for _ in range(2)]
+    Kb = planes.Planes.empty(slots, 32768, d, True, cuda)
+    Vb = planes.Planes.empty(slots, 32768, d, True, cuda)
+    planes.encode_planes(big[0], Kb)
+    planes.encode_planes(big[1], Vb)
+    qb = (torch.randn(slots, d, generator=g) * 0.5).half().to(cuda)
+    (Ka, Va), (Kc, Vc) = filled_pair(slots, 4096, d, True, S0, cuda, seed=32)
+    q = (torch.randn(slots, d, generator=g) * 0.5).half().to(cuda)
+    kh = (torch.randn(slots, d, generator=g) * 0.5).half().pin_memory()
+    for trial in range(3):
+        vdev = torch.zeros(slots, d, dtype=torch.float16, device=cuda)
+        torch.cuda.synchronize()
+        planes.decode_attention(qb, Kb, Vb, 32768, out=vdev)  # writes new_v in its final epilogue
+        got = planes.decode_step(q, kh, vdev, Ka, Va, S0 + 1, S0)
+        torch.cuda.synchronize()
+        want = planes.decode_step(q, kh.to(cuda), vdev.clone(), Kc, Vc, S0 + 1, S0)
+        torch.cuda.synchronize()
+        assert vdev.abs().sum() > 0
+        assert torch.equal(got, want), f"trial {trial}: the step read new_v before the previous kernel wrote it"
+        planes_equal(Ka, Kc, S0 + 1, True)
+        planes_equal(Va, Vc, S0 + 1, True)

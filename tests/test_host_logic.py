@@ -178,3 +178,30 @@ def test_oracle_joint_selection_matches_bruteforce():
         want = np.zeros(S, np.uint8)
         want[order[:33]] = 1
         assert np.array_equal(keep[j], want)
+
+
+def test_bench_job_partition_and_shared_config():
+    """bench.py: C3 splits the sequence across GPUs by default, the batched
+    configurations shard heads; both arms print the same config dict."""
+    import sys
+    from types import SimpleNamespace
+
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    import bench
+
+    def args(cfg, split="auto"):
+        return SimpleNamespace(config=cfg, head_dim=0, split=split, binary=False)
+
+    assert bench.resolve_split(args("C3"), 1) == "none"
+    assert bench.resolve_split(args("C3"), 8) == "seqx"
+    assert bench.resolve_split(args("C4"), 8) == "heads"
+    assert bench.resolve_split(args("C3", "seq"), 2) == "seq"
+    for world in (1, 2, 8):
+        jobs = [bench.Job(args("C3"), world, r) for r in range(world)]
+        assert sum(j.my_S for j in jobs) == 65536 and all(j.my_slots == 32 for j in jobs)
+        assert sum(j.bytes_rank for j in jobs) == jobs[0].bytes_total == 343_932_928
+        assert all(j.config() == jobs[0].config() for j in jobs)
+    jobs = [bench.Job(args("C4"), 8, r) for r in range(8)]
+    assert [j.my_slots for j in jobs] == [16] * 8 and all(j.my_S == 32768 for j in jobs)
+    c5 = bench.Job(SimpleNamespace(config="C5", head_dim=256, split="auto", binary=False), 1, 0)
+    assert c5.d == 256 and c5.adaptive and "d=256" in c5.config()["workload"]
