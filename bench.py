@@ -435,17 +435,21 @@ def main():
 
     stream = torch.cuda.current_stream(dev)
     n_warm = max(3, args.warmup)
-    t0 = time.perf_counter()
     for i in range(n_warm):
         full_step(i)
     torch.cuda.synchronize()
     barrier()
     # Every rank must run the same number of steps (the sequence splits wait
-    # for all ranks inside each step), so the busy-loop length is agreed once.
-    per_step_s = agreed_max((time.perf_counter() - t0) / n_warm)
+    # for all ranks inside each step), so the busy-loop length is agreed once,
+    # from the wall time of warm steps.
+    t0 = time.perf_counter()
+    for j in range(20):
+        full_step(n_warm + j)
+    torch.cuda.synchronize()
+    per_step_s = agreed_max((time.perf_counter() - t0) / 20)
     n_busy = max(50, int(0.6 / max(per_step_s, 1e-6)))
     n_tail = max(50, int(0.4 / max(per_step_s, 1e-6)))
-    i = n_warm
+    i = n_warm + 20
 
     # clocks sampled over a busy window that contains the timed region
     sampler = ClockSampler(local)
