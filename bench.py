@@ -64,6 +64,9 @@ def parse():
                     help="small profiling run: one cache copy, only the decode kernel, warmup+steps launches")
     ap.add_argument("--profile-seq", type=int, default=0,
                     help="with --profile: override the config's sequence length (a smaller capture)")
+    ap.add_argument("--profile-kernel", default="decode",
+                    choices=["decode", "encode", "append", "entropy", "select", "compact", "merge", "records"],
+                    help="with --profile: the kernel whose launches the run makes (warmup + steps of them)")
     return ap.parse_args()
 
 
@@ -298,9 +301,91 @@ def run_reference(args):
 # ---------------------------------------------------------------------------
 # Our arm
 # ---------------------------------------------------------------------------
+def run_profile_kernel(args, w, dev):
+    """--profile with a kernel other than the decode: warmup + steps launches of it
+    on the workload `w` (the encoder, the decode-step append, the reference-API
+    entropy, the adaptive selection and compaction, the log-sum-exp merge, the
+    reference-record attention), nothing else after the set-up.  Prints the
+    algorithmic bytes of one launch."""
+    import torch
+
+    from bitcache_b200 import _C, planes, workloads
+
+    S, d, n = w.seq_len, w.head_dim, w.n_slots
+    comp = not args.binary
+    rm = planes.RES_FP16_SCALE if comp else planes.RES_NONE
+    launches = args.warmup + args.steps
+    kern = args.profile_kernel
+    k = w.k.reshape(n, S, d)
+    if kern == "encode":  # k_encode_planes_lpv: fp16 in, planes out
+        K = planes.Planes.empty(n, planes.round_stride(S), d, comp, dev, zero=False)
+        torch.cuda.synchronize()
+        for _ in range(launches):
+            planes.encode_planes(k, K, rm)
+        nbytes = n * S * (2 * d + planes.vector_bytes(d, comp))
+    elif kern == "append":  # k_append_kv: one K and one V token per slot
+        K = planes.Planes.empty(n, planes.round_stride(S), d, comp, dev)
+        V = planes.Planes.empty(n, planes.round_stride(S), d, comp, dev)
+        kv = w.k[:, :, :2].reshape(n, 2, d)
+        kt, vt = kv[:, 0].contiguous(), kv[:, 1].contiguous()
+        torch.cuda.synchronize()
+        for i in range(launches):
+            planes.append_kv(kt, vt, K, V, i % S, planes.RES_FP32_SCALE if comp else planes.RES_NONE)
+        nbytes = 2 * n * (2 * d + planes.vector_bytes(d, comp))
+    elif kern == "entropy":  # k_head_entropy on reference records (the reference API)
+        kb = _C.binary_encode(k.reshape(-1, d))
+        q = w.q.reshape(-1, d)[:n].contiguous()
+        torch.cuda.synchronize()
+        for _ in range(launches):
+            _C.compute_head_entropy(q.view(1, n, d), kb, 1, n, S, d)
+        nbytes = n * S * (d // 8 + 2)  # used record fields: sign words + scale
+    elif kern in ("select", "compact"):  # k_select_topk (joint K+V) / k_compact_adaptive
+        K = planes.Planes.empty(n, planes.round_stride(S), d, True, dev, zero=False)
+        V = planes.Planes.empty(n, planes.round_stride(S), d, True, dev, zero=False)
+        planes.encode_planes(k, K)
+        planes.encode_planes(w.v.reshape(n, S, d), V)
+        n_keep = planes.keep_count(S, w.extra.get("keep", 0.25))
+        keep = planes.select_positions_topk(K, V, S, n_keep)
+        torch.cuda.synchronize()
+        for _ in range(launches):
+            if kern == "select":
+                planes.select_positions_topk(K, V, S, n_keep)
+            else:
+                planes.compact_adaptive(K, V, keep, S, n_keep)
+        if kern == "select":
+            nbytes = 2 * n * S * (d // 2 + 2) + n * S  # residual planes of K and V read, keep mask written
+        else:  # K and V planes and the mask read; signs and scales of all, residuals of the kept written
+            nbytes = (2 * n * S * planes.vector_bytes(d, True) + n * S
+                      + 2 * n * (S * planes.vector_bytes(d, False) + n_keep * (d // 2 + 2)))
+    elif kern == "merge":  # k_lse_merge of 8 partial triples per head (an 8-way sequence split)
+        heads = w.q.numel() // d
+        parts = torch.randn(8, heads, d + 2, device=dev)
+        out = torch.empty(heads, d, dtype=torch.float16, device=dev)
+        torch.cuda.synchronize()
+        for _ in range(launches):
+            planes.lse_merge(parts, out=out)
+        nbytes = parts.numel() * 4 + out.numel() * 2
+    else:  # records: k_decode_records, the reference-layout compensated attention
+        kb = _C.binary_encode(k.reshape(-1, d))
+        vb = _C.binary_encode(w.v.reshape(-1, d))
+        kr = _C.residual_encode(k.reshape(-1, d), kb) if comp else None
+        vr = _C.residual_encode(w.v.reshape(-1, d), vb) if comp else None
+        q = w.q.reshape(-1, d)[:n].contiguous().view(1, n, d)
+        torch.cuda.synchronize()
+        for _ in range(launches):
+            if comp:
+                _C.compensated_attention(q, kb, kr, vb, vr, 1, n, S, d)
+            else:
+                _C.binary_attention(q, kb, vb, 1, n, S, d)
+        nbytes = workloads.step_cache_bytes(1, n, S, d, comp)
+    torch.cuda.synchronize()
+    print(json.dumps({"profile": args.config, "kernel": kern, "launches": launches, "bytes_per_launch": nbytes}))
+
+
 def run_profile(args):
     """Minimal run for ncu: one cache copy of the workload (> L2), fp16 inputs freed,
-    then warmup + steps launches of the decode kernel and nothing else."""
+    then warmup + steps launches of the decode kernel and nothing else
+    (--profile-kernel picks another kernel)."""
     import torch
 
     from bitcache_b200 import planes, workloads
@@ -311,6 +396,9 @@ def run_profile(args):
     if args.profile_seq:
         over["seq_len"] = args.profile_seq
     w = workloads.make(args.config, device=dev, **over)
+    if args.profile_kernel != "decode":
+        run_profile_kernel(args, w, dev)
+        return
     S, d, n = w.seq_len, w.head_dim, w.n_slots
     K = planes.Planes.empty(n, planes.round_stride(S), d, comp, dev, zero=False)
     V = planes.Planes.empty(n, planes.round_stride(S), d, comp, dev, zero=False)
