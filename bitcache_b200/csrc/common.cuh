@@ -34,6 +34,19 @@ __host__ __device__ __forceinline__ int64_t nib_chunk_offset(int64_t row, int c,
     return (row >> 3) * (int64_t)(4 * d) + (int64_t)c * 128 + (row & 7) * 16;
 }
 
+// Which dims a chunk holds.  Head dims other than 128 keep the reference's
+// element order: byte j of chunk c holds dims 32c + 2j (low nibble) and
+// 32c + 2j + 1 (high nibble).  At head_dim 128 the order is "by bit": byte j
+// of chunk c holds dims 8j + c (low) and 8j + c + 4 (high), so chunk c holds
+// exactly the dims of bits c and c + 4 of every sign byte, and the decode
+// kernel's tensor-core value phase gives a dim's sign bit and its code the
+// same accumulator row.  The values are the reference's; only their places
+// differ (the record converters permute).
+__host__ __device__ constexpr bool nib_by_bit(int d) { return d == 128; }
+__host__ __device__ constexpr int nib_dim(int d, int c, int j, int hi) {
+    return nib_by_bit(d) ? 8 * j + c + 4 * hi : 32 * c + 2 * j + hi;
+}
+
 // ---------------------------------------------------------------------------
 // Device-side error word.  Kernels never trap: a bounded wait that gives up
 // ORs a code into the error word (defined once, in decode.cu, whose kernels

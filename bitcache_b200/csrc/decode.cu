@@ -69,6 +69,9 @@ __device__ unsigned int g_bc_device_error = 0;
 #ifndef BC_DEC_BIN_GC
 #define BC_DEC_BIN_GC 2        // most query heads per CTA in binary grouped-query caches (2: tensor-core value phase)
 #endif
+#ifndef BC_DEC_GQA_GC
+#define BC_DEC_GQA_GC 4        // most query heads per CTA in compensated grouped-query caches at head_dim 128
+#endif
 #ifndef BC_DEC_KCOMB
 #define BC_DEC_KCOMB 8         // split partials each combining thread loads per L2 round trip
 #endif
@@ -104,10 +107,15 @@ struct DecCfg {
     static constexpr int NS = (D == 256) ? 2 : BC_DEC_STAGES;  // ring stages
     static constexpr int LAG = 1;            // refill the stage consumed one tile ago
     static constexpr int T = kTile;
+    // Tensor-core value phase (head_dim 128, up to four heads per CTA): the
+    // value sums of GC heads are NT column tiles of 8 (two heads x four
+    // coefficient bytes each).
+    static constexpr bool MMA = BC_DEC_MMA && D == 128 && GC <= 4;
+    static constexpr int NT = (GC + 1) / 2;
     // Binary caches on the tensor-core path stage TPS tiles per ring slot (a
     // binary tile is only 4.6 KB at head_dim 128): attention and entropy
     // stream that many per stage, the step and record kernels one.
-    static constexpr int TPS = (BC_DEC_MMA && D == 128 && GC <= 2 && !COMP) ? BC_DEC_BIN_TPS : 1;
+    static constexpr int TPS = (MMA && !COMP) ? BC_DEC_BIN_TPS : 1;
     static constexpr int KEYS = T * TPS;     // keys a stage can hold
     static constexpr int SIGN_B = KEYS * D / 8;
     static constexpr int NIB_B = COMP ? T * D / 2 : 0;
@@ -123,17 +131,23 @@ struct DecCfg {
     static constexpr int STAGE_B = OFF_VRS + (COMP ? SC_B : 0);
     static constexpr int RING_B = NS * STAGE_B;
     static constexpr int MERGE_B = kWarps * GC * (D + 2) * 4;  // reuses the ring after the main loop
-    static constexpr int BODY_B = RING_B > MERGE_B ? RING_B : MERGE_B;
     // tensor-core value phase: the warps' accumulators are dumped after the
-    // merge records ([warp][lane][65] ints) for the final read-out
+    // merge records ([warp][lane][NT * 32 + 1] ints) for the final read-out
+    static constexpr int DUMP_STRIDE = NT * 32 + 1;
     static constexpr int DUMP_OFF = (MERGE_B + 127) & ~127;
-    static constexpr int DUMP_B = kWarps * 32 * 65 * 4;
+    static constexpr int DUMP_B = kWarps * 32 * DUMP_STRIDE * 4;
+    // the ring, reused after the main loop by the merge records and the dump
+    static constexpr int AFTER_B = MMA ? DUMP_OFF + DUMP_B : MERGE_B;
+    static constexpr int BODY_B = RING_B > AFTER_B ? RING_B : AFTER_B;
     static constexpr int QF_OFF = BODY_B;                       // float q[GC][D]
     static constexpr int Q16_OFF = QF_OFF + GC * D * 4;         // int Q16[GC][D]
     static constexpr int QSIGN_OFF = Q16_OFF + GC * D * 4;      // uint32 [GC][8]
     static constexpr int QCONST_OFF = QSIGN_OFF + GC * 8 * 4;   // [GC][4]: bco, rco, off8, eco
-    static constexpr int QPK_OFF = QCONST_OFF + GC * 4 * 4;     // uint32 [GC][D/8][4] query packs
-    static constexpr int FULL_OFF = QPK_OFF + GC * (D / 8) * 16;  // mbarriers
+    // the residual score's query operand: dp4a packs, uint32 [GC][D/8][4], or
+    // on the tensor-core path the A matrix of the score MMA, [4 chunks][2][16 rows][16 B]
+    static constexpr int QPK_OFF = QCONST_OFF + GC * 4 * 4;
+    static constexpr int QPK_B = MMA ? 2048 : GC * (D / 8) * 16;
+    static constexpr int FULL_OFF = QPK_OFF + QPK_B;            // mbarriers
     static constexpr int EMPTY_OFF = FULL_OFF + NS * 8;         // mbarriers: all warps done with a stage
     static constexpr int FLAG_OFF = EMPTY_OFF + NS * 8;         // abort flag
     // Fused decode step: the appended K and V rows, staged once per CTA in
@@ -142,14 +156,17 @@ struct DecCfg {
     static constexpr int NEWROW_B = NEWSIGN_B + D / 2 + 16;
     static constexpr int NEW_OFF = FLAG_OFF + 16;               // [2][NEWROW_B]: K row, V row
     static constexpr int NEWRAW_OFF = NEW_OFF + 2 * NEWROW_B;   // fp16 [2][D]: the new K, V rows as given
-    // Tensor-core value phase (compensated, head_dim 128, one or two heads per
-    // CTA): per warp, the fixed-point key coefficients as bytes, [part][row][48].
-    static constexpr bool MMA = BC_DEC_MMA && D == 128 && GC <= 2;
+    // Tensor-core path, per warp: the fixed-point key coefficients as bytes,
+    // [part: sign, code][8 NT rows: head * 4 + byte][48], and the residual
+    // score dots of the warp's 32 keys, int [GC][32].
     static constexpr int WB_ROW = 48;                           // padded: the fragment loads hit distinct banks
-    static constexpr int WB_WARP = 2 * 8 * WB_ROW;
+    static constexpr int WB_PART = 8 * NT * WB_ROW;
+    static constexpr int WB_WARP = 2 * WB_PART;
+    static constexpr int DOT_WARP = GC * 40 * 4;  // int [GC][40]: the warp's 32 keys, padded rows
     static constexpr int WB_OFF = NEWRAW_OFF + 4 * D;
-    static constexpr int SMEM_B = WB_OFF + (MMA ? kWarps * WB_WARP : 0) + 128;  // + slack to align the base to 128 B
-    static_assert(!MMA || !COMP || DUMP_OFF + DUMP_B <= BODY_B, "accumulator dump exceeds the ring");
+    static constexpr int DOT_OFF = WB_OFF + (MMA ? kWarps * WB_WARP : 0);
+    static constexpr int SMEM_B = DOT_OFF + (MMA ? kWarps * DOT_WARP : 0) + 128;  // + slack to align the base to 128 B
+    static_assert(!MMA || DUMP_OFF + DUMP_B <= BODY_B, "accumulator dump exceeds the ring");
     // Resident CTAs per SM that shared memory allows at head_dim <= 128 with one
     // head per CTA; the register budget is held to it (0: no bound).
     static constexpr int MIN_CTAS =
@@ -263,9 +280,17 @@ __device__ __forceinline__ bool prefetch_query(const DecodeArgs& a, int slot, in
     return true;
 }
 
-template <int D, int GC, bool COMP, typename Cfg>
+// QMMA: the residual score runs on the tensor cores (head_dim 128): q is
+// quantised to |Q16| <= 32639 and split into balanced digits Q16 = 256 hi + lo
+// with hi, lo in [-128, 127] (s8 operands); the A matrix of the score MMA,
+// [chunk c][half h][row][16 bytes], holds at byte k of row g (head g's hi
+// digit) / row 8 + g (its lo digit) the digit of dim 8k + c + 4h, the dims of
+// byte k of nibble chunk c (low nibble for h = 0, high for h = 1).
+// Otherwise q is quantised to |Q16| <= 32767 and packed for dp4a.
+template <int D, int GC, bool COMP, typename Cfg, bool QMMA = false>
 __device__ __forceinline__ void prepare_query(const DecodeArgs& a, int slot, int hg, uint8_t* smem,
                                               QState<D, GC>& qs, bool staged = false) {
+    constexpr float kQMax = QMMA ? 32639.0f : 32767.0f;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     float* qf = reinterpret_cast<float*>(smem + Cfg::QF_OFF);
     int* q16 = reinterpret_cast<int*>(smem + Cfg::Q16_OFF);
@@ -293,7 +318,7 @@ __device__ __forceinline__ void prepare_query(const DecodeArgs& a, int slot, int
         }
 #pragma unroll
         for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-        const float qscale = mx > 0.0f ? 32767.0f / mx : 0.0f;
+        const float qscale = mx > 0.0f ? kQMax / mx : 0.0f;
         int sum16 = 0;
         for (int k = 0; k < D / 32; ++k) {
             const int v = __float2int_rn(qf[g * D + 32 * k + lane] * qscale);
@@ -322,7 +347,7 @@ __device__ __forceinline__ void prepare_query(const DecodeArgs& a, int slot, int
         if (lane == 0) {
             sq /= (float)D;
             qc[g * 4 + 0] = sq * inv_sqrt_d * kLog2e;
-            qc[g * 4 + 1] = (mx / 32767.0f) * (1.0f / 7.0f) * inv_sqrt_d * kLog2e;
+            qc[g * 4 + 1] = (mx / kQMax) * (1.0f / 7.0f) * inv_sqrt_d * kLog2e;
             reinterpret_cast<int*>(qc)[g * 4 + 2] = 8 * sum16;
         }
     }
@@ -336,7 +361,7 @@ __device__ __forceinline__ void prepare_query(const DecodeArgs& a, int slot, int
         qs.off8[g] = reinterpret_cast<const int*>(qc)[g * 4 + 2];
         qs.eco[g] = qc[g * 4 + 3];
         qs.pk = reinterpret_cast<const uint4*>(smem + Cfg::QPK_OFF);
-        if (COMP) {
+        if (COMP && !QMMA) {
             uint4* dst = reinterpret_cast<uint4*>(smem + Cfg::QPK_OFF);
             for (int w = threadIdx.x; w < D / 8; w += kDecThreads) {
                 uint32_t eh = 0, el = 0, oh = 0, ol = 0;
@@ -350,6 +375,24 @@ __device__ __forceinline__ void prepare_query(const DecodeArgs& a, int slot, int
                 }
                 dst[g * (D / 8) + w] = make_uint4(eh, el, oh, ol);
             }
+        }
+    }
+    if constexpr (QMMA && COMP) {
+        static_assert(D == 128 && GC <= 8, "score MMA: head_dim 128, at most 8 heads");
+        uint32_t* qa = reinterpret_cast<uint32_t*>(smem + Cfg::QPK_OFF);
+        for (int w = threadIdx.x; w < 512; w += kDecThreads) {  // word w: chunk, half, row, bytes 4k4..4k4+3
+            const int k4 = w & 3, row = (w >> 2) & 15, h = (w >> 6) & 1, c = w >> 7;
+            const int g = row & 7;
+            uint32_t word = 0;
+            if (g < GC) {
+#pragma unroll
+                for (int b = 0; b < 4; ++b) {
+                    const int v = q16[g * D + 8 * (4 * k4 + b) + c + 4 * h];
+                    const int lo = ((v + 128) & 255) - 128, hi = (v - lo) >> 8;
+                    word |= ((uint32_t)(row < 8 ? hi : lo) & 0xFFu) << (8 * b);
+                }
+            }
+            qa[w] = word;
         }
     }
     __syncthreads();
@@ -374,27 +417,29 @@ __device__ __forceinline__ void init_soft(SoftState<GC, NP>& st) {
 }
 
 // State of the tensor-core value phase.  The value sums live in integer MMA
-// accumulators: acc[part][t] is the m16n8 tile t of part 0 (sign) or 1
-// (residual), rows = dims, columns = (head, byte of the key coefficient).
-// A key's coefficient (2 w bscale for the sign bits, w rscale / 7 for the
-// codes, w = 2^(s - m)) enters as a 32-bit fixed-point number in units of
-// 2^U[g] (absolute, log2), split into four byte columns, so the softmax's
-// lazy max m never touches the accumulators; U moves only when a coefficient
-// would reach 2^31 units, and the accumulators are then shifted down exactly.
+// accumulators: acc[n][t] is the m16n8 tile t (rows = dims, see
+// consume_warp_tile_mma) of column tile n (columns = head 2n + col / 4, byte
+// col % 4 of the key coefficient).  The sign bits and the INT4 codes of a dim
+// share its accumulator row: the sign bit enters with the coefficient 2 w
+// bscale, the code with w rscale / 7 (w = 2^(s - m)), both as 32-bit
+// fixed-point numbers in units of 2^U[g] (absolute, log2) split into four byte
+// columns, so the softmax's lazy max m never touches the accumulators; U
+// moves only when a coefficient would reach 2^31 units, and the accumulators
+// are then shifted down exactly.
 constexpr int kUUnset = -0x40000000;
 
-template <int GC, int P = 2>
+template <int GC>
 struct MmaState {
-    static constexpr int PARTS = P;  // 2: sign and residual; 1: binary-only cache
+    static constexpr int NT = (GC + 1) / 2;
     float m[GC];
     float l[GC], t[GC];
-    int acc[P][8][4];
+    int acc[NT][8][4];
     int U[GC];
     float em[GC], ez[GC], ew[GC];
 };
 
-template <int GC, int P>
-__device__ __forceinline__ void init_soft(MmaState<GC, P>& st) {
+template <int GC>
+__device__ __forceinline__ void init_soft(MmaState<GC>& st) {
 #pragma unroll
     for (int g = 0; g < GC; ++g) {
         st.m[g] = -INFINITY;
@@ -406,11 +451,11 @@ __device__ __forceinline__ void init_soft(MmaState<GC, P>& st) {
         st.ew[g] = 0.0f;
     }
 #pragma unroll
-    for (int p = 0; p < P; ++p)
+    for (int n = 0; n < MmaState<GC>::NT; ++n)
 #pragma unroll
         for (int t = 0; t < 8; ++t)
 #pragma unroll
-            for (int i = 0; i < 4; ++i) st.acc[p][t][i] = 0;
+            for (int i = 0; i < 4; ++i) st.acc[n][t][i] = 0;
 }
 
 // ---------------------------------------------------------------------------
@@ -632,24 +677,41 @@ __device__ __forceinline__ void consume_warp_tile(const QState<D, GC>& qs, SoftS
 }
 
 // ---------------------------------------------------------------------------
-// Tensor-core value phase (compensated, head_dim 128, GC <= 2 heads).
+// Tensor-core path (head_dim 128, up to four query heads per CTA).
 //
-// Per warp and tile: D[dims x (head, byte)] += V[dims x 32 keys] . W[32 keys x
-// (head, byte)] with mma.sync m16n8k32 u8 x u8 -> s32.  Lane = 4 g8 + q; MMA
-// k index = the warp's key.  ldmatrix .m16n16 .trans .b8 on 16 keys x 16
-// bytes hands lane (g8, q) byte g8 (and g8 + 8) of keys 4q .. 4q + 3: the u8
-// A fragment of one byte position, so one mask per fragment remains.
-//  * Sign part, tile t: rows g8 / g8 + 8 are dims 8 g8 + t / 64 + 8 g8 + t
-//    (sign bytes g8, g8 + 8; bit t, value 2^t).
-//  * Residual part, tile 2c + h: rows g8 / g8 + 8 are dims 32c + 16h + 2 g8
-//    (low nibble, u) / the next dim (high nibble, 16 u), from 16-byte chunk c.
-//  * Coefficients: each lane writes its key's fixed-point bytes to the warp's
-//    scratch ([part][head*4 + byte][key]); lane reads its B fragment (column
-//    g8 = head g8/4, byte g8%4; keys 4q.., 4q + 16..) as two 32-bit words.
+// Score: the XNOR popcount stays on SIMT, one lane per key.  The INT4
+// residual dot sum_d u_d Q16_d of the warp's 32 keys and all GC heads is one
+// set of sixteen mma.sync m16n8k32 s8 x u8 -> s32 (residual_dots_mma): A = the
+// query's balanced hi/lo digits (rows), B = the offset-binary codes (keys).
+//
+// Values: per warp and tile, D[dims x (head, byte)] += A[dims x 32 keys] .
+// W[32 keys x (head, byte)] with mma.sync m16n8k32 u8 x u8 -> s32; lane =
+// 4 g8 + q, MMA k index = the warp's key.  ldmatrix .m16n16 .trans .b8 on 16
+// keys x 16 bytes hands lane (g8, q) byte g8 (and g8 + 8) of keys 4q .. 4q + 3,
+// so one shift and mask per fragment remain.  Row tile t = 2c + h has
+//   row g8     = dim 64 h + 8 g8 + c      (one unit per unit of the operand)
+//   row g8 + 8 = dim 64 h + 8 g8 + c + 4  (16 units per unit)
+// for both parts: sign bit c (row g8 + 8: bit c + 4) of sign byte g8 + 8h,
+// shifted down by c and masked with 0x01 (0x10) per byte; and the low (high)
+// nibble of byte g8 + 8h of nibble chunk c, which in the by-bit nibble order
+// holds exactly those two dims.  So the sign bits and the codes of a dim
+// accumulate in the same row, with the sign coefficient 2 w bscale and the
+// code coefficient w rscale / 7 as their B operands.  Each lane writes its
+// key's fixed-point coefficient bytes to the warp's scratch
+// ([part][head * 4 + byte][key]) and reads its B fragments (column g8 of
+// column tile n: head 2n + g8 / 4, byte g8 % 4; keys 4q.., 4q + 16..) as two
+// 32-bit words.
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void mma_u8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
                                        uint32_t b1) {
     asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.u8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ void mma_s8u8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                         uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.u8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
         : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
@@ -663,42 +725,124 @@ __device__ __forceinline__ void ldsm_x2_trans_b8(const uint8_t* row, uint32_t& r
                  : "r"(smem_u32(row)));
 }
 
-// Divide head g's accumulators by 2^delta (delta >= 1), exactly up to the
-// dropped low bits: each (row, part, tile) value is rebuilt from its four byte
-// columns (lanes 2g and 2g + 1), shifted, and split back into byte columns.
-template <int GC, int P>
-__device__ __forceinline__ void mma_shift_down(MmaState<GC, P>& st, int g, int delta) {
-    const int q = threadIdx.x & 3;
-    const bool mine = (q >> 1) == g, upper = q & 1;
-#pragma unroll
-    for (int p = 0; p < P; ++p)
-#pragma unroll
-        for (int t = 0; t < 8; ++t)
-#pragma unroll
-            for (int r = 0; r < 2; ++r) {
-                const uint64_t v = (uint64_t)(uint32_t)st.acc[p][t][2 * r] + ((uint64_t)(uint32_t)st.acc[p][t][2 * r + 1] << 8);
-                const uint64_t vn = __shfl_xor_sync(0xffffffffu, v, 1);
-                const uint64_t lo = upper ? vn : v, hi = upper ? v : vn;
-                const uint64_t T = delta >= 63 ? 0 : (lo + (hi << 16)) >> delta;
-                if (mine) {
-                    st.acc[p][t][2 * r] = (int)(upper ? (T >> 16) & 0xFFu : T & 0xFFu);
-                    st.acc[p][t][2 * r + 1] = (int)(upper ? (T >> 24) : (T >> 8) & 0xFFu);
-                }
-            }
+// Four 8x8 b16 matrices (rows of 16 bytes; lanes 8i .. 8i + 7 give the rows of
+// matrix i): lane (g8, q) receives bytes 4q .. 4q + 3 of row g8 of each.
+__device__ __forceinline__ void ldsm_x4(const uint8_t* row, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(smem_u32(row)));
 }
 
-// RES = false: binary-only keys (the adaptive cache's second segment), the
-// sign part alone; the residual accumulators are left untouched.
-template <int D, int GC, typename Cfg, bool ENT = false, bool RES = true, int P>
-__device__ __forceinline__ void consume_warp_tile_mma(const QState<D, GC>& qs, MmaState<GC, P>& st, const uint8_t* sb,
-                                                      int kw, int nk, uint8_t* wb) {
-    static_assert(D == 128 && GC <= 2, "tensor-core value phase: head_dim 128, at most two heads per CTA");
-    static_assert(!RES || P == 2, "the residual part needs its accumulators");
+// Where the tensor-core path finds the CTA's query state (shared memory):
+// sign words [GC][8], constants [GC][4] (bco, rco, off8 as int, eco) and the A
+// matrix of the score MMA (see prepare_query).
+struct QSmem {
+    const uint32_t* sign;
+    const float* c;
+    const uint8_t* qa;
+};
+
+constexpr int kDotRow = 40;  // ints per head row of a warp's dot buffer (padded: conflict-free stores)
+
+// Residual dots of the warp's keys kw .. kw + 31 for GC heads:
+// dotb[g * kDotRow + key] = sum_d u_d Q16_d (u = code + 8).  B fragments:
+// chunk c of an 8-key block is 8 consecutive 16-byte rows; lane (g8, q) gets
+// bytes 4q .. 4q + 3 of key g8, whose low nibbles are the k = 4q.. elements
+// (dims 8k + c) and whose high nibbles, shifted down, the k = 16 + 4q..
+// elements (dims 8k + c + 4).  D rows g / 8 + g are head g's hi / lo digit,
+// columns the keys, so dot = 256 D[g] + D[8 + g] stays in one lane.
+template <int GC>
+__device__ __forceinline__ void residual_dots_mma(const uint8_t* knib, int kw, const uint8_t* qa, int* dotb) {
+    const int lane = threadIdx.x & 31, g8 = lane >> 2, q = lane & 3;
+    uint32_t a[4][4];
+#pragma unroll
+    for (int c = 0; c < 4; ++c)
+        ldsm_x4(qa + ((2 * c + (lane >> 4)) * 16 + ((lane >> 3) & 1) * 8 + (lane & 7)) * 16, a[c][0], a[c][1],
+                a[c][2], a[c][3]);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        uint32_t nb[4];
+        ldsm_x4(knib + ((kw + 8 * j) >> 3) * 512 + 128 * (lane >> 3) + 16 * (lane & 7), nb[0], nb[1], nb[2], nb[3]);
+        int acc[4] = {0, 0, 0, 0};
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+            mma_s8u8(acc, a[c][0], a[c][1], a[c][2], a[c][3], nb[c] & 0x0F0F0F0Fu, (nb[c] >> 4) & 0x0F0F0F0Fu);
+        if (g8 < GC)
+            *reinterpret_cast<int2*>(dotb + g8 * kDotRow + 8 * j + 2 * q) =
+                make_int2(acc[0] * 256 + acc[2], acc[1] * 256 + acc[3]);
+    }
+}
+
+// Divide head g's accumulators by 2^delta (delta >= 1), exactly up to the
+// dropped low bits: each (row, tile) value is rebuilt from its four byte
+// columns (lanes with q = 2 (g % 2), 2 (g % 2) + 1 of column tile g / 2),
+// shifted, and split back into byte columns.
+template <int GC>
+__device__ __forceinline__ void mma_shift_down(MmaState<GC>& st, int g, int delta) {
+    const int q = threadIdx.x & 3;
+    const bool mine = (q >> 1) == (g & 1), upper = q & 1;
+    const int n = g >> 1;
+#pragma unroll
+    for (int t = 0; t < 8; ++t)
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+            const uint64_t v = (uint64_t)(uint32_t)st.acc[n][t][2 * r] + ((uint64_t)(uint32_t)st.acc[n][t][2 * r + 1] << 8);
+            const uint64_t vn = __shfl_xor_sync(0xffffffffu, v, 1);
+            const uint64_t lo = upper ? vn : v, hi = upper ? v : vn;
+            const uint64_t T = delta >= 63 ? 0 : (lo + (hi << 16)) >> delta;
+            if (mine) {
+                st.acc[n][t][2 * r] = (int)(upper ? (T >> 16) & 0xFFu : T & 0xFFu);
+                st.acc[n][t][2 * r + 1] = (int)(upper ? (T >> 24) : (T >> 8) & 0xFFu);
+            }
+        }
+}
+
+// One warp consumes its 32 keys (kw .. kw + 31) of a tile on the tensor-core
+// path.  RES = false: binary-only keys (a binary cache, or the adaptive
+// cache's second segment): no residual score, the sign part alone.
+template <int D, int GC, typename Cfg, bool ENT = false, bool RES = true>
+__device__ __forceinline__ void consume_warp_tile_mma(const QSmem& qs, MmaState<GC>& st, const uint8_t* sb, int kw,
+                                                      int nk, uint8_t* wb, int* dotb) {
+    static_assert(D == 128 && GC <= 4, "tensor-core path: head_dim 128, at most four heads per CTA");
+    constexpr int NT = MmaState<GC>::NT;
+    constexpr int WB_PART = 8 * NT * Cfg::WB_ROW;
     const int lane = threadIdx.x & 31;
     const int kk = kw + lane;
     const bool valid = kk < nk;
+    if constexpr (RES) {
+        residual_dots_mma<GC>(sb + Cfg::OFF_KNIB, kw, qs.qa, dotb);
+        __syncwarp();
+    }
+    // ---- score phase: lane `lane` scores key kk for the GC heads ----------------
+    const uint4 ks = *reinterpret_cast<const uint4*>(sb + Cfg::OFF_KSIGN + kk * (D / 8));
+    const float kbs = __half2float(reinterpret_cast<const __half*>(sb + Cfg::OFF_KBS)[kk]);
+    const float krs = RES ? __half2float(reinterpret_cast<const __half*>(sb + Cfg::OFF_KRS)[kk]) : 0.0f;
     float s2[GC];
-    score_keys<D, GC, RES, Cfg, ENT>(qs, st, sb, kk, valid, s2);
+#pragma unroll
+    for (int g = 0; g < GC; ++g) {
+        const uint4 qv = *reinterpret_cast<const uint4*>(qs.sign + 8 * g);
+        const float4 cst = *reinterpret_cast<const float4*>(qs.c + 4 * g);  // bco, rco, off8, eco
+        const int pop = __popc(qv.x ^ ks.x) + __popc(qv.y ^ ks.y) + __popc(qv.z ^ ks.z) + __popc(qv.w ^ ks.w);
+        float s = cst.x * kbs * (float)(D - 2 * pop);
+        if (RES) s = fmaf(cst.y * krs, (float)(dotb[g * kDotRow + lane] - __float_as_int(cst.z)), s);
+        s2[g] = valid ? s : -INFINITY;
+        if constexpr (ENT) {
+            // xnor_dot without 1/sqrt(d), online per lane (adaptive_precision.cu:69-102)
+            if (valid) {
+                const float sc = cst.w * kbs * (float)(D - 2 * pop);
+                if (sc > st.em[g]) {
+                    const float f = (st.em[g] == -INFINITY) ? 0.0f : __expf(st.em[g] - sc);
+                    st.ez[g] = st.ez[g] * f + 1.0f;
+                    st.ew[g] = st.ew[g] * f + sc;
+                    st.em[g] = sc;
+                } else {
+                    const float e = __expf(sc - st.em[g]);
+                    st.ez[g] += e;
+                    st.ew[g] += e * sc;
+                }
+            }
+        }
+    }
     const float vbs = valid ? __half2float(reinterpret_cast<const __half*>(sb + Cfg::OFF_VBS)[kk]) : 0.0f;
     const float vrs = (RES && valid) ? __half2float(reinterpret_cast<const __half*>(sb + Cfg::OFF_VRS)[kk]) : 0.0f;
 #pragma unroll
@@ -739,42 +883,51 @@ __device__ __forceinline__ void consume_warp_tile_mma(const QState<D, GC>& qs, M
 #pragma unroll
         for (int n = 0; n < 4; ++n) {
             wb[(4 * g + n) * Cfg::WB_ROW + lane] = (uint8_t)(A >> (8 * n));
-            if (RES) wb[(8 + 4 * g + n) * Cfg::WB_ROW + lane] = (uint8_t)(R >> (8 * n));
+            if (RES) wb[WB_PART + (4 * g + n) * Cfg::WB_ROW + lane] = (uint8_t)(R >> (8 * n));
         }
     }
     __syncwarp();
     const int g8 = lane >> 2, q = lane & 3;
-    uint32_t bs0 = 0, bs1 = 0, br0 = 0, br1 = 0;
-    if (g8 < 4 * GC) {
-        const uint8_t* rs = wb + g8 * Cfg::WB_ROW + 4 * q;
-        const uint8_t* rr = wb + (8 + g8) * Cfg::WB_ROW + 4 * q;
-        bs0 = *reinterpret_cast<const uint32_t*>(rs);
-        bs1 = *reinterpret_cast<const uint32_t*>(rs + 16);
-        if (RES) {
-            br0 = *reinterpret_cast<const uint32_t*>(rr);
-            br1 = *reinterpret_cast<const uint32_t*>(rr + 16);
-        }
+    uint32_t bs[NT][2], br[NT][2];
+#pragma unroll
+    for (int n = 0; n < NT; ++n) {
+        const bool ok = 8 * n + g8 < 4 * GC;
+        const uint8_t* rs = wb + (8 * n + g8) * Cfg::WB_ROW + 4 * q;
+        bs[n][0] = ok ? *reinterpret_cast<const uint32_t*>(rs) : 0u;
+        bs[n][1] = ok ? *reinterpret_cast<const uint32_t*>(rs + 16) : 0u;
+        br[n][0] = (RES && ok) ? *reinterpret_cast<const uint32_t*>(rs + WB_PART) : 0u;
+        br[n][1] = (RES && ok) ? *reinterpret_cast<const uint32_t*>(rs + WB_PART + 16) : 0u;
     }
-    // ---- sign part -------------------------------------------------------------
+    // ---- sign part: bits c and c + 4 of sign bytes g8, g8 + 8 -------------------
     {
         uint32_t r0, r1, r2, r3;
-        ldsm_x2_trans_b8(sb + Cfg::OFF_VSIGN + (kw + lane) * (D / 8), r0, r1, r2, r3);
+        ldsm_x2_trans_b8(sb + Cfg::OFF_VSIGN + kk * (D / 8), r0, r1, r2, r3);
 #pragma unroll
-        for (int t = 0; t < 8; ++t) {
-            const uint32_t mk = 0x01010101u << t;
-            mma_u8(st.acc[0][t], r0 & mk, r1 & mk, r2 & mk, r3 & mk, bs0, bs1);
+        for (int c = 0; c < 4; ++c) {
+            const uint32_t s0 = r0 >> c, s1 = r1 >> c, s2b = r2 >> c, s3 = r3 >> c;
+#pragma unroll
+            for (int n = 0; n < NT; ++n) {
+                mma_u8(st.acc[n][2 * c], s0 & 0x01010101u, s0 & 0x10101010u, s2b & 0x01010101u, s2b & 0x10101010u,
+                       bs[n][0], bs[n][1]);
+                mma_u8(st.acc[n][2 * c + 1], s1 & 0x01010101u, s1 & 0x10101010u, s3 & 0x01010101u, s3 & 0x10101010u,
+                       bs[n][0], bs[n][1]);
+            }
         }
     }
-    // ---- residual part ---------------------------------------------------------
-    if constexpr (RES && P == 2) {
-        const uint8_t* vn = sb + Cfg::OFF_VNIB + ((kw + lane) >> 3) * (4 * D) + 16 * ((kw + lane) & 7);
+    // ---- residual part: nibble chunk c, bytes g8, g8 + 8 --------------------------
+    if constexpr (RES) {
+        const uint8_t* vn = sb + Cfg::OFF_VNIB + (kk >> 3) * (4 * D) + 16 * (kk & 7);
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
             uint32_t r0, r1, r2, r3;
             ldsm_x2_trans_b8(vn + 128 * c, r0, r1, r2, r3);
-            mma_u8(st.acc[1][2 * c], r0 & 0x0F0F0F0Fu, r0 & 0xF0F0F0F0u, r2 & 0x0F0F0F0Fu, r2 & 0xF0F0F0F0u, br0, br1);
-            mma_u8(st.acc[1][2 * c + 1], r1 & 0x0F0F0F0Fu, r1 & 0xF0F0F0F0u, r3 & 0x0F0F0F0Fu, r3 & 0xF0F0F0F0u, br0,
-                   br1);
+#pragma unroll
+            for (int n = 0; n < NT; ++n) {
+                mma_u8(st.acc[n][2 * c], r0 & 0x0F0F0F0Fu, r0 & 0xF0F0F0F0u, r2 & 0x0F0F0F0Fu, r2 & 0xF0F0F0F0u,
+                       br[n][0], br[n][1]);
+                mma_u8(st.acc[n][2 * c + 1], r1 & 0x0F0F0F0Fu, r1 & 0xF0F0F0F0u, r3 & 0x0F0F0F0Fu, r3 & 0xF0F0F0F0u,
+                       br[n][0], br[n][1]);
+            }
         }
     }
     __syncwarp();  // the scratch is rewritten by the next tile
@@ -948,51 +1101,21 @@ __device__ __forceinline__ void warp_records(float* mg, SoftState<GC, Cfg::NP>& 
 }
 
 // The same record from the tensor-core accumulators.  Each lane dumps its
-// fragments to shared memory (the ring is free by now); lane 2g of each quad
-// then rebuilds head g's values from its byte columns (0, 1) and those of
-// lane 2g + 1 (2, 3), rows g8 and g8 + 8, and owns the quad's 16 dims.
+// fragments to shared memory (the ring is free by now); lane l then takes dims
+// 4l .. 4l + 3 of every head: dim = 64 h + 8 g8 + c + 4 hi sits in row tile
+// 2c + h, row g8 + 8 hi (16 units per unit when hi), column tile g / 2, byte
+// columns 0-1 in lane 4 g8 + 2 (g % 2) and 2-3 in the lane after it.
 template <int D, int GC, typename Cfg>
-__device__ __forceinline__ void warp_records(float* mg, MmaState<GC, 1>& st) {
-    // sign part only: read out from registers (lane 2g of each quad owns
-    // rows g8 / g8 + 8, i.e. dims 8 g8 + t / 64 + 8 g8 + t)
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, g8 = lane >> 2, q = lane & 3;
-#pragma unroll
-    for (int g = 0; g < GC; ++g) {
-        float l = st.l[g], t = st.t[g];
-#pragma unroll
-        for (int off = 16; off > 0; off >>= 1) {
-            l += __shfl_xor_sync(0xffffffffu, l, off);
-            t += __shfl_xor_sync(0xffffffffu, t, off);
-        }
-        float* rec = mg + ((size_t)warp * GC + g) * (D + 2);
-        if (lane == 0) {
-            rec[0] = st.m[g];
-            rec[1] = l;
-        }
-        const float sc = (st.U[g] != kUUnset && st.m[g] > -INFINITY) ? exp2f((float)st.U[g] - st.m[g]) : 0.0f;
-#pragma unroll
-        for (int tt = 0; tt < 8; ++tt)
-#pragma unroll
-            for (int r = 0; r < 2; ++r) {
-                const uint64_t P0 = (uint64_t)(uint32_t)st.acc[0][tt][2 * r] +
-                                    ((uint64_t)(uint32_t)st.acc[0][tt][2 * r + 1] << 8);
-                const uint64_t P1 = __shfl_xor_sync(0xffffffffu, P0, 1);
-                if (q == 2 * g)
-                    rec[2 + 64 * r + 8 * g8 + tt] = ((float)P0 + 65536.0f * (float)P1) * sc * exp2i(-tt) - t;
-            }
-    }
-}
-
-template <int D, int GC, typename Cfg>
-__device__ __forceinline__ void warp_records(float* mg, MmaState<GC, 2>& st) {
+__device__ __forceinline__ void warp_records(float* mg, MmaState<GC>& st) {
+    constexpr int NT = MmaState<GC>::NT, DS = Cfg::DUMP_STRIDE;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    int* dump = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(mg) + Cfg::DUMP_OFF) + warp * 32 * 65;
+    int* dump = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(mg) + Cfg::DUMP_OFF) + warp * 32 * DS;
 #pragma unroll
-    for (int p = 0; p < 2; ++p)
+    for (int n = 0; n < NT; ++n)
 #pragma unroll
         for (int t = 0; t < 8; ++t)
 #pragma unroll
-            for (int i = 0; i < 4; ++i) dump[lane * 65 + 32 * p + 4 * t + i] = st.acc[p][t][i];
+            for (int i = 0; i < 4; ++i) dump[lane * DS + 32 * n + 4 * t + i] = st.acc[n][t][i];
     __syncwarp();
 #pragma unroll
     for (int g = 0; g < GC; ++g) {
@@ -1009,23 +1132,16 @@ __device__ __forceinline__ void warp_records(float* mg, MmaState<GC, 2>& st) {
         }
         // accumulator unit relative to the warp's max: 2^(U - m)
         const float sc = (st.U[g] != kUUnset && st.m[g] > -INFINITY) ? exp2f((float)st.U[g] - st.m[g]) : 0.0f;
-        // lane takes dims 4 lane .. 4 lane + 3
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
             const int dim = 4 * lane + e;
-            // sign: quad (dim % 64) / 8, tile dim % 8, row dim / 64
-            const int* ls = dump + (4 * ((dim & 63) >> 3) + 2 * g) * 65;
-            const int cs = 4 * (dim & 7) + 2 * (dim >> 6);
-            // residual: quad (dim / 2) % 8, tile 2 (dim / 32) + (dim / 16) % 2, row dim % 2
-            const int* lr = dump + (4 * ((dim >> 1) & 7) + 2 * g) * 65;
-            const int cr = 32 + 4 * (2 * (dim >> 5) + ((dim >> 4) & 1)) + 2 * (dim & 1);
-            const uint64_t s0 = (uint64_t)(uint32_t)ls[cs] + ((uint64_t)(uint32_t)ls[cs + 1] << 8);
-            const uint64_t s1 = (uint64_t)(uint32_t)ls[65 + cs] + ((uint64_t)(uint32_t)ls[65 + cs + 1] << 8);
-            const uint64_t r0 = (uint64_t)(uint32_t)lr[cr] + ((uint64_t)(uint32_t)lr[cr + 1] << 8);
-            const uint64_t r1 = (uint64_t)(uint32_t)lr[65 + cr] + ((uint64_t)(uint32_t)lr[65 + cr + 1] << 8);
-            const float vs = ((float)s0 + 65536.0f * (float)s1) * exp2i(-(dim & 7));
-            const float vr = ((float)r0 + 65536.0f * (float)r1) * ((dim & 1) ? (1.0f / 16.0f) : 1.0f);
-            rec[2 + dim] = (vs + vr) * sc - t;
+            const int h = dim >> 6, g8 = (dim >> 3) & 7, c = dim & 3, hi = (dim >> 2) & 1;
+            const int* la = dump + (4 * g8 + 2 * (g & 1)) * DS + 32 * (g >> 1) + 4 * (2 * c + h) + 2 * hi;
+            const int* lb = la + DS;
+            const uint64_t v0 = (uint64_t)(uint32_t)la[0] + ((uint64_t)(uint32_t)la[1] << 8);
+            const uint64_t v1 = (uint64_t)(uint32_t)lb[0] + ((uint64_t)(uint32_t)lb[1] << 8);
+            const float v = ((float)v0 + 65536.0f * (float)v1) * (hi ? (1.0f / 16.0f) : 1.0f);
+            rec[2 + dim] = v * sc - t;
         }
     }
 }
@@ -1227,10 +1343,16 @@ struct StagedRowSink {
     }
     __device__ __forceinline__ void nib(const uint32_t (&nw)[NW], int lane) {
         if (store) g.nib(nw, lane);
+        if constexpr (nib_by_bit(32 * NW)) {  // lanes c < 4 hold chunk c
+            if (lane < 4)
+                *reinterpret_cast<uint4*>(srow + nib_off + 16 * lane) =
+                    make_uint4(nw[0] ^ 0x88888888u, nw[1] ^ 0x88888888u, nw[2] ^ 0x88888888u, nw[3] ^ 0x88888888u);
+        } else {
 #pragma unroll
-        for (int k = 0; k < NW; ++k)
-            if ((lane & 7) == 0)
-                reinterpret_cast<uint32_t*>(srow + nib_off + 16 * k)[lane >> 3] = nw[k] ^ 0x88888888u;
+            for (int k = 0; k < NW; ++k)
+                if ((lane & 7) == 0)
+                    reinterpret_cast<uint32_t*>(srow + nib_off + 16 * k)[lane >> 3] = nw[k] ^ 0x88888888u;
+        }
     }
     __device__ __forceinline__ void rscale(uint16_t b) {
         if (store) g.rscale(b);
@@ -1322,6 +1444,7 @@ __global__ void __launch_bounds__(kDecThreads, DecCfg<D, GC, COMP>::MIN_CTAS)
     k_decode_planes(const DecodeArgs a) {
     constexpr bool STEP = VAR == 1, ENT = VAR == 2, ADA = VAR == 3;
     using Cfg = DecCfg<D, GC, COMP>;
+    static_assert(Cfg::MMA || !nib_by_bit(D), "head_dim-128 planes (by-bit nibble order) need the tensor-core path");
     constexpr int NS = Cfg::NS, LAG = Cfg::LAG, T = Cfg::T;
     extern __shared__ __align__(128) uint8_t smem_raw[];
     uint8_t* smem = aligned_smem(smem_raw);
@@ -1451,7 +1574,9 @@ __global__ void __launch_bounds__(kDecThreads, DecCfg<D, GC, COMP>::MIN_CTAS)
     }
 
     QState<D, GC> qs;
-    prepare_query<D, GC, COMP, Cfg>(a, slot, hg, smem, qs, staged);
+    prepare_query<D, GC, COMP, Cfg, Cfg::MMA>(a, slot, hg, smem, qs, staged);
+    const QSmem qsm{reinterpret_cast<const uint32_t*>(smem + Cfg::QSIGN_OFF),
+                    reinterpret_cast<const float*>(smem + Cfg::QCONST_OFF), smem + Cfg::QPK_OFF};
 
     // Fused step: warps 0 and 1 encode the new K and V row; the owning warp
     // patches tile patch_it at key patch_kk (patch_it = -1: not this warp).
@@ -1474,7 +1599,7 @@ __global__ void __launch_bounds__(kDecThreads, DecCfg<D, GC, COMP>::MIN_CTAS)
     // the tensor-core value phase (in adaptive caches the binary-only
     // segment runs its sign part alone)
     constexpr bool MMA = Cfg::MMA;
-    std::conditional_t<MMA, MmaState<GC, COMP ? 2 : 1>, SoftState<GC, Cfg::NP>> st;
+    std::conditional_t<MMA, MmaState<GC>, SoftState<GC, Cfg::NP>> st;
     init_soft(st);
 
     int it = 0;
@@ -1503,20 +1628,21 @@ __global__ void __launch_bounds__(kDecThreads, DecCfg<D, GC, COMP>::MIN_CTAS)
         }
         if constexpr (MMA) {
             uint8_t* wb = smem + Cfg::WB_OFF + warp * Cfg::WB_WARP;
+            int* dotb = reinterpret_cast<int*>(smem + Cfg::DOT_OFF + warp * Cfg::DOT_WARP);
+            uint8_t* sbuf = smem + stage * Cfg::STAGE_B;
             if (wide) {
                 if constexpr (BIN4) {
                     for (int j = 0; j < BinStageCfg<D>::TILES && j * T < nk; ++j)
-                        consume_warp_tile_mma<D, GC, BinStageCfg<D>, false, false>(
-                            qs, st, smem + stage * Cfg::STAGE_B, j * T + warp * 32, nk, wb);
+                        consume_warp_tile_mma<D, GC, BinStageCfg<D>, false, false>(qsm, st, sbuf, j * T + warp * 32, nk,
+                                                                                   wb, dotb);
                 }
             } else if (Cfg::TPS > 1 && TS > T) {
                 for (int j = 0; j < Cfg::TPS && j * T < nk; ++j)
-                    consume_warp_tile_mma<D, GC, Cfg, ENT, COMP>(qs, st, smem + stage * Cfg::STAGE_B, j * T + warp * 32,
-                                                                 nk, wb);
+                    consume_warp_tile_mma<D, GC, Cfg, ENT, COMP>(qsm, st, sbuf, j * T + warp * 32, nk, wb, dotb);
             } else if (ADA && seg_bin)
-                consume_warp_tile_mma<D, GC, Cfg, false, false>(qs, st, smem + stage * Cfg::STAGE_B, warp * 32, nk, wb);
+                consume_warp_tile_mma<D, GC, Cfg, false, false>(qsm, st, sbuf, warp * 32, nk, wb, dotb);
             else
-                consume_warp_tile_mma<D, GC, Cfg, ENT, COMP>(qs, st, smem + stage * Cfg::STAGE_B, warp * 32, nk, wb);
+                consume_warp_tile_mma<D, GC, Cfg, ENT, COMP>(qsm, st, sbuf, warp * 32, nk, wb, dotb);
         } else {
             if (ADA && seg_bin)
                 consume_warp_tile<D, GC, false, Cfg>(qs, st, smem + stage * Cfg::STAGE_B, warp * 32, nk);
@@ -1673,14 +1799,14 @@ struct Plan {
 };
 
 
-// Query heads handled per CTA: up to two (compensated) or four (binary) of a
-// slot's group, so one read and one bit extraction of every KV key serve
-// them all; the CTAs of a slot's remaining head groups, adjacent in the
-// grid, share the KV tiles through L2.
+// Query heads handled per CTA, so that one read of every KV key serves them
+// all: at head_dim 128 (tensor-core path) up to four heads of a slot's group
+// for compensated caches, whose accumulators hold two heads per column tile;
+// elsewhere two (compensated, f32x2 value phase) or BC_DEC_BIN_GC (binary).
+// The CTAs of a slot's remaining head groups, adjacent in the grid, share the
+// KV tiles through L2.
 int heads_per_cta(int group, int d, bool comp) {
-    (void)d;
-    // accumulator registers: 32 per head (compensated), 16 (binary, f32x2)
-    const int cap = comp ? 2 : BC_DEC_BIN_GC;
+    const int cap = comp ? ((BC_DEC_MMA && d == 128) ? BC_DEC_GQA_GC : 2) : BC_DEC_BIN_GC;
     return group < cap ? group : cap;
 }
 
@@ -1917,6 +2043,10 @@ int run_decode_d(const DecodeArgs& a, bool comp, int var, void* ws, size_t wsb, 
             return comp ? run_decode_t<D, 2, true>(a, var, ws, wsb, st, fit)
                         : run_decode_t<D, 2, false>(a, var, ws, wsb, st, fit);
         default:
+            if constexpr (D == 128) {
+                if (comp) return run_decode_t<D, 4, true>(a, var, ws, wsb, st, fit);
+            }
+            if (comp) return BC_ERR_UNSUPPORTED;
             return run_decode_t<D, 4, false>(a, var, ws, wsb, st, fit);
     }
 }
@@ -2154,7 +2284,7 @@ size_t bc_decode_adaptive_workspace_bytes(int n_slots, int group, int seq_len, i
         !bc_valid_head_dim(head_dim))
         return 0;
     size_t best = 0;
-    for (int gc = 1; gc <= 2 && gc <= group; gc *= 2) {  // compensated CTAs hold one or two heads
+    for (int gc = 1; gc <= 4 && gc <= group; gc *= 2) {  // compensated CTAs hold one, two or four heads
         DecodeArgs a{};
         a.n_slots = n_slots;
         a.group = group;

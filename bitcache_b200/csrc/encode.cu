@@ -70,7 +70,7 @@ __global__ void __launch_bounds__(kEncWarps * 32) k_residual_encode_rec(const __
     for (int k = 0; k < NW; ++k) w[k] = reinterpret_cast<const uint32_t*>(brec)[k];
     const float s = __half2float(__ushort_as_half(*reinterpret_cast<const uint16_t*>(brec + kBinScaleOff)));
     uint32_t nw[NW], nh[NW];
-    const float absmax = quantise_residual<NW>(x, w, s, lane, nw, nh);
+    const float absmax = quantise_residual<NW, false>(x, w, s, lane, nw, nh);
     store_resvec<NW>(out + v * kResRecBytes, nh, f2h_bits(absmax), lane);
 }
 
@@ -92,7 +92,7 @@ __global__ void __launch_bounds__(kEncWarps * 32) k_online_encode_rec(const __ha
     store_binvec<NW>(bin + cache_idx * kBinRecBytes, w, f2h_bits(scale_bin), lane);
     if (res != nullptr) {
         uint32_t nw[NW], nh[NW];
-        const float absmax = quantise_residual<NW>(x, w, scale_bin, lane, nw, nh);
+        const float absmax = quantise_residual<NW, false>(x, w, scale_bin, lane, nw, nh);
         store_resvec<NW>(res + cache_idx * kResRecBytes, nh, f2h_bits(absmax), lane);
     }
 }
@@ -194,11 +194,171 @@ __device__ __forceinline__ float lpv_abs_sum(const uint4* row) {
     return v0 + v1;                                                                      // stride 1
 }
 
-// Encode the vector in shared-memory row `row` into plane row v (lane-local).
+// ---- head_dim 128: two passes over the row ------------------------------
+// Pass 1 sums |x| in the reference's tree order (as lpv_tree16) and also keeps
+// min |x| and max |x| (fp16, exact).  The residual's absmax needs no pass of
+// its own: |x - rec| = |fl(|x| - sc)| for every element (rec = +sc for
+// x >= 0, -sc otherwise, and RN is symmetric), and fl(a - sc) is monotone in
+// a, so the largest |x - rec| is reached at min |x| or at max |x|.  With a NaN
+// element sc is NaN and both terms are NaN, which fmaxf drops, as the
+// reference's per-element fmaxf does.  Pass 2 builds the sign bits and the
+// INT4 codes with packed fp32x2 arithmetic, in the by-bit nibble order.
+__device__ __forceinline__ float2 add2_ftz(float2 a, float2 b) {
+    unsigned long long r;
+    asm("add.rn.ftz.f32x2 %0, %1, %2;"
+        : "=l"(r)
+        : "l"(*reinterpret_cast<unsigned long long*>(&a)), "l"(*reinterpret_cast<unsigned long long*>(&b)));
+    return *reinterpret_cast<float2*>(&r);
+}
+__device__ __forceinline__ float2 mul2_ftz(float2 a, float2 b) {
+    unsigned long long r;
+    asm("mul.rn.ftz.f32x2 %0, %1, %2;"
+        : "=l"(r)
+        : "l"(*reinterpret_cast<unsigned long long*>(&a)), "l"(*reinterpret_cast<unsigned long long*>(&b)));
+    return *reinterpret_cast<float2*>(&r);
+}
+// 0xFFFF in each half where that fp16 element is >= 0 (so -0 is, NaN is not).
+__device__ __forceinline__ uint32_t hge0_mask(uint32_t h2) {
+    uint32_t m;
+    asm("set.ge.u32.f16x2 %0, %1, %2;" : "=r"(m) : "r"(h2), "r"(0u));
+    return m;
+}
+__device__ __forceinline__ uint32_t bfi32(uint32_t src, uint32_t base, uint32_t pos, uint32_t len) {
+    uint32_t r;
+    asm("bfi.b32 %0, %1, %2, %3, %4;" : "=r"(r) : "r"(src), "r"(base), "r"(pos), "r"(len));
+    return r;
+}
+// Four per-element flags (0xFFFF / 0 halves of a, then b) as bits 0..3: the
+// high bytes of the halves gathered by one byte permute, their top bits moved
+// to bits 28..31 by one multiply (the four partial products land on distinct
+// bits, so no carries).
+__device__ __forceinline__ uint32_t flags4(uint32_t a, uint32_t b) {
+    return ((__byte_perm(a, b, 0x7531) & 0x80808080u) * 0x00204081u) >> 28;
+}
+__device__ __forceinline__ uint4 lds128_volatile(const void* p) {
+    uint4 r;
+    asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "r"(smem_u32(p)) : "memory");
+    return r;
+}
+__device__ __forceinline__ void sts32_volatile(void* p, uint32_t v) {
+    asm volatile("st.shared.u32 [%0], %1;" ::"r"(smem_u32(p)), "r"(v) : "memory");
+}
+__device__ __forceinline__ float2 h2_to_f2(uint32_t h2) {
+    return __half22float2(*reinterpret_cast<const __half2*>(&h2));
+}
+
+template <int L, int K>
+__device__ __forceinline__ void lpv_tree16_mm(const uint4* row, float (&out)[8], __half2& mx, __half2& mn) {
+    if constexpr (L == 4) {  // leaf: chunk K of the 16 (head_dim 128)
+        const uint4 t = row[K];
+        const uint32_t w[4] = {t.x & 0x7FFF7FFFu, t.y & 0x7FFF7FFFu, t.z & 0x7FFF7FFFu, t.w & 0x7FFF7FFFu};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const __half2 h = *reinterpret_cast<const __half2*>(&w[i]);
+            mx = __hmax2(mx, h);
+            mn = __hmin2(mn, h);
+            const float2 f = __half22float2(h);
+            out[2 * i] = f.x;
+            out[2 * i + 1] = f.y;
+        }
+    } else {
+        float right[8];
+        lpv_tree16_mm<L + 1, K>(row, out, mx, mn);
+        lpv_tree16_mm<L + 1, K + (1 << L)>(row, right, mx, mn);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float2 s = add2_ftz(make_float2(out[2 * i], out[2 * i + 1]), make_float2(right[2 * i], right[2 * i + 1]));
+            out[2 * i] = s.x;
+            out[2 * i + 1] = s.y;
+        }
+    }
+}
+
+template <int RES>
+__device__ __forceinline__ void lpv_encode_row_128(const uint4* row, bc_kv_planes P, int64_t v, int seq_len,
+                                                   int64_t kv_stride, int head_dim) {
+    constexpr int D = 128;
+    float a[8];
+    __half2 mx = __float2half2_rn(0.0f), mn = __float2half2_rn(INFINITY);
+    lpv_tree16_mm<0, 0>(row, a, mx, mn);
+    const float u0 = a[0] + a[4], u1 = a[1] + a[5], u2 = a[2] + a[6], u3 = a[3] + a[7];  // stride 4
+    const float v0 = u0 + u2, v1 = u1 + u3;                                              // stride 2
+    const float mean_abs = (v0 + v1) / (float)head_dim;                                  // stride 1
+    const uint16_t sb = f2h_bits(mean_abs);
+    const float sc = (RES == BC_RES_FP16_SCALE) ? __half2float(__ushort_as_half(sb)) : mean_abs;
+    float absmax = 0.0f;
+    if constexpr (RES != BC_RES_NONE) {
+        const float lo = fminf(__low2float(mn), __high2float(mn)), hi = fmaxf(__low2float(mx), __high2float(mx));
+        absmax = fmaxf(fmaxf(0.0f, fabsf(lo - sc)), fabsf(hi - sc));
+    }
+    const float inv_absmax = (absmax > 0.0f) ? (7.0f / absmax) : 0.0f;
+    // See lpv_encode_row for the rounding by adding 1.5 * 2^23.
+    constexpr float kRound = 12582912.0f;
+    const float2 nsc = make_float2(-sc, -sc), inv2 = make_float2(inv_absmax, inv_absmax),
+                 rnd2 = make_float2(kRound, kRound);
+    const bool live = inv_absmax > 0.0f;
+    // Four input chunks (one word of each output chunk) per step.  The loads
+    // and the stores of finished words are volatile, so the compiler keeps one
+    // step's 16 input words live, not the whole row's 64.  Finished nibble
+    // words go back into the row's first 64 bytes (input chunks 0-3, no longer
+    // read): word w of output chunk c at byte 16c + 4w.
+    uint8_t* rb = reinterpret_cast<uint8_t*>(const_cast<uint4*>(row));
+    uint32_t sw[4];
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+        uint32_t cur[4] = {0u, 0u, 0u, 0u};  // word w of output chunks 0..3
+        uint32_t sword = 0u;
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj) {  // input chunk j = 4w + jj: dims 8j .. 8j + 7
+            const int j = 4 * w + jj;
+            const uint4 t = lds128_volatile(rb + 16 * j);
+            const uint32_t h[4] = {t.x, t.y, t.z, t.w};
+            uint32_t m[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) m[i] = hge0_mask(h[i]);
+            sword = bfi32(flags4(m[0], m[1]) | (flags4(m[2], m[3]) << 4), sword, 8 * jj, 8);
+            if constexpr (RES != BC_RES_NONE) {
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {  // elements 2i, 2i + 1
+                    // (|x| - sc) * inv, negated for x < 0: the rounded (x - rec) * inv_absmax
+                    float2 p = mul2_ftz(add2_ftz(h2_to_f2(h[i] & 0x7FFF7FFFu), nsc), inv2);
+                    p.x = __uint_as_float(__float_as_uint(p.x) ^ ((~m[i] << 16) & 0x80000000u));
+                    p.y = __uint_as_float(__float_as_uint(p.y) ^ (~m[i] & 0x80000000u));
+                    const float2 q = add2_ftz(p, rnd2);
+                    const int e0 = 2 * i, e1 = 2 * i + 1;  // element e: chunk e % 4, high nibble for e >= 4
+                    cur[e0 & 3] = bfi32(__float_as_uint(q.x), cur[e0 & 3], 8 * jj + 4 * (e0 >> 2), 4);
+                    cur[e1 & 3] = bfi32(__float_as_uint(q.y), cur[e1 & 3], 8 * jj + 4 * (e1 >> 2), 4);
+                }
+            }
+        }
+        sw[w] = sword;
+        if constexpr (RES != BC_RES_NONE) {
+#pragma unroll
+            for (int c = 0; c < 4; ++c)
+                sts32_volatile(rb + 16 * c + 4 * w, live ? cur[c] ^ 0x88888888u : 0x88888888u);  // code + 8
+        }
+    }
+    const int64_t slot = v / seq_len, pos = v - slot * seq_len;
+    const int64_t r = slot * kv_stride + pos;
+    *reinterpret_cast<uint4*>(reinterpret_cast<uint32_t*>(P.sign) + r * 4) = make_uint4(sw[0], sw[1], sw[2], sw[3]);
+    reinterpret_cast<uint16_t*>(P.bscale)[r] = sb;
+    if constexpr (RES != BC_RES_NONE) {
+        uint8_t* nb = reinterpret_cast<uint8_t*>(P.nib);
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+            *reinterpret_cast<uint4*>(nb + nib_chunk_offset(r, c, D)) = lds128_volatile(rb + 16 * c);
+        reinterpret_cast<uint16_t*>(P.rscale)[r] = f2h_bits(absmax);
+    }
+}
+
+// Encode the vector in shared-memory row `row` into plane row v (lane-local),
+// head dims below 128 (reference nibble order): three passes over the row.
 template <int NW, int RES>
-__device__ __forceinline__ void lpv_encode_row(const uint4* row, bc_kv_planes P, int64_t v, int seq_len,
-                                               int64_t kv_stride, int head_dim) {
+__device__ __forceinline__ void lpv_encode_row_small(const uint4* row, bc_kv_planes P, int64_t v, int seq_len,
+                                                     int64_t kv_stride, int head_dim) {
     constexpr int D = 32 * NW;
+    static_assert(!nib_by_bit(D), "head_dim 128 has its own row encoder");
     const float mean_abs = lpv_abs_sum<D>(row) / (float)head_dim;
     const uint16_t sb = f2h_bits(mean_abs);
     const float sc = (RES == BC_RES_FP16_SCALE) ? __half2float(__ushort_as_half(sb)) : mean_abs;
@@ -266,6 +426,15 @@ __device__ __forceinline__ void lpv_encode_row(const uint4* row, bc_kv_planes P,
         }
         reinterpret_cast<uint16_t*>(P.rscale)[r] = f2h_bits(absmax);
     }
+}
+
+template <int NW, int RES>
+__device__ __forceinline__ void lpv_encode_row(const uint4* row, bc_kv_planes P, int64_t v, int seq_len,
+                                               int64_t kv_stride, int head_dim) {
+    if constexpr (NW == 4)
+        lpv_encode_row_128<RES>(row, P, v, seq_len, kv_stride, head_dim);
+    else
+        lpv_encode_row_small<NW, RES>(row, P, v, seq_len, kv_stride, head_dim);
 }
 
 template <int NW, int RES>
@@ -361,9 +530,21 @@ __global__ void __launch_bounds__(kEncWarps * 32) k_records_to_planes(const uint
     if (res != nullptr && P.nib != nullptr) {
         const uint16_t* r = reinterpret_cast<const uint16_t*>(res + v * kResRecBytes);
         uint8_t* nib = reinterpret_cast<uint8_t*>(P.nib);
-        for (int i = lane; i < 8 * NW; i += 32)
-            *reinterpret_cast<uint16_t*>(nib + nib_chunk_offset(v, i >> 3, 32 * NW) + 2 * (i & 7)) =
-                (uint16_t)(r[i] ^ 0x8888u);
+        if constexpr (nib_by_bit(32 * NW)) {
+            // lane j < 16: record word j holds dims 8j .. 8j + 7 (nibble r = dim 8j + r);
+            // plane byte j of chunk c takes nibbles c (low) and c + 4 (high)
+            if (lane < 16) {
+                const uint32_t W = (uint32_t)r[2 * lane] | ((uint32_t)r[2 * lane + 1] << 16);
+#pragma unroll
+                for (int c = 0; c < 4; ++c)
+                    nib[nib_chunk_offset(v, c, 32 * NW) + lane] =
+                        (uint8_t)((((W >> (4 * c)) & 0xFu) | (((W >> (4 * c + 16)) & 0xFu) << 4)) ^ 0x88u);
+            }
+        } else {
+            for (int i = lane; i < 8 * NW; i += 32)
+                *reinterpret_cast<uint16_t*>(nib + nib_chunk_offset(v, i >> 3, 32 * NW) + 2 * (i & 7)) =
+                    (uint16_t)(r[i] ^ 0x8888u);
+        }
         if (lane == 0) reinterpret_cast<uint16_t*>(P.rscale)[v] = r[64];
     }
 }
@@ -380,10 +561,26 @@ __global__ void __launch_bounds__(kEncWarps * 32) k_planes_to_records(bc_kv_plan
     if (res != nullptr && P.nib != nullptr) {
         uint16_t* r = reinterpret_cast<uint16_t*>(res + v * kResRecBytes);
         const uint8_t* nib = reinterpret_cast<const uint8_t*>(P.nib);
-        for (int i = lane; i < 64; i += 32)
-            r[i] = (i < 8 * NW) ? (uint16_t)(*reinterpret_cast<const uint16_t*>(nib + nib_chunk_offset(v, i >> 3, 32 * NW) +
-                                                                              2 * (i & 7)) ^ 0x8888u)
-                                : (uint16_t)0;
+        if constexpr (nib_by_bit(32 * NW)) {
+            // lane j < 16 rebuilds record word j (dims 8j .. 8j + 7) from byte j of the four chunks
+            if (lane < 16) {
+                uint32_t W = 0;
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    const uint32_t b = nib[nib_chunk_offset(v, c, 32 * NW) + lane] ^ 0x88u;
+                    W |= ((b & 0xFu) << (4 * c)) | ((b >> 4) << (4 * c + 16));
+                }
+                r[2 * lane] = (uint16_t)W;
+                r[2 * lane + 1] = (uint16_t)(W >> 16);
+            }
+            r[32 + lane] = 0;  // nibbles 64..127 of the record, unused at head_dim 128
+        } else {
+            for (int i = lane; i < 64; i += 32)
+                r[i] = (i < 8 * NW) ? (uint16_t)(*reinterpret_cast<const uint16_t*>(
+                                                     nib + nib_chunk_offset(v, i >> 3, 32 * NW) + 2 * (i & 7)) ^
+                                                 0x8888u)
+                                    : (uint16_t)0;
+        }
         if (lane == 0) r[64] = reinterpret_cast<const uint16_t*>(P.rscale)[v];
     }
 }

@@ -48,10 +48,13 @@ __device__ __forceinline__ float tree_abs_sum(const float (&x)[NW]) {
 }
 
 // INT4 residual of x against sign bits w and binary scale s (residual.cu:30-77,
-// online_encode.cu:85-119).  On return lanes 8m (m < 4) hold nibble word 4k+m
-// in nw[k] (8 codes, element 8j low nibble first) and lanes 4m (m < 8) hold the
-// 16-bit pair of bytes 16k+2m, 16k+2m+1 in nh[k].
-template <int NW>
+// online_encode.cu:85-119).  Codes are two's complement.
+//  PLANE = false (reference records): lanes 4m (m < 8) hold the 16-bit pair of
+//    bytes 16k+2m, 16k+2m+1 of the reference byte order in nh[k].
+//  PLANE = true (nibble planes): at head_dim 128 (by-bit order) lanes c < 4
+//    hold word k of chunk c in nw[k]; at other head dims lanes 8m (m < 4) hold
+//    word m of chunk k in nw[k] (8 codes, element 8j low nibble first).
+template <int NW, bool PLANE>
 __device__ __forceinline__ float quantise_residual(const float (&x)[NW], const uint32_t (&w)[NW], float s, int lane,
                                                    uint32_t (&nw)[NW], uint32_t (&nh)[NW]) {
     float r[NW];
@@ -72,12 +75,21 @@ __device__ __forceinline__ float quantise_residual(const float (&x)[NW], const u
         int q = __float2int_rn(r[k] * inv_absmax);
         q = max(-7, min(7, q));
         const uint32_t nb = (uint32_t)q & 0xFu;
-        const uint32_t hi = __shfl_down_sync(0xffffffffu, nb, 1);
-        const uint32_t byte = nb | (hi << 4);
-        const uint32_t t1 = byte | (__shfl_down_sync(0xffffffffu, byte, 2) << 8);
-        const uint32_t t2 = t1 | (__shfl_down_sync(0xffffffffu, t1, 4) << 16);
-        nh[k] = t1;
-        nw[k] = t2;
+        if constexpr (PLANE && nib_by_bit(32 * NW)) {
+            // lane l holds dim 32k + l = 8(4k + b) + c + 4h with l = 8b + c + 4h:
+            // byte 4k + b of chunk c is (lane 8b + c, lane 8b + c + 4)
+            const uint32_t byte = nb | (__shfl_down_sync(0xffffffffu, nb, 4) << 4);
+            const uint32_t t1 = byte | (__shfl_down_sync(0xffffffffu, byte, 8) << 8);
+            nw[k] = t1 | (__shfl_down_sync(0xffffffffu, t1, 16) << 16);
+            nh[k] = 0;
+        } else {
+            const uint32_t hi = __shfl_down_sync(0xffffffffu, nb, 1);
+            const uint32_t byte = nb | (hi << 4);
+            const uint32_t t1 = byte | (__shfl_down_sync(0xffffffffu, byte, 2) << 8);
+            const uint32_t t2 = t1 | (__shfl_down_sync(0xffffffffu, t1, 4) << 16);
+            nh[k] = t1;
+            nw[k] = t2;
+        }
     }
     return absmax;
 }
@@ -94,21 +106,27 @@ __device__ __forceinline__ void store_sign_row(uint32_t* row, const uint32_t (&w
         if (lane == k) row[k] = w[k];
 }
 
-// Nibble word 4k+m of plane row `row` (chunk k, word m), interleaved layout,
-// stored offset-binary (each nibble holds code + 8).
+// The nibble chunks of plane row `row` from quantise_residual<NW, true>'s
+// words, interleaved layout, stored offset-binary (each nibble holds code + 8).
 template <int NW>
 __device__ __forceinline__ void store_nib_row(uint8_t* plane, int64_t row, const uint32_t (&nw)[NW], int lane) {
+    if constexpr (nib_by_bit(32 * NW)) {
+        if (lane < 4)  // chunk `lane`: words 0..3
+            *reinterpret_cast<uint4*>(plane + nib_chunk_offset(row, lane, 32 * NW)) =
+                make_uint4(nw[0] ^ 0x88888888u, nw[1] ^ 0x88888888u, nw[2] ^ 0x88888888u, nw[3] ^ 0x88888888u);
+    } else {
 #pragma unroll
-    for (int k = 0; k < NW; ++k)
-        if ((lane & 7) == 0)
-            *reinterpret_cast<uint32_t*>(plane + nib_chunk_offset(row, k, 32 * NW) + 4 * (lane >> 3)) =
-                nw[k] ^ 0x88888888u;  // offset-binary: code + 8
+        for (int k = 0; k < NW; ++k)
+            if ((lane & 7) == 0)
+                *reinterpret_cast<uint32_t*>(plane + nib_chunk_offset(row, k, 32 * NW) + 4 * (lane >> 3)) =
+                    nw[k] ^ 0x88888888u;  // offset-binary: code + 8
+    }
 }
 
 // Encode one vector and hand its pieces to `sink`:
 //   sink.sign(w, lane)       every lane holds all NW sign words
 //   sink.bscale(bits)        called on lane 0
-//   sink.nib(nw, lane)       lanes 8m hold nibble word 4k+m in nw[k] (two's-complement codes)
+//   sink.nib(nw, lane)       nibble words as quantise_residual<NW, true> leaves them (two's-complement codes)
 //   sink.rscale(bits)        called on lane 0
 // The plane writer below and the fused decode step (which also stages the
 // row in shared memory) are both sinks, so the arithmetic exists once.
@@ -123,7 +141,7 @@ __device__ __forceinline__ void encode_row(const float (&x)[NW], int lane, int h
     if (RES != BC_RES_NONE) {
         const float s = (RES == BC_RES_FP16_SCALE) ? __half2float(__ushort_as_half(sb)) : mean_abs;
         uint32_t nw[NW], nh[NW];
-        const float absmax = quantise_residual<NW>(x, w, s, lane, nw, nh);
+        const float absmax = quantise_residual<NW, true>(x, w, s, lane, nw, nh);
         sink.nib(nw, lane);
         if (lane == 0) sink.rscale(f2h_bits(absmax));
     }

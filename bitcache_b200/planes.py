@@ -88,19 +88,36 @@ class Planes:
             self.nib.fill_(0x88)
 
 
+def _by_bit(head_dim: int) -> bool:
+    """Nibble order of the planes: at head_dim 128 byte j of chunk c holds dims 8j + c
+    (low nibble) and 8j + c + 4 (high); at other head dims dims 32c + 2j and 32c + 2j + 1,
+    the reference's order."""
+    return head_dim == 128
+
+
 def nib_rows(nib: torch.Tensor, head_dim: int) -> torch.Tensor:
     """De-interleave a nibble plane [slots, kv_stride, head_dim/2] into per-position rows of
     the reference's byte format (two's-complement codes, element 2i in the low nibble)."""
     slots, stride = nib.shape[0], nib.shape[1]
     rows = (nib.reshape(slots, stride // 8, head_dim // 32, 8, 16).permute(0, 1, 3, 2, 4)
             .reshape(slots, stride, head_dim // 2))
-    return torch.bitwise_xor(rows, 0x88).contiguous()
+    rows = torch.bitwise_xor(rows, 0x88)
+    if _by_bit(head_dim):  # [c][j] chunk bytes -> codes in dim order (8j + 4e + c) -> reference bytes
+        p = rows.reshape(slots, stride, 4, 16)
+        codes = torch.stack([p & 0xF, p >> 4], -1).permute(0, 1, 3, 4, 2).reshape(slots, stride, head_dim)
+        rows = codes[..., 0::2] | (codes[..., 1::2] << 4)
+    return rows.contiguous()
 
 
 def nib_interleave(rows: torch.Tensor, head_dim: int) -> torch.Tensor:
     """Inverse of nib_rows: reference-format rows [slots, kv_stride, head_dim/2] -> plane bytes."""
     slots, stride = rows.shape[0], rows.shape[1]
-    x = torch.bitwise_xor(rows, 0x88)
+    x = rows
+    if _by_bit(head_dim):  # reference bytes -> codes in dim order -> [c][j] chunk bytes
+        codes = torch.stack([x & 0xF, x >> 4], -1).reshape(slots, stride, 16, 2, 4)
+        p = codes.permute(0, 1, 4, 2, 3)  # [c][j][e]
+        x = (p[..., 0] | (p[..., 1] << 4)).reshape(slots, stride, head_dim // 2)
+    x = torch.bitwise_xor(x, 0x88)
     return (x.reshape(slots, stride // 8, 8, head_dim // 32, 16).permute(0, 1, 3, 2, 4)
             .reshape(slots, stride, head_dim // 2).contiguous())
 
