@@ -67,7 +67,7 @@ __device__ unsigned int g_bc_device_error = 0;
 #define BC_DEC_MIN_CTAS_B1 5   // resident CTAs per SM the binary one-head kernel is held to
 #endif
 #ifndef BC_DEC_BIN_GC
-#define BC_DEC_BIN_GC 2        // most query heads per CTA in binary grouped-query caches (2: tensor-core value phase)
+#define BC_DEC_BIN_GC 4        // most query heads per CTA in binary grouped-query caches (binary C4: 4 heads 91 us, 2 heads 106 us)
 #endif
 #ifndef BC_DEC_GQA_GC
 #define BC_DEC_GQA_GC 4        // most query heads per CTA in compensated grouped-query caches at head_dim 128
@@ -139,9 +139,7 @@ struct DecCfg {
     // the ring, reused after the main loop by the merge records and the dump
     static constexpr int AFTER_B = MMA ? DUMP_OFF + DUMP_B : MERGE_B;
     static constexpr int BODY_B = RING_B > AFTER_B ? RING_B : AFTER_B;
-    static constexpr int QF_OFF = BODY_B;                       // float q[GC][D]
-    static constexpr int Q16_OFF = QF_OFF + GC * D * 4;         // int Q16[GC][D]
-    static constexpr int QSIGN_OFF = Q16_OFF + GC * D * 4;      // uint32 [GC][8]
+    static constexpr int QSIGN_OFF = BODY_B;                    // uint32 [GC][8]
     static constexpr int QCONST_OFF = QSIGN_OFF + GC * 8 * 4;   // [GC][4]: bco, rco, off8, eco
     // the residual score's query operand: dp4a packs, uint32 [GC][D/8][4], or
     // on the tensor-core path the A matrix of the score MMA, [4 chunks][2][16 rows][16 B]
@@ -156,16 +154,23 @@ struct DecCfg {
     static constexpr int NEWROW_B = NEWSIGN_B + D / 2 + 16;
     static constexpr int NEW_OFF = FLAG_OFF + 16;               // [2][NEWROW_B]: K row, V row
     static constexpr int NEWRAW_OFF = NEW_OFF + 2 * NEWROW_B;   // fp16 [2][D]: the new K, V rows as given
-    // Tensor-core path, per warp: the fixed-point key coefficients as bytes,
-    // [part: sign, code][8 NT rows: head * 4 + byte][48], and the residual
-    // score dots of the warp's 32 keys, int [GC][32].
+    // Scratch used either before the main loop (query preparation: q as
+    // float [GC][D], then Q16 int [GC][D]) or inside it (tensor-core path,
+    // per warp: the fixed-point key coefficients as bytes, [part: sign,
+    // code][8 NT rows: head * 4 + byte][48], and the residual score dots of
+    // the warp's 32 keys, int [GC][40]), never both at once.
+    static constexpr int SCR_OFF = NEWRAW_OFF + 4 * D;
+    static constexpr int QF_OFF = SCR_OFF;
+    static constexpr int Q16_OFF = QF_OFF + GC * D * 4;
     static constexpr int WB_ROW = 48;                           // padded: the fragment loads hit distinct banks
     static constexpr int WB_PART = 8 * NT * WB_ROW;
     static constexpr int WB_WARP = 2 * WB_PART;
-    static constexpr int DOT_WARP = GC * 40 * 4;  // int [GC][40]: the warp's 32 keys, padded rows
-    static constexpr int WB_OFF = NEWRAW_OFF + 4 * D;
+    static constexpr int DOT_WARP = GC * 40 * 4;
+    static constexpr int WB_OFF = SCR_OFF;
     static constexpr int DOT_OFF = WB_OFF + (MMA ? kWarps * WB_WARP : 0);
-    static constexpr int SMEM_B = DOT_OFF + (MMA ? kWarps * DOT_WARP : 0) + 128;  // + slack to align the base to 128 B
+    static constexpr int LOOP_SCR_B = MMA ? kWarps * (WB_WARP + DOT_WARP) : 0;
+    static constexpr int SCR_B = LOOP_SCR_B > 2 * GC * D * 4 ? LOOP_SCR_B : 2 * GC * D * 4;
+    static constexpr int SMEM_B = SCR_OFF + SCR_B + 128;       // + slack to align the base to 128 B
     static_assert(!MMA || DUMP_OFF + DUMP_B <= BODY_B, "accumulator dump exceeds the ring");
     // Resident CTAs per SM that shared memory allows at head_dim <= 128 with one
     // head per CTA; the register budget is held to it (0: no bound).
