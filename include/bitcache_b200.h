@@ -24,10 +24,13 @@
  *    [slot][position] with a row stride kv_stride (positions per slot):
  *        sign   uint32 [slots][kv_stride][head_dim/32]   bit i%32 of word i/32 = (x_i >= 0)
  *        nib    uint8  [slots][kv_stride][head_dim/2]    INT4 residual codes stored offset-binary
- *               (each nibble holds code + 8, i.e. the reference's byte XOR 0x88), interleaved in blocks
- *               of 8 positions: the 16-byte chunk c (dims 32c..32c+31, element 2i in the low
- *               nibble of byte i) of plane row r = slot*kv_stride + pos starts at byte
- *               (r/8)*(4*head_dim) + c*128 + (r%8)*16
+ *               (each nibble holds code + 8), interleaved in blocks of 8 positions: the
+ *               16-byte chunk c of plane row r = slot*kv_stride + pos starts at byte
+ *               (r/8)*(4*head_dim) + c*128 + (r%8)*16.  Byte j of chunk c holds
+ *                 head_dim 128:   dims 8j + c (low nibble) and 8j + c + 4 (high nibble),
+ *                                 the dims of bits c and c+4 of sign byte j;
+ *                 other head_dim: dims 32c + 2j (low) and 32c + 2j + 1 (high), the
+ *                                 reference's element order (its byte XOR 0x88).
  *        bscale fp16   [slots][kv_stride]                mean |x| (binary scale)
  *        rscale fp16   [slots][kv_stride]                residual absmax
  *    5*head_dim/8 + 4 bytes per vector (84 B at head_dim 128).  The field
