@@ -627,10 +627,10 @@ def main():
         vh = host_in[nq + nkv:].view(cache.batch, cache.n_kv_heads, d)
 
         def e2e_step(j):
-            cache.step(qh, kh, vh, out=oh)  # append + attend, one launch, host operands
+            cache.step(qh, kh, vh, out=oh)  # stage the inputs, then append + attend; host operands
 
-        path = ("BitCache.step (fused append + attend, one launch) on pinned host Q/K/V and output, which the "
-                "kernel reads and writes over the host link")
+        path = ("BitCache.step on pinned host Q/K/V and output: one staging launch copies the inputs to the "
+                "device (bc_stage_rows), then the fused append + attend launch writes the output over the host link")
         h2d, d2h = host_in.numel() * 2 * world, oh.numel() * 2 * world
     del k_all, v_all
     for j in range(n_warm):
@@ -650,7 +650,7 @@ def main():
     assert _lib.device_error() == 0, "device-side timeout during the end-to-end leg"
     e2e = {"value": job.bytes_total / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s", "ms_per_step": e2e_ms,
            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "path": path,
-           "gpu_launches_per_step": 2 if seq_split else 1}
+           "gpu_launches_per_step": 2 if (seq_split or not (adaptive or job.split in ("seq", "seqx"))) else 1}
 
     # ---- prefill encode throughput (fused binary + INT4 residual into planes) ----
     prefill = None

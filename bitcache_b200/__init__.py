@@ -74,6 +74,34 @@ class BitCache:
         self._res_mode = _planes.RES_FP32_SCALE if compensated else _planes.RES_NONE
         self._write_pos = 0
         self._filled = 0
+        self._n_slots = n_slots
+        # the planes never move: their C descriptors are built once
+        self._Kc, self._Vc = self._K.c(), self._V.c()
+        self._stage: Tensor | None = None  # device copy of a step's pinned Q, K, V
+        self._segs = None
+        self._ws_bytes: dict[int, int] = {}
+
+    def _staging(self, nq: int, nkv: int):
+        """The device buffer a step's pinned Q, K, V are staged into, and the
+        bc_copy_seg array of that copy (sources filled in per call)."""
+        if self._stage is None:
+            self._stage = torch.empty(nq + 2 * nkv, dtype=torch.float16, device=self._K.sign.device)
+            base = self._stage.data_ptr()
+            self._stage_ptrs = (base, base + 2 * nq, base + 2 * (nq + nkv))
+            self._segs = (_lib.CopySeg * 3)()
+            for i, (dst, n) in enumerate(zip(self._stage_ptrs, (nq, nkv, nkv))):
+                self._segs[i].dst, self._segs[i].bytes = dst, 2 * n
+        return self._segs, self._stage_ptrs
+
+    def _step_workspace(self, seq_len: int, dev: torch.device, stream: int) -> tuple[int | None, int]:
+        """Split-K workspace of a step over seq_len keys (sizes cached per length)."""
+        nbytes = self._ws_bytes.get(seq_len)
+        if nbytes is None:
+            nbytes = _lib.load().bc_decode_workspace_bytes(self._n_slots, self.n_heads // self.n_kv_heads, seq_len,
+                                                           self.head_dim)
+            self._ws_bytes[seq_len] = nbytes
+        ws = _lib.workspace(dev, stream, nbytes, ("decode", self._n_slots, self.n_heads // self.n_kv_heads))
+        return (None, 0) if ws is None else (ws.data_ptr(), ws.numel())
 
     # -- core API ------------------------------------------------------------
     def append(self, K: Tensor, V: Tensor) -> None:
@@ -112,25 +140,44 @@ class BitCache:
         contents.  The new token is encoded inside the attention kernel and
         attended from the encoder's output.
 
-        Q, K, V (and ``out``) may also be pinned host tensors: the kernel then
-        reads the step's inputs and writes the output over the host link
-        itself, so a host-driven decode loop needs no separate copies."""
+        Q, K, V (and ``out``) may also be pinned host tensors.  The inputs then
+        cross the host link once, staged into a device buffer by a small kernel
+        launched ahead of the step (bc_stage_rows), instead of once per split
+        CTA; the step kernel writes the output over the host link itself.  A
+        host loop that rewrites the pinned inputs synchronises on the previous
+        step first (it reads that step's output anyway)."""
         pinned = not Q.is_cuda
-        for t, name, shape in ((K, "K", (self.batch, self.n_kv_heads, self.head_dim)),
-                               (V, "V", (self.batch, self.n_kv_heads, self.head_dim)),
+        kv_shape = (self.batch, self.n_kv_heads, self.head_dim)
+        for t, name, shape in ((K, "K", kv_shape), (V, "V", kv_shape),
                                (Q, "Q", (self.batch, self.n_heads, self.head_dim))):
-            assert t.shape == torch.Size(shape), f"{name} shape {tuple(t.shape)} != {shape}"
+            assert t.shape == shape, f"{name} shape {tuple(t.shape)} != {shape}"
             assert t.dtype == torch.float16, f"{name} must be float16"
             assert t.is_contiguous(), f"{name} must be contiguous"
             assert (t.is_pinned() if pinned else t.is_cuda), f"{name}: all of Q, K, V on CUDA, or all pinned host"
-        if out is not None:
+        if out is None:
+            out = (torch.empty(Q.shape, dtype=torch.float16).pin_memory() if pinned
+                   else torch.empty(Q.shape, dtype=torch.float16, device=self.device))
+        else:
             assert out.shape == Q.shape and out.dtype == torch.float16 and out.is_contiguous(), "out mismatch"
+            assert out.is_cuda or out.is_pinned(), "out must be a CUDA tensor or pinned host memory"
         pos = self._write_pos
         filled = min(self._filled + 1, self.max_seq)
-        mode = _planes.MODE_COMPENSATED if self.compensated else _planes.MODE_BINARY
-        res = _planes.decode_step(Q.view(-1, self.head_dim), K.view(-1, self.head_dim), V.view(-1, self.head_dim),
-                                  self._K, self._V, filled, pos, mode, self._res_mode,
-                                  out=None if out is None else out.view(-1, self.head_dim))
+        lib = _lib.load()
+        dev = self._K.sign.device
+        st = _lib.stream_of(dev)
+        qp, kp, vp = Q.data_ptr(), K.data_ptr(), V.data_ptr()
+        if pinned and (qp | kp | vp) % 16 == 0:
+            # one host-link crossing per step: stage Q, K, V on the device first
+            segs, dev_ptrs = self._staging(Q.numel(), K.numel())
+            segs[0].src, segs[1].src, segs[2].src = qp, kp, vp
+            _lib.check(lib.bc_stage_rows(segs, 3, st), "stage_rows")
+            qp, kp, vp = dev_ptrs
+        ws, wsb = self._step_workspace(filled, dev, st)
+        mode = _lib.BC_MODE_COMPENSATED if self.compensated else _lib.BC_MODE_BINARY
+        _lib.check(lib.bc_decode_step(qp, kp, vp, self._Kc, self._Vc, out.data_ptr(), None, self._n_slots,
+                                      self.n_heads // self.n_kv_heads, filled, self._kv_stride, self.head_dim, mode,
+                                      pos, self._res_mode, ws, wsb, st), "decode_step")
+        res = out
         self._write_pos = (pos + 1) % self.max_seq
         self._filled = filled
         return res.view(self.batch, self.n_heads, self.head_dim)

@@ -43,6 +43,12 @@ class PageTable(ctypes.Structure):
                 ("n_pages", ctypes.c_int32)]
 
 
+class CopySeg(ctypes.Structure):
+    """bc_copy_seg: one host -> device segment of bc_stage_rows."""
+
+    _fields_ = [("src", c_void_p), ("dst", c_void_p), ("bytes", ctypes.c_uint64)]
+
+
 class Xchg(ctypes.Structure):
     """bc_xchg: every rank's exchange buffer as mapped here, world, rank, epoch, the
     poll limit of one exchange word (0: the library default) and the buffers' size."""
@@ -105,6 +111,7 @@ _SIGS = {
     "bc_select_residual_topk": (c_int, [KVPlanes, c_int, c_int, c_int64, c_int, c_int, c_void_p, c_int, c_void_p,
                                         c_size_t, c_void_p]),
     "bc_lse_merge": (c_int, [c_void_p, c_int, c_int64, c_int, c_void_p, c_void_p]),
+    "bc_stage_rows": (c_int, [c_void_p, c_int, c_void_p]),
     "bc_xnor_popcount": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int64, c_int, c_void_p]),
     "bc_records_to_planes": (c_int, [c_void_p, c_void_p, KVPlanes, c_int64, c_int, c_void_p]),
     "bc_planes_to_records": (c_int, [KVPlanes, c_void_p, c_void_p, c_int64, c_int, c_void_p]),

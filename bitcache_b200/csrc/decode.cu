@@ -433,7 +433,10 @@ __device__ __forceinline__ void init_soft(SoftState<GC, NP>& st) {
 // are then shifted down exactly.
 constexpr int kUUnset = -0x40000000;
 
-template <int GC>
+// BITMAP: a binary-only cache, whose rows need not line up with the codes'
+// (row tile t = sign bit t of bytes g8 / g8 + 8, 2^t units per unit: one
+// mask per fragment instead of a shift and a mask).
+template <int GC, bool BITMAP = false>
 struct MmaState {
     static constexpr int NT = (GC + 1) / 2;
     float m[GC];
@@ -443,8 +446,8 @@ struct MmaState {
     float em[GC], ez[GC], ew[GC];
 };
 
-template <int GC>
-__device__ __forceinline__ void init_soft(MmaState<GC>& st) {
+template <int GC, bool BM>
+__device__ __forceinline__ void init_soft(MmaState<GC, BM>& st) {
 #pragma unroll
     for (int g = 0; g < GC; ++g) {
         st.m[g] = -INFINITY;
@@ -456,7 +459,7 @@ __device__ __forceinline__ void init_soft(MmaState<GC>& st) {
         st.ew[g] = 0.0f;
     }
 #pragma unroll
-    for (int n = 0; n < MmaState<GC>::NT; ++n)
+    for (int n = 0; n < MmaState<GC, BM>::NT; ++n)
 #pragma unroll
         for (int t = 0; t < 8; ++t)
 #pragma unroll
@@ -782,8 +785,8 @@ __device__ __forceinline__ void residual_dots_mma(const uint8_t* knib, int kw, c
 // dropped low bits: each (row, tile) value is rebuilt from its four byte
 // columns (lanes with q = 2 (g % 2), 2 (g % 2) + 1 of column tile g / 2),
 // shifted, and split back into byte columns.
-template <int GC>
-__device__ __forceinline__ void mma_shift_down(MmaState<GC>& st, int g, int delta) {
+template <int GC, bool BM>
+__device__ __forceinline__ void mma_shift_down(MmaState<GC, BM>& st, int g, int delta) {
     const int q = threadIdx.x & 3;
     const bool mine = (q >> 1) == (g & 1), upper = q & 1;
     const int n = g >> 1;
@@ -805,11 +808,12 @@ __device__ __forceinline__ void mma_shift_down(MmaState<GC>& st, int g, int delt
 // One warp consumes its 32 keys (kw .. kw + 31) of a tile on the tensor-core
 // path.  RES = false: binary-only keys (a binary cache, or the adaptive
 // cache's second segment): no residual score, the sign part alone.
-template <int D, int GC, typename Cfg, bool ENT = false, bool RES = true>
-__device__ __forceinline__ void consume_warp_tile_mma(const QSmem& qs, MmaState<GC>& st, const uint8_t* sb, int kw,
-                                                      int nk, uint8_t* wb, int* dotb) {
+template <int D, int GC, typename Cfg, bool ENT = false, bool RES = true, bool BM = false>
+__device__ __forceinline__ void consume_warp_tile_mma(const QSmem& qs, MmaState<GC, BM>& st, const uint8_t* sb,
+                                                      int kw, int nk, uint8_t* wb, int* dotb) {
     static_assert(D == 128 && GC <= 4, "tensor-core path: head_dim 128, at most four heads per CTA");
-    constexpr int NT = MmaState<GC>::NT;
+    static_assert(!(BM && RES), "the binary row map has no room for codes");
+    constexpr int NT = MmaState<GC, BM>::NT;
     constexpr int WB_PART = 8 * NT * Cfg::WB_ROW;
     const int lane = threadIdx.x & 31;
     const int kk = kw + lane;
@@ -904,7 +908,16 @@ __device__ __forceinline__ void consume_warp_tile_mma(const QSmem& qs, MmaState<
         br[n][1] = (RES && ok) ? *reinterpret_cast<const uint32_t*>(rs + WB_PART + 16) : 0u;
     }
     // ---- sign part: bits c and c + 4 of sign bytes g8, g8 + 8 -------------------
-    {
+    if constexpr (BM) {  // binary row map: tile t = bit t of sign bytes g8, g8 + 8
+        uint32_t r0, r1, r2, r3;
+        ldsm_x2_trans_b8(sb + Cfg::OFF_VSIGN + kk * (D / 8), r0, r1, r2, r3);
+#pragma unroll
+        for (int t = 0; t < 8; ++t) {
+            const uint32_t mk = 0x01010101u << t;
+#pragma unroll
+            for (int n = 0; n < NT; ++n) mma_u8(st.acc[n][t], r0 & mk, r1 & mk, r2 & mk, r3 & mk, bs[n][0], bs[n][1]);
+        }
+    } else {
         uint32_t r0, r1, r2, r3;
         ldsm_x2_trans_b8(sb + Cfg::OFF_VSIGN + kk * (D / 8), r0, r1, r2, r3);
 #pragma unroll
@@ -1110,9 +1123,9 @@ __device__ __forceinline__ void warp_records(float* mg, SoftState<GC, Cfg::NP>& 
 // 4l .. 4l + 3 of every head: dim = 64 h + 8 g8 + c + 4 hi sits in row tile
 // 2c + h, row g8 + 8 hi (16 units per unit when hi), column tile g / 2, byte
 // columns 0-1 in lane 4 g8 + 2 (g % 2) and 2-3 in the lane after it.
-template <int D, int GC, typename Cfg>
-__device__ __forceinline__ void warp_records(float* mg, MmaState<GC>& st) {
-    constexpr int NT = MmaState<GC>::NT, DS = Cfg::DUMP_STRIDE;
+template <int D, int GC, typename Cfg, bool BM>
+__device__ __forceinline__ void warp_records(float* mg, MmaState<GC, BM>& st) {
+    constexpr int NT = MmaState<GC, BM>::NT, DS = Cfg::DUMP_STRIDE;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     int* dump = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(mg) + Cfg::DUMP_OFF) + warp * 32 * DS;
 #pragma unroll
@@ -1141,11 +1154,14 @@ __device__ __forceinline__ void warp_records(float* mg, MmaState<GC>& st) {
         for (int e = 0; e < 4; ++e) {
             const int dim = 4 * lane + e;
             const int h = dim >> 6, g8 = (dim >> 3) & 7, c = dim & 3, hi = (dim >> 2) & 1;
-            const int* la = dump + (4 * g8 + 2 * (g & 1)) * DS + 32 * (g >> 1) + 4 * (2 * c + h) + 2 * hi;
+            // shared map: tile 2c + h, row g8 + 8 hi; binary map: tile dim % 8, row g8 + 8 h
+            const int tile = BM ? (dim & 7) : 2 * c + h, upper = BM ? h : hi;
+            const int* la = dump + (4 * g8 + 2 * (g & 1)) * DS + 32 * (g >> 1) + 4 * tile + 2 * upper;
             const int* lb = la + DS;
             const uint64_t v0 = (uint64_t)(uint32_t)la[0] + ((uint64_t)(uint32_t)la[1] << 8);
             const uint64_t v1 = (uint64_t)(uint32_t)lb[0] + ((uint64_t)(uint32_t)lb[1] << 8);
-            const float v = ((float)v0 + 65536.0f * (float)v1) * (hi ? (1.0f / 16.0f) : 1.0f);
+            const float unit = BM ? exp2i(-(dim & 7)) : (hi ? (1.0f / 16.0f) : 1.0f);
+            const float v = ((float)v0 + 65536.0f * (float)v1) * unit;
             rec[2 + dim] = v * sc - t;
         }
     }
@@ -1604,7 +1620,7 @@ __global__ void __launch_bounds__(kDecThreads, DecCfg<D, GC, COMP>::MIN_CTAS)
     // the tensor-core value phase (in adaptive caches the binary-only
     // segment runs its sign part alone)
     constexpr bool MMA = Cfg::MMA;
-    std::conditional_t<MMA, MmaState<GC>, SoftState<GC, Cfg::NP>> st;
+    std::conditional_t<MMA, MmaState<GC, !COMP>, SoftState<GC, Cfg::NP>> st;
     init_soft(st);
 
     int it = 0;
@@ -1765,6 +1781,49 @@ __global__ void k_lse_merge(const float* __restrict__ parts, int n_parts, int64_
         }
         out[h * d + i] = __float2half((L > 0.0f) ? O / L : 0.0f);
     }
+}
+
+// Staging of a decode step's host-resident inputs (bc_stage_rows): every
+// thread loads its 16-byte pieces of the segments (pinned host memory, over
+// the host link) before waiting for the previous kernel in the stream, so the
+// link latency overlaps that kernel's tail, then stores them to device memory.
+// The decode kernel that follows (programmatic dependent launch) waits for
+// this grid and reads its q rows from device memory: one host-link crossing
+// per step instead of one per split CTA.
+constexpr int kStageThreads = 256;
+constexpr int kStageMaxSegs = 4;
+constexpr int kStagePerThread = 4;  // 16-byte pieces a thread holds between the loads and the wait
+struct StageArgs {
+    const uint4* src[kStageMaxSegs];
+    uint4* dst[kStageMaxSegs];
+    int64_t n16[kStageMaxSegs];  // 16-byte pieces of each segment
+    int n_segs;
+};
+
+__global__ void __launch_bounds__(kStageThreads) k_stage_rows(const StageArgs a) {
+    uint4 v[kStagePerThread];
+    int seg[kStagePerThread];
+    int64_t idx[kStagePerThread];
+    const int64_t first = ((int64_t)blockIdx.x * kStageThreads + threadIdx.x) * kStagePerThread;
+#pragma unroll
+    for (int j = 0; j < kStagePerThread; ++j) {
+        int64_t i = first + j;
+        seg[j] = -1;
+        for (int s = 0; s < a.n_segs; ++s) {
+            if (i < a.n16[s]) {
+                seg[j] = s;
+                idx[j] = i;
+                v[j] = a.src[s][i];
+                break;
+            }
+            i -= a.n16[s];
+        }
+    }
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+#pragma unroll
+    for (int j = 0; j < kStagePerThread; ++j)
+        if (seg[j] >= 0) a.dst[seg[j]][idx[j]] = v[j];
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
 __global__ void k_xnor_popcount(const __half* __restrict__ q, const uint32_t* __restrict__ ksign,
@@ -2492,6 +2551,37 @@ int bc_compensated_attention(const void* q, const void* k_bin, const void* k_res
                              void* workspace, size_t workspace_bytes, void* stream) {
     return record_attention(q, k_bin, k_res, v_bin, v_res, out, batch, n_heads, seq_len, head_dim, true, workspace,
                             workspace_bytes, stream);
+}
+
+int bc_stage_rows(const bc_copy_seg* segs, int n_segs, void* stream) {
+    if (n_segs < 0 || n_segs > kStageMaxSegs || (n_segs > 0 && !segs)) return BC_ERR_ARG;
+    StageArgs a{};
+    int64_t total = 0;
+    a.n_segs = n_segs;
+    for (int s = 0; s < n_segs; ++s) {
+        if (segs[s].bytes % 16 != 0) return BC_ERR_ALIGN;
+        if (segs[s].bytes > 0 && (!segs[s].src || !segs[s].dst)) return BC_ERR_ARG;
+        if (!bc_aligned(segs[s].src, 16) || !bc_aligned(segs[s].dst, 16)) return BC_ERR_ALIGN;
+        a.src[s] = reinterpret_cast<const uint4*>(segs[s].src);
+        a.dst[s] = reinterpret_cast<uint4*>(segs[s].dst);
+        a.n16[s] = (int64_t)(segs[s].bytes / 16);
+        total += a.n16[s];
+    }
+    if (total == 0) return BC_OK;
+    const int64_t per_cta = (int64_t)kStageThreads * kStagePerThread;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)((total + per_cta - 1) / per_cta));
+    cfg.blockDim = dim3(kStageThreads);
+    cfg.stream = (cudaStream_t)stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, k_stage_rows, a);
+    if (e != cudaSuccess) return BC_ERR_CUDA_BASE + (int)e;
+    BC_LAUNCH_CHECK();
+    return BC_OK;
 }
 
 int bc_lse_merge(const float* parts, int n_parts, int64_t n_heads, int head_dim, void* out, void* stream) {

@@ -427,6 +427,21 @@ def select_residual_topk(P: Planes, seq_len: int, n_keep: int, apply: bool = Tru
     return keep
 
 
+def stage_rows(pairs: list[tuple[torch.Tensor, torch.Tensor]]) -> None:
+    """bc_stage_rows: copy each (pinned host src, device dst) pair of equally sized,
+    16-byte aligned contiguous tensors with one kernel on the current stream of
+    the destinations' device.  The sources are read before the kernel waits for
+    the previous one in the stream, so no GPU work queued earlier may write them."""
+    if not 0 < len(pairs) <= 4:
+        raise RuntimeError("stage_rows takes 1 to 4 segments")
+    segs = (_lib.CopySeg * len(pairs))()
+    for i, (src, dst) in enumerate(pairs):
+        if src.nbytes != dst.nbytes or not src.is_contiguous() or not dst.is_contiguous():
+            raise RuntimeError("stage_rows: segments must be contiguous and of equal size")
+        segs[i].src, segs[i].dst, segs[i].bytes = src.data_ptr(), dst.data_ptr(), src.nbytes
+    _lib.check(_lib.load().bc_stage_rows(segs, len(pairs), _lib.stream_of(pairs[0][1].device)), "stage_rows")
+
+
 def lse_merge(parts: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
     """Merge partial triples float32 [n_parts, n_heads, head_dim + 2] -> fp16 [n_heads, head_dim]."""
     n_parts, n_heads, dp2 = parts.shape

@@ -143,3 +143,15 @@ def test_bitcache_import_name():
     assert F.compensated_attention is functional.compensated_attention
     assert C.online_encode_token is _C.online_encode_token
     assert callable(bitcache._require_extension)
+
+
+def test_stage_rows_argument_checks():
+    """bc_stage_rows refuses unaligned segments and too many segments before launching."""
+    lib = _lib.load()
+    segs = (_lib.CopySeg * 5)()
+    segs[0].src, segs[0].dst, segs[0].bytes = 16, 32, 24  # size not a multiple of 16
+    assert lib.bc_stage_rows(segs, 1, None) == 3
+    segs[0].src, segs[0].dst, segs[0].bytes = 8, 32, 32  # unaligned source
+    assert lib.bc_stage_rows(segs, 1, None) == 3
+    assert lib.bc_stage_rows(segs, 5, None) == 2  # at most 4 segments
+    assert lib.bc_stage_rows(segs, 0, None) == 0  # nothing to do

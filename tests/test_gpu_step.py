@@ -260,3 +260,22 @@ def test_step_mixed_host_and_device_rows_wait_for_the_previous_kernel(cuda):
         assert torch.equal(got, want), f"trial {trial}: the step read new_v before the previous kernel wrote it"
         planes_equal(Ka, Kc, S0 + 1, True)
         planes_equal(Va, Vc, S0 + 1, True)
+
+
+def test_stage_rows_copies_host_segments(cuda):
+    """bc_stage_rows copies pinned host segments to device memory exactly, with
+    the sources read ahead of the previous kernel and written after it."""
+    g = torch.Generator().manual_seed(41)
+    srcs = [torch.randint(0, 256, (n,), generator=g, dtype=torch.uint8).pin_memory() for n in (4096, 16, 80000)]
+    dsts = [torch.zeros(s.numel(), dtype=torch.uint8, device=cuda) for s in srcs]
+    # a long kernel ahead in the stream that also writes the destinations: the
+    # staged values must land after it
+    for d in dsts:
+        d.fill_(7)
+    torch.cuda._sleep(1_000_000)
+    for d in dsts:
+        d.fill_(9)
+    planes.stage_rows(list(zip(srcs, dsts)))
+    torch.cuda.synchronize()
+    for s, d in zip(srcs, dsts):
+        assert torch.equal(d.cpu(), s)
