@@ -34,17 +34,33 @@ __host__ __device__ __forceinline__ int64_t nib_chunk_offset(int64_t row, int c,
     return (row >> 3) * (int64_t)(4 * d) + (int64_t)c * 128 + (row & 7) * 16;
 }
 
-// Which dims a chunk holds.  Head dims other than 128 keep the reference's
-// element order: byte j of chunk c holds dims 32c + 2j (low nibble) and
-// 32c + 2j + 1 (high nibble).  At head_dim 128 the order is "by bit": byte j
-// of chunk c holds dims 8j + c (low) and 8j + c + 4 (high), so chunk c holds
-// exactly the dims of bits c and c + 4 of every sign byte, and the decode
-// kernel's tensor-core value phase gives a dim's sign bit and its code the
-// same accumulator row.  The values are the reference's; only their places
-// differ (the record converters permute).
-__host__ __device__ constexpr bool nib_by_bit(int d) { return d == 128; }
+// Which dims a chunk holds.  At head dims 64, 128 and 256 the order is "by
+// bit": every nibble byte holds bits t and t + 4 (t < 4) of one sign byte b,
+// i.e. dims 8b + t (low nibble) and 8b + t + 4 (high nibble), placed so that
+// the bytes of one 16-byte chunk line up with one 16-byte window of the sign
+// row (the decode kernel's tensor-core value phase then gives a dim's sign
+// bit and its code the same accumulator row):
+//   d = 128: byte j of chunk c is (b = j, t = c);
+//   d = 256: byte j of chunk c is (b = 16 (c / 4) + j, t = c % 4);
+//   d = 64:  byte j of chunk c is (b = j % 8, t = 2c + j / 8) (the sign row is
+//            8 bytes, so one 16-byte chunk holds two bits of each sign byte).
+// Other head dims keep the reference's element order: byte j of chunk c holds
+// dims 32c + 2j (low) and 32c + 2j + 1 (high).  The values are the
+// reference's; only their places differ (the record converters permute).
+__host__ __device__ constexpr bool nib_by_bit(int d) { return d == 64 || d == 128 || d == 256; }
 __host__ __device__ constexpr int nib_dim(int d, int c, int j, int hi) {
-    return nib_by_bit(d) ? 8 * j + c + 4 * hi : 32 * c + 2 * j + hi;
+    return d == 128   ? 8 * j + c + 4 * hi
+           : d == 256 ? 128 * (c / 4) + 8 * j + (c % 4) + 4 * hi
+           : d == 64  ? 8 * (j % 8) + 2 * c + j / 8 + 4 * hi
+                      : 32 * c + 2 * j + hi;
+}
+// Inverse of the by-bit order: the chunk and the byte within it that hold
+// bits t and t + 4 of sign byte b (t < 4).
+__host__ __device__ constexpr int nib_byte_chunk(int d, int b, int t) {
+    return d == 128 ? t : d == 256 ? 4 * (b / 16) + t : t / 2;
+}
+__host__ __device__ constexpr int nib_byte_index(int d, int b, int t) {
+    return d == 128 ? b : d == 256 ? b % 16 : 8 * (t % 2) + b;
 }
 
 // ---------------------------------------------------------------------------

@@ -85,7 +85,7 @@ __device__ unsigned int g_bc_device_error = 0;
 #define BC_DEC_MIN_TILES 1     // fewest 128-key tiles a split is planned with
 #endif
 #ifndef BC_DEC_MMA
-#define BC_DEC_MMA 1           // compensated head_dim-128 value phase on the tensor cores (u8 mma.sync)
+#define BC_DEC_MMA 1           // value phase on the tensor cores (u8 mma.sync); by-bit planes need it
 #endif
 constexpr int kDecThreads = BC_DEC_THREADS;
 constexpr int kWarps = kDecThreads / 32;
@@ -107,11 +107,16 @@ struct DecCfg {
     static constexpr int NS = (D == 256) ? 2 : BC_DEC_STAGES;  // ring stages
     static constexpr int LAG = 1;            // refill the stage consumed one tile ago
     static constexpr int T = kTile;
-    // Tensor-core value phase (head_dim 128, up to four heads per CTA): the
-    // value sums of GC heads are NT column tiles of 8 (two heads x four
-    // coefficient bytes each).
-    static constexpr bool MMA = BC_DEC_MMA && D == 128 && GC <= 4;
+    // Tensor-core value phase: the value sums of GC heads are NT column tiles
+    // of 8 (two heads x four coefficient bytes each) by NRT row tiles of 16
+    // dims.  Compensated caches at head dims 64, 128 (up to four heads per
+    // CTA) and 256 (up to two: 64 accumulator registers per head pair),
+    // binary ones at head_dim 128.  BM: the binary row map (MmaState).
+    static constexpr bool MMA =
+        BC_DEC_MMA && ((D == 128 && GC <= 4) || (COMP && ((D == 64 && GC <= 4) || (D == 256 && GC <= 2))));
+    static constexpr bool BM = MMA && !COMP;
     static constexpr int NT = (GC + 1) / 2;
+    static constexpr int NRT = D / 16;
     // Binary caches on the tensor-core path stage TPS tiles per ring slot (a
     // binary tile is only 4.6 KB at head_dim 128): attention and entropy
     // stream that many per stage, the step and record kernels one.
@@ -132,8 +137,8 @@ struct DecCfg {
     static constexpr int RING_B = NS * STAGE_B;
     static constexpr int MERGE_B = kWarps * GC * (D + 2) * 4;  // reuses the ring after the main loop
     // tensor-core value phase: the warps' accumulators are dumped after the
-    // merge records ([warp][lane][NT * 32 + 1] ints) for the final read-out
-    static constexpr int DUMP_STRIDE = NT * 32 + 1;
+    // merge records ([warp][lane][NT * NRT * 4 + 1] ints) for the final read-out
+    static constexpr int DUMP_STRIDE = NT * NRT * 4 + 1;
     static constexpr int DUMP_OFF = (MERGE_B + 127) & ~127;
     static constexpr int DUMP_B = kWarps * 32 * DUMP_STRIDE * 4;
     // the ring, reused after the main loop by the merge records and the dump
@@ -141,10 +146,12 @@ struct DecCfg {
     static constexpr int BODY_B = RING_B > AFTER_B ? RING_B : AFTER_B;
     static constexpr int QSIGN_OFF = BODY_B;                    // uint32 [GC][8]
     static constexpr int QCONST_OFF = QSIGN_OFF + GC * 8 * 4;   // [GC][4]: bco, rco, off8, eco
-    // the residual score's query operand: dp4a packs, uint32 [GC][D/8][4], or
-    // on the tensor-core path the A matrix of the score MMA, [4 chunks][2][16 rows][16 B]
+    // the residual score's query operand: dp4a packs, uint32 [GC][D/8][4]
+    // (the record kernel), and on the tensor-core path the A matrix of the
+    // score MMA, [D/32 chunks][2][16 rows][16 B]
     static constexpr int QPK_OFF = QCONST_OFF + GC * 4 * 4;
-    static constexpr int QPK_B = MMA ? 2048 : GC * (D / 8) * 16;
+    static constexpr int QPK_DP4A_B = GC * (D / 8) * 16;
+    static constexpr int QPK_B = (MMA && D * 16 > QPK_DP4A_B) ? D * 16 : QPK_DP4A_B;
     static constexpr int FULL_OFF = QPK_OFF + QPK_B;            // mbarriers
     static constexpr int EMPTY_OFF = FULL_OFF + NS * 8;         // mbarriers: all warps done with a stage
     static constexpr int FLAG_OFF = EMPTY_OFF + NS * 8;         // abort flag
@@ -285,12 +292,12 @@ __device__ __forceinline__ bool prefetch_query(const DecodeArgs& a, int slot, in
     return true;
 }
 
-// QMMA: the residual score runs on the tensor cores (head_dim 128): q is
+// QMMA: the residual score runs on the tensor cores (by-bit planes): q is
 // quantised to |Q16| <= 32639 and split into balanced digits Q16 = 256 hi + lo
 // with hi, lo in [-128, 127] (s8 operands); the A matrix of the score MMA,
 // [chunk c][half h][row][16 bytes], holds at byte k of row g (head g's hi
-// digit) / row 8 + g (its lo digit) the digit of dim 8k + c + 4h, the dims of
-// byte k of nibble chunk c (low nibble for h = 0, high for h = 1).
+// digit) / row 8 + g (its lo digit) the digit of dim nib_dim(D, c, k, h), the
+// dim of byte k of nibble chunk c (low nibble for h = 0, high for h = 1).
 // Otherwise q is quantised to |Q16| <= 32767 and packed for dp4a.
 template <int D, int GC, bool COMP, typename Cfg, bool QMMA = false>
 __device__ __forceinline__ void prepare_query(const DecodeArgs& a, int slot, int hg, uint8_t* smem,
@@ -383,16 +390,16 @@ __device__ __forceinline__ void prepare_query(const DecodeArgs& a, int slot, int
         }
     }
     if constexpr (QMMA && COMP) {
-        static_assert(D == 128 && GC <= 8, "score MMA: head_dim 128, at most 8 heads");
+        static_assert(nib_by_bit(D) && GC <= 8, "score MMA: by-bit planes, at most 8 heads");
         uint32_t* qa = reinterpret_cast<uint32_t*>(smem + Cfg::QPK_OFF);
-        for (int w = threadIdx.x; w < 512; w += kDecThreads) {  // word w: chunk, half, row, bytes 4k4..4k4+3
+        for (int w = threadIdx.x; w < D * 4; w += kDecThreads) {  // word w: chunk, half, row, bytes 4k4..4k4+3
             const int k4 = w & 3, row = (w >> 2) & 15, h = (w >> 6) & 1, c = w >> 7;
             const int g = row & 7;
             uint32_t word = 0;
             if (g < GC) {
 #pragma unroll
                 for (int b = 0; b < 4; ++b) {
-                    const int v = q16[g * D + 8 * (4 * k4 + b) + c + 4 * h];
+                    const int v = q16[g * D + nib_dim(D, c, 4 * k4 + b, h)];
                     const int lo = ((v + 128) & 255) - 128, hi = (v - lo) >> 8;
                     word |= ((uint32_t)(row < 8 ? hi : lo) & 0xFFu) << (8 * b);
                 }
@@ -434,20 +441,21 @@ __device__ __forceinline__ void init_soft(SoftState<GC, NP>& st) {
 constexpr int kUUnset = -0x40000000;
 
 // BITMAP: a binary-only cache, whose rows need not line up with the codes'
-// (row tile t = sign bit t of bytes g8 / g8 + 8, 2^t units per unit: one
-// mask per fragment instead of a shift and a mask).
-template <int GC, bool BITMAP = false>
+// (head_dim 128: row tile t = sign bit t of bytes g8 / g8 + 8, 2^t units per
+// unit: one mask per fragment instead of a shift and a mask).  NRT: row
+// tiles (head_dim / 16).
+template <int GC, bool BITMAP = false, int NRT = 8>
 struct MmaState {
     static constexpr int NT = (GC + 1) / 2;
     float m[GC];
     float l[GC], t[GC];
-    int acc[NT][8][4];
+    int acc[NT][NRT][4];
     int U[GC];
     float em[GC], ez[GC], ew[GC];
 };
 
-template <int GC, bool BM>
-__device__ __forceinline__ void init_soft(MmaState<GC, BM>& st) {
+template <int GC, bool BM, int NRT>
+__device__ __forceinline__ void init_soft(MmaState<GC, BM, NRT>& st) {
 #pragma unroll
     for (int g = 0; g < GC; ++g) {
         st.m[g] = -INFINITY;
@@ -459,9 +467,9 @@ __device__ __forceinline__ void init_soft(MmaState<GC, BM>& st) {
         st.ew[g] = 0.0f;
     }
 #pragma unroll
-    for (int n = 0; n < MmaState<GC, BM>::NT; ++n)
+    for (int n = 0; n < MmaState<GC, BM, NRT>::NT; ++n)
 #pragma unroll
-        for (int t = 0; t < 8; ++t)
+        for (int t = 0; t < NRT; ++t)
 #pragma unroll
             for (int i = 0; i < 4; ++i) st.acc[n][t][i] = 0;
 }
@@ -685,7 +693,7 @@ __device__ __forceinline__ void consume_warp_tile(const QState<D, GC>& qs, SoftS
 }
 
 // ---------------------------------------------------------------------------
-// Tensor-core path (head_dim 128, up to four query heads per CTA).
+// Tensor-core path (written out here for head_dim 128; 256 and 64 below).
 //
 // Score: the XNOR popcount stays on SIMT, one lane per key.  The INT4
 // residual dot sum_d u_d Q16_d of the warp's 32 keys and all GC heads is one
@@ -709,6 +717,18 @@ __device__ __forceinline__ void consume_warp_tile(const QState<D, GC>& qs, SoftS
 // ([part][head * 4 + byte][key]) and reads its B fragments (column g8 of
 // column tile n: head 2n + g8 / 4, byte g8 % 4; keys 4q.., 4q + 16..) as two
 // 32-bit words.
+//
+// head_dim 256: the same for each 16-byte window w of the 32-byte sign row:
+// row tile 8w + 2c + h holds dims 128w + 64h + 8g8 + c (+ 4), sign byte
+// 16w + 8h + g8 and nibble chunk 4w + c.
+// head_dim 64: the sign row is 8 bytes, so one ldmatrix .m16n16 .x1 .trans on
+// the warp's 256 sign bytes, read as 16 rows of two keys, hands lane (g8, q)
+// byte g8 of keys 8q + 2i (first register) and 8q + 2i + 1 (second), i < 4.
+// Row tile t (< 4) holds dims 8g8 + t (row g8) and 8g8 + t + 4 (row g8 + 8):
+// sign bits t and t + 4 of byte g8, and the two nibbles of byte 8 (t % 2) + g8
+// of chunk t / 2 (by-bit order at 64).  The sign fragments take the keys in
+// the order above, so the sign coefficients are written to the scratch at the
+// matching MMA k index (sign_k), the code coefficients in key order.
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void mma_u8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
                                        uint32_t b1) {
@@ -722,6 +742,14 @@ __device__ __forceinline__ void mma_s8u8(int (&d)[4], uint32_t a0, uint32_t a1, 
     asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.u8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
         : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// One 16x16 byte matrix, transposed: lanes 0-15 give its rows; lane (g8, q)
+// receives bytes 4q .. 4q + 3 of columns g8 (r0) and g8 + 8 (r1).
+__device__ __forceinline__ void ldsm_x1_trans_b8(const uint8_t* row, uint32_t& r0, uint32_t& r1) {
+    asm volatile("ldmatrix.sync.aligned.m16n16.x1.trans.shared.b8 {%0,%1}, [%2];"
+                 : "=r"(r0), "=r"(r1)
+                 : "r"(smem_u32(row)));
 }
 
 // Two 16x16 byte matrices, transposed: lanes 0-15 give the rows of the first,
@@ -756,42 +784,67 @@ constexpr int kDotRow = 40;  // ints per head row of a warp's dot buffer (padded
 // dotb[g * kDotRow + key] = sum_d u_d Q16_d (u = code + 8).  B fragments:
 // chunk c of an 8-key block is 8 consecutive 16-byte rows; lane (g8, q) gets
 // bytes 4q .. 4q + 3 of key g8, whose low nibbles are the k = 4q.. elements
-// (dims 8k + c) and whose high nibbles, shifted down, the k = 16 + 4q..
-// elements (dims 8k + c + 4).  D rows g / 8 + g are head g's hi / lo digit,
-// columns the keys, so dot = 256 D[g] + D[8 + g] stays in one lane.
-template <int GC>
+// and whose high nibbles, shifted down, the k = 16 + 4q.. elements of the
+// chunk's A matrix.  D rows g / 8 + g are head g's hi / lo digit, columns
+// the keys, so dot = 256 D[g] + D[8 + g] stays in one lane.  One x4 load
+// takes four chunks of a block (head_dim >= 128) or both chunks of two
+// blocks (head_dim 64).
+template <int D, int GC>
 __device__ __forceinline__ void residual_dots_mma(const uint8_t* knib, int kw, const uint8_t* qa, int* dotb) {
-    const int lane = threadIdx.x & 31, g8 = lane >> 2, q = lane & 3;
-    uint32_t a[4][4];
+    constexpr int NCH = D / 32, CG = NCH < 4 ? NCH : 4;
+    const int lane = threadIdx.x & 31, g8 = lane >> 2, q = lane & 3, mi = lane >> 3;
+    const uint8_t* kb = knib + (kw >> 3) * (4 * D) + 16 * (lane & 7);
+    int acc[4][4];
 #pragma unroll
-    for (int c = 0; c < 4; ++c)
-        ldsm_x4(qa + ((2 * c + (lane >> 4)) * 16 + ((lane >> 3) & 1) * 8 + (lane & 7)) * 16, a[c][0], a[c][1],
-                a[c][2], a[c][3]);
+    for (int j = 0; j < 4; ++j)
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-        uint32_t nb[4];
-        ldsm_x4(knib + ((kw + 8 * j) >> 3) * 512 + 128 * (lane >> 3) + 16 * (lane & 7), nb[0], nb[1], nb[2], nb[3]);
-        int acc[4] = {0, 0, 0, 0};
+        for (int i = 0; i < 4; ++i) acc[j][i] = 0;
 #pragma unroll
-        for (int c = 0; c < 4; ++c)
-            mma_s8u8(acc, a[c][0], a[c][1], a[c][2], a[c][3], nb[c] & 0x0F0F0F0Fu, (nb[c] >> 4) & 0x0F0F0F0Fu);
-        if (g8 < GC)
-            *reinterpret_cast<int2*>(dotb + g8 * kDotRow + 8 * j + 2 * q) =
-                make_int2(acc[0] * 256 + acc[2], acc[1] * 256 + acc[3]);
+    for (int c0 = 0; c0 < NCH; c0 += CG) {
+        uint32_t a[CG][4];
+#pragma unroll
+        for (int c = 0; c < CG; ++c)
+            ldsm_x4(qa + ((2 * (c0 + c) + (lane >> 4)) * 16 + ((lane >> 3) & 1) * 8 + (lane & 7)) * 16, a[c][0],
+                    a[c][1], a[c][2], a[c][3]);
+        if constexpr (NCH >= 4) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                uint32_t nb[4];
+                ldsm_x4(kb + j * (4 * D) + 128 * (c0 + mi), nb[0], nb[1], nb[2], nb[3]);
+#pragma unroll
+                for (int c = 0; c < 4; ++c)
+                    mma_s8u8(acc[j], a[c][0], a[c][1], a[c][2], a[c][3], nb[c] & 0x0F0F0F0Fu, (nb[c] >> 4) & 0x0F0F0F0Fu);
+            }
+        } else {  // head_dim 64: matrix mi = block 2jj + mi / 2, chunk mi % 2
+#pragma unroll
+            for (int jj = 0; jj < 2; ++jj) {
+                uint32_t nb[4];
+                ldsm_x4(kb + (2 * jj + (mi >> 1)) * (4 * D) + 128 * (mi & 1), nb[0], nb[1], nb[2], nb[3]);
+#pragma unroll
+                for (int m = 0; m < 4; ++m)
+                    mma_s8u8(acc[2 * jj + (m >> 1)], a[m & 1][0], a[m & 1][1], a[m & 1][2], a[m & 1][3],
+                             nb[m] & 0x0F0F0F0Fu, (nb[m] >> 4) & 0x0F0F0F0Fu);
+            }
+        }
     }
+    if (g8 < GC)
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+            *reinterpret_cast<int2*>(dotb + g8 * kDotRow + 8 * j + 2 * q) =
+                make_int2(acc[j][0] * 256 + acc[j][2], acc[j][1] * 256 + acc[j][3]);
 }
 
 // Divide head g's accumulators by 2^delta (delta >= 1), exactly up to the
 // dropped low bits: each (row, tile) value is rebuilt from its four byte
 // columns (lanes with q = 2 (g % 2), 2 (g % 2) + 1 of column tile g / 2),
 // shifted, and split back into byte columns.
-template <int GC, bool BM>
-__device__ __forceinline__ void mma_shift_down(MmaState<GC, BM>& st, int g, int delta) {
+template <int GC, bool BM, int NRT>
+__device__ __forceinline__ void mma_shift_down(MmaState<GC, BM, NRT>& st, int g, int delta) {
     const int q = threadIdx.x & 3;
     const bool mine = (q >> 1) == (g & 1), upper = q & 1;
     const int n = g >> 1;
 #pragma unroll
-    for (int t = 0; t < 8; ++t)
+    for (int t = 0; t < NRT; ++t)
 #pragma unroll
         for (int r = 0; r < 2; ++r) {
             const uint64_t v = (uint64_t)(uint32_t)st.acc[n][t][2 * r] + ((uint64_t)(uint32_t)st.acc[n][t][2 * r + 1] << 8);
@@ -808,30 +861,45 @@ __device__ __forceinline__ void mma_shift_down(MmaState<GC, BM>& st, int g, int 
 // One warp consumes its 32 keys (kw .. kw + 31) of a tile on the tensor-core
 // path.  RES = false: binary-only keys (a binary cache, or the adaptive
 // cache's second segment): no residual score, the sign part alone.
-template <int D, int GC, typename Cfg, bool ENT = false, bool RES = true, bool BM = false>
-__device__ __forceinline__ void consume_warp_tile_mma(const QSmem& qs, MmaState<GC, BM>& st, const uint8_t* sb,
+template <int D, int GC, typename Cfg, bool ENT = false, bool RES = true, bool BM = false, int NRT = 8>
+__device__ __forceinline__ void consume_warp_tile_mma(const QSmem& qs, MmaState<GC, BM, NRT>& st, const uint8_t* sb,
                                                       int kw, int nk, uint8_t* wb, int* dotb) {
-    static_assert(D == 128 && GC <= 4, "tensor-core path: head_dim 128, at most four heads per CTA");
-    static_assert(!(BM && RES), "the binary row map has no room for codes");
-    constexpr int NT = MmaState<GC, BM>::NT;
+    static_assert(nib_by_bit(D) && NRT == D / 16, "tensor-core path: head dims 64, 128, 256");
+    static_assert(!(BM && RES) && !(BM && D != 128), "the binary row map: head_dim 128, no codes");
+    constexpr int NT = MmaState<GC, BM, NRT>::NT, NWD = D / 32;
     constexpr int WB_PART = 8 * NT * Cfg::WB_ROW;
     const int lane = threadIdx.x & 31;
     const int kk = kw + lane;
     const bool valid = kk < nk;
     if constexpr (RES) {
-        residual_dots_mma<GC>(sb + Cfg::OFF_KNIB, kw, qs.qa, dotb);
+        residual_dots_mma<D, GC>(sb + Cfg::OFF_KNIB, kw, qs.qa, dotb);
         __syncwarp();
     }
     // ---- score phase: lane `lane` scores key kk for the GC heads ----------------
-    const uint4 ks = *reinterpret_cast<const uint4*>(sb + Cfg::OFF_KSIGN + kk * (D / 8));
+    uint32_t ks[NWD];
+    if constexpr (NWD == 2) {
+        const uint2 v = *reinterpret_cast<const uint2*>(sb + Cfg::OFF_KSIGN + kk * (D / 8));
+        ks[0] = v.x;
+        ks[1] = v.y;
+    } else {
+#pragma unroll
+        for (int c = 0; c < NWD / 4; ++c) {
+            const uint4 v = *reinterpret_cast<const uint4*>(sb + Cfg::OFF_KSIGN + kk * (D / 8) + 16 * c);
+            ks[4 * c] = v.x;
+            ks[4 * c + 1] = v.y;
+            ks[4 * c + 2] = v.z;
+            ks[4 * c + 3] = v.w;
+        }
+    }
     const float kbs = __half2float(reinterpret_cast<const __half*>(sb + Cfg::OFF_KBS)[kk]);
     const float krs = RES ? __half2float(reinterpret_cast<const __half*>(sb + Cfg::OFF_KRS)[kk]) : 0.0f;
     float s2[GC];
 #pragma unroll
     for (int g = 0; g < GC; ++g) {
-        const uint4 qv = *reinterpret_cast<const uint4*>(qs.sign + 8 * g);
         const float4 cst = *reinterpret_cast<const float4*>(qs.c + 4 * g);  // bco, rco, off8, eco
-        const int pop = __popc(qv.x ^ ks.x) + __popc(qv.y ^ ks.y) + __popc(qv.z ^ ks.z) + __popc(qv.w ^ ks.w);
+        int pop = 0;
+#pragma unroll
+        for (int k = 0; k < NWD; ++k) pop += __popc(qs.sign[8 * g + k] ^ ks[k]);
         float s = cst.x * kbs * (float)(D - 2 * pop);
         if (RES) s = fmaf(cst.y * krs, (float)(dotb[g * kDotRow + lane] - __float_as_int(cst.z)), s);
         s2[g] = valid ? s : -INFINITY;
@@ -889,9 +957,11 @@ __device__ __forceinline__ void consume_warp_tile_mma(const QSmem& qs, MmaState<
         }
         const bool have = st.U[g] != kUUnset;
         const uint32_t A = have ? __float2uint_rn(xa) : 0u, R = have ? __float2uint_rn(xr) : 0u;
+        // head_dim 64: the sign fragments' k index of key `lane` (see above)
+        const int sign_k = (D == 64) ? ((lane & 1) ? 16 : 0) + 4 * (lane >> 3) + ((lane & 7) >> 1) : lane;
 #pragma unroll
         for (int n = 0; n < 4; ++n) {
-            wb[(4 * g + n) * Cfg::WB_ROW + lane] = (uint8_t)(A >> (8 * n));
+            wb[(4 * g + n) * Cfg::WB_ROW + sign_k] = (uint8_t)(A >> (8 * n));
             if (RES) wb[WB_PART + (4 * g + n) * Cfg::WB_ROW + lane] = (uint8_t)(R >> (8 * n));
         }
     }
@@ -917,18 +987,32 @@ __device__ __forceinline__ void consume_warp_tile_mma(const QSmem& qs, MmaState<
 #pragma unroll
             for (int n = 0; n < NT; ++n) mma_u8(st.acc[n][t], r0 & mk, r1 & mk, r2 & mk, r3 & mk, bs[n][0], bs[n][1]);
         }
+    } else if constexpr (D == 64) {  // tile t: bits t, t + 4 of sign byte g8; keys in sign_k order
+        uint32_t r0, r1;
+        ldsm_x1_trans_b8(sb + Cfg::OFF_VSIGN + kw * (D / 8) + 16 * (lane & 15), r0, r1);
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+            const uint32_t s0 = r0 >> t, s1 = r1 >> t;
+#pragma unroll
+            for (int n = 0; n < NT; ++n)
+                mma_u8(st.acc[n][t], s0 & 0x01010101u, s0 & 0x10101010u, s1 & 0x01010101u, s1 & 0x10101010u,
+                       bs[n][0], bs[n][1]);
+        }
     } else {
-        uint32_t r0, r1, r2, r3;
-        ldsm_x2_trans_b8(sb + Cfg::OFF_VSIGN + kk * (D / 8), r0, r1, r2, r3);
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-            const uint32_t s0 = r0 >> c, s1 = r1 >> c, s2b = r2 >> c, s3 = r3 >> c;
+        for (int w = 0; w < D / 128; ++w) {  // 16-byte window w of the sign row: tiles 8w ..
+            uint32_t r0, r1, r2, r3;
+            ldsm_x2_trans_b8(sb + Cfg::OFF_VSIGN + kk * (D / 8) + 16 * w, r0, r1, r2, r3);
 #pragma unroll
-            for (int n = 0; n < NT; ++n) {
-                mma_u8(st.acc[n][2 * c], s0 & 0x01010101u, s0 & 0x10101010u, s2b & 0x01010101u, s2b & 0x10101010u,
-                       bs[n][0], bs[n][1]);
-                mma_u8(st.acc[n][2 * c + 1], s1 & 0x01010101u, s1 & 0x10101010u, s3 & 0x01010101u, s3 & 0x10101010u,
-                       bs[n][0], bs[n][1]);
+            for (int c = 0; c < 4; ++c) {
+                const uint32_t s0 = r0 >> c, s1 = r1 >> c, s2b = r2 >> c, s3 = r3 >> c;
+#pragma unroll
+                for (int n = 0; n < NT; ++n) {
+                    mma_u8(st.acc[n][8 * w + 2 * c], s0 & 0x01010101u, s0 & 0x10101010u, s2b & 0x01010101u,
+                           s2b & 0x10101010u, bs[n][0], bs[n][1]);
+                    mma_u8(st.acc[n][8 * w + 2 * c + 1], s1 & 0x01010101u, s1 & 0x10101010u, s3 & 0x01010101u,
+                           s3 & 0x10101010u, bs[n][0], bs[n][1]);
+                }
             }
         }
     }
@@ -936,14 +1020,18 @@ __device__ __forceinline__ void consume_warp_tile_mma(const QSmem& qs, MmaState<
     if constexpr (RES) {
         const uint8_t* vn = sb + Cfg::OFF_VNIB + (kk >> 3) * (4 * D) + 16 * (kk & 7);
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
+        for (int c = 0; c < D / 32; ++c) {
             uint32_t r0, r1, r2, r3;
             ldsm_x2_trans_b8(vn + 128 * c, r0, r1, r2, r3);
+            // row tiles of the chunk's bytes g8 and g8 + 8: 2c, 2c + 1 (head_dim 64:
+            // chunk c holds tiles 2c, 2c + 1 as its two byte halves); head_dim 256:
+            // window c / 4, tiles 8 (c / 4) + 2 (c % 4) (+ 1)
+            const int t0 = (D == 256) ? 8 * (c >> 2) + 2 * (c & 3) : 2 * c;
 #pragma unroll
             for (int n = 0; n < NT; ++n) {
-                mma_u8(st.acc[n][2 * c], r0 & 0x0F0F0F0Fu, r0 & 0xF0F0F0F0u, r2 & 0x0F0F0F0Fu, r2 & 0xF0F0F0F0u,
+                mma_u8(st.acc[n][t0], r0 & 0x0F0F0F0Fu, r0 & 0xF0F0F0F0u, r2 & 0x0F0F0F0Fu, r2 & 0xF0F0F0F0u,
                        br[n][0], br[n][1]);
-                mma_u8(st.acc[n][2 * c + 1], r1 & 0x0F0F0F0Fu, r1 & 0xF0F0F0F0u, r3 & 0x0F0F0F0Fu, r3 & 0xF0F0F0F0u,
+                mma_u8(st.acc[n][t0 + 1], r1 & 0x0F0F0F0Fu, r1 & 0xF0F0F0F0u, r3 & 0x0F0F0F0Fu, r3 & 0xF0F0F0F0u,
                        br[n][0], br[n][1]);
             }
         }
@@ -1120,20 +1208,21 @@ __device__ __forceinline__ void warp_records(float* mg, SoftState<GC, Cfg::NP>& 
 
 // The same record from the tensor-core accumulators.  Each lane dumps its
 // fragments to shared memory (the ring is free by now); lane l then takes dims
-// 4l .. 4l + 3 of every head: dim = 64 h + 8 g8 + c + 4 hi sits in row tile
-// 2c + h, row g8 + 8 hi (16 units per unit when hi), column tile g / 2, byte
-// columns 0-1 in lane 4 g8 + 2 (g % 2) and 2-3 in the lane after it.
-template <int D, int GC, typename Cfg, bool BM>
-__device__ __forceinline__ void warp_records(float* mg, MmaState<GC, BM>& st) {
-    constexpr int NT = MmaState<GC, BM>::NT, DS = Cfg::DUMP_STRIDE;
+// (D / 32) l .. of every head: dim = 128 w + 64 h + 8 g8 + c + 4 hi sits in row
+// tile 8 w + 2c + h (head_dim 64: tile c + 2 h', dim = 8 g8 + 2 h' + c' + 4 hi,
+// i.e. tile dim % 4), row g8 + 8 hi (16 units per unit when hi), column tile
+// g / 2, byte columns 0-1 in lane 4 g8 + 2 (g % 2) and 2-3 in the lane after it.
+template <int D, int GC, typename Cfg, bool BM, int NRT>
+__device__ __forceinline__ void warp_records(float* mg, MmaState<GC, BM, NRT>& st) {
+    constexpr int NT = MmaState<GC, BM, NRT>::NT, DS = Cfg::DUMP_STRIDE;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     int* dump = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(mg) + Cfg::DUMP_OFF) + warp * 32 * DS;
 #pragma unroll
     for (int n = 0; n < NT; ++n)
 #pragma unroll
-        for (int t = 0; t < 8; ++t)
+        for (int t = 0; t < NRT; ++t)
 #pragma unroll
-            for (int i = 0; i < 4; ++i) dump[lane * DS + 32 * n + 4 * t + i] = st.acc[n][t][i];
+            for (int i = 0; i < 4; ++i) dump[lane * DS + 4 * NRT * n + 4 * t + i] = st.acc[n][t][i];
     __syncwarp();
 #pragma unroll
     for (int g = 0; g < GC; ++g) {
@@ -1151,12 +1240,13 @@ __device__ __forceinline__ void warp_records(float* mg, MmaState<GC, BM>& st) {
         // accumulator unit relative to the warp's max: 2^(U - m)
         const float sc = (st.U[g] != kUUnset && st.m[g] > -INFINITY) ? exp2f((float)st.U[g] - st.m[g]) : 0.0f;
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            const int dim = 4 * lane + e;
-            const int h = dim >> 6, g8 = (dim >> 3) & 7, c = dim & 3, hi = (dim >> 2) & 1;
-            // shared map: tile 2c + h, row g8 + 8 hi; binary map: tile dim % 8, row g8 + 8 h
-            const int tile = BM ? (dim & 7) : 2 * c + h, upper = BM ? h : hi;
-            const int* la = dump + (4 * g8 + 2 * (g & 1)) * DS + 32 * (g >> 1) + 4 * tile + 2 * upper;
+        for (int e = 0; e < D / 32; ++e) {
+            const int dim = (D / 32) * lane + e;
+            const int h = (dim >> 6) & 1, w = dim >> 7, g8 = (dim >> 3) & 7, c = dim & 3, hi = (dim >> 2) & 1;
+            // shared map: tile 8w + 2c + h (head_dim 64: tile c), row g8 + 8 hi;
+            // binary map (head_dim 128): tile dim % 8, row g8 + 8 h
+            const int tile = BM ? (dim & 7) : (D == 64 ? c : 8 * w + 2 * c + h), upper = BM ? h : hi;
+            const int* la = dump + (4 * g8 + 2 * (g & 1)) * DS + 4 * NRT * (g >> 1) + 4 * tile + 2 * upper;
             const int* lb = la + DS;
             const uint64_t v0 = (uint64_t)(uint32_t)la[0] + ((uint64_t)(uint32_t)la[1] << 8);
             const uint64_t v1 = (uint64_t)(uint32_t)lb[0] + ((uint64_t)(uint32_t)lb[1] << 8);
@@ -1364,10 +1454,8 @@ struct StagedRowSink {
     }
     __device__ __forceinline__ void nib(const uint32_t (&nw)[NW], int lane) {
         if (store) g.nib(nw, lane);
-        if constexpr (nib_by_bit(32 * NW)) {  // lanes c < 4 hold chunk c
-            if (lane < 4)
-                *reinterpret_cast<uint4*>(srow + nib_off + 16 * lane) =
-                    make_uint4(nw[0] ^ 0x88888888u, nw[1] ^ 0x88888888u, nw[2] ^ 0x88888888u, nw[3] ^ 0x88888888u);
+        if constexpr (nib_by_bit(32 * NW)) {  // lanes L < 4 hold the row's words (staged chunks 16 B apart)
+            if (lane < 4) nib_words_to<NW>(srow + nib_off, 16, nw, lane);
         } else {
 #pragma unroll
             for (int k = 0; k < NW; ++k)
@@ -1465,7 +1553,8 @@ __global__ void __launch_bounds__(kDecThreads, DecCfg<D, GC, COMP>::MIN_CTAS)
     k_decode_planes(const DecodeArgs a) {
     constexpr bool STEP = VAR == 1, ENT = VAR == 2, ADA = VAR == 3;
     using Cfg = DecCfg<D, GC, COMP>;
-    static_assert(Cfg::MMA || !nib_by_bit(D), "head_dim-128 planes (by-bit nibble order) need the tensor-core path");
+    static_assert(Cfg::MMA || !COMP || !nib_by_bit(D),
+                  "compensated planes in the by-bit nibble order need the tensor-core path");
     constexpr int NS = Cfg::NS, LAG = Cfg::LAG, T = Cfg::T;
     extern __shared__ __align__(128) uint8_t smem_raw[];
     uint8_t* smem = aligned_smem(smem_raw);
@@ -1620,7 +1709,7 @@ __global__ void __launch_bounds__(kDecThreads, DecCfg<D, GC, COMP>::MIN_CTAS)
     // the tensor-core value phase (in adaptive caches the binary-only
     // segment runs its sign part alone)
     constexpr bool MMA = Cfg::MMA;
-    std::conditional_t<MMA, MmaState<GC, !COMP>, SoftState<GC, Cfg::NP>> st;
+    std::conditional_t<MMA, MmaState<GC, Cfg::BM, Cfg::NRT>, SoftState<GC, Cfg::NP>> st;
     init_soft(st);
 
     int it = 0;
@@ -1864,13 +1953,14 @@ struct Plan {
 
 
 // Query heads handled per CTA, so that one read of every KV key serves them
-// all: at head_dim 128 (tensor-core path) up to four heads of a slot's group
-// for compensated caches, whose accumulators hold two heads per column tile;
-// elsewhere two (compensated, f32x2 value phase) or BC_DEC_BIN_GC (binary).
+// all: compensated caches at head dims 64 and 128 (tensor-core path) up to
+// four heads of a slot's group, whose accumulators hold two heads per column
+// tile; at 256 (tensor-core path, 64 accumulator registers per head pair) and
+// at 32 (f32x2 value phase) two; binary caches BC_DEC_BIN_GC.
 // The CTAs of a slot's remaining head groups, adjacent in the grid, share the
 // KV tiles through L2.
 int heads_per_cta(int group, int d, bool comp) {
-    const int cap = comp ? ((BC_DEC_MMA && d == 128) ? BC_DEC_GQA_GC : 2) : BC_DEC_BIN_GC;
+    const int cap = comp ? ((BC_DEC_MMA && (d == 64 || d == 128)) ? BC_DEC_GQA_GC : 2) : BC_DEC_BIN_GC;
     return group < cap ? group : cap;
 }
 
@@ -2107,7 +2197,7 @@ int run_decode_d(const DecodeArgs& a, bool comp, int var, void* ws, size_t wsb, 
             return comp ? run_decode_t<D, 2, true>(a, var, ws, wsb, st, fit)
                         : run_decode_t<D, 2, false>(a, var, ws, wsb, st, fit);
         default:
-            if constexpr (D == 128) {
+            if constexpr (D == 64 || D == 128) {
                 if (comp) return run_decode_t<D, 4, true>(a, var, ws, wsb, st, fit);
             }
             if (comp) return BC_ERR_UNSUPPORTED;

@@ -194,7 +194,7 @@ __device__ __forceinline__ float lpv_abs_sum(const uint4* row) {
     return v0 + v1;                                                                      // stride 1
 }
 
-// ---- head_dim 128: two passes over the row ------------------------------
+// ---- head_dim 64 and 128 (by-bit nibble order): two passes over the row ----
 // Pass 1 sums |x| in the reference's tree order (as lpv_tree16) and also keeps
 // min |x| and max |x| (fp16, exact).  The residual's absmax needs no pass of
 // its own: |x - rec| = |fl(|x| - sc)| for every element (rec = +sc for
@@ -248,9 +248,12 @@ __device__ __forceinline__ float2 h2_to_f2(uint32_t h2) {
     return __half22float2(*reinterpret_cast<const __half2*>(&h2));
 }
 
-template <int L, int K>
+template <int D, int L, int K>
 __device__ __forceinline__ void lpv_tree16_mm(const uint4* row, float (&out)[8], __half2& mx, __half2& mn) {
-    if constexpr (L == 4) {  // leaf: chunk K of the 16 (head_dim 128)
+    if constexpr (L == 4 && 8 * K >= D) {  // leaf beyond head_dim: zeros
+#pragma unroll
+        for (int j = 0; j < 8; ++j) out[j] = 0.0f;
+    } else if constexpr (L == 4) {  // leaf: chunk K
         const uint4 t = row[K];
         const uint32_t w[4] = {t.x & 0x7FFF7FFFu, t.y & 0x7FFF7FFFu, t.z & 0x7FFF7FFFu, t.w & 0x7FFF7FFFu};
 #pragma unroll
@@ -262,10 +265,13 @@ __device__ __forceinline__ void lpv_tree16_mm(const uint4* row, float (&out)[8],
             out[2 * i] = f.x;
             out[2 * i + 1] = f.y;
         }
+    } else if constexpr (8 * (K + (1 << L)) >= D) {
+        // the right subtree covers chunks beyond head_dim only: adding +0.0f is exact for a >= 0
+        lpv_tree16_mm<D, L + 1, K>(row, out, mx, mn);
     } else {
         float right[8];
-        lpv_tree16_mm<L + 1, K>(row, out, mx, mn);
-        lpv_tree16_mm<L + 1, K + (1 << L)>(row, right, mx, mn);
+        lpv_tree16_mm<D, L + 1, K>(row, out, mx, mn);
+        lpv_tree16_mm<D, L + 1, K + (1 << L)>(row, right, mx, mn);
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
             const float2 s = add2_ftz(make_float2(out[2 * i], out[2 * i + 1]), make_float2(right[2 * i], right[2 * i + 1]));
@@ -275,13 +281,14 @@ __device__ __forceinline__ void lpv_tree16_mm(const uint4* row, float (&out)[8],
     }
 }
 
-template <int RES>
-__device__ __forceinline__ void lpv_encode_row_128(const uint4* row, bc_kv_planes P, int64_t v, int seq_len,
-                                                   int64_t kv_stride, int head_dim) {
-    constexpr int D = 128;
+template <int D, int RES>
+__device__ __forceinline__ void lpv_encode_row_bybit(const uint4* row, bc_kv_planes P, int64_t v, int seq_len,
+                                                     int64_t kv_stride, int head_dim) {
+    static_assert(D == 64 || D == 128, "one vector per lane: head_dim 64 or 128");
+    constexpr int NW = D / 32;
     float a[8];
     __half2 mx = __float2half2_rn(0.0f), mn = __float2half2_rn(INFINITY);
-    lpv_tree16_mm<0, 0>(row, a, mx, mn);
+    lpv_tree16_mm<D, 0, 0>(row, a, mx, mn);
     const float u0 = a[0] + a[4], u1 = a[1] + a[5], u2 = a[2] + a[6], u3 = a[3] + a[7];  // stride 4
     const float v0 = u0 + u2, v1 = u1 + u3;                                              // stride 2
     const float mean_abs = (v0 + v1) / (float)head_dim;                                  // stride 1
@@ -293,21 +300,24 @@ __device__ __forceinline__ void lpv_encode_row_128(const uint4* row, bc_kv_plane
         absmax = fmaxf(fmaxf(0.0f, fabsf(lo - sc)), fabsf(hi - sc));
     }
     const float inv_absmax = (absmax > 0.0f) ? (7.0f / absmax) : 0.0f;
-    // See lpv_encode_row for the rounding by adding 1.5 * 2^23.
+    // See lpv_encode_row_small for the rounding by adding 1.5 * 2^23.
     constexpr float kRound = 12582912.0f;
     const float2 nsc = make_float2(-sc, -sc), inv2 = make_float2(inv_absmax, inv_absmax),
                  rnd2 = make_float2(kRound, kRound);
     const bool live = inv_absmax > 0.0f;
-    // Four input chunks (one word of each output chunk) per step.  The loads
-    // and the stores of finished words are volatile, so the compiler keeps one
-    // step's 16 input words live, not the whole row's 64.  Finished nibble
-    // words go back into the row's first 64 bytes (input chunks 0-3, no longer
-    // read): word w of output chunk c at byte 16c + 4w.
+    // Four input chunks (sign byte j = 4w .. 4w + 3: dims 8j .. 8j + 7) per
+    // step.  Element r of input chunk j is bit r of sign byte j; its code goes
+    // to nibble r / 4 of the nibble byte of (j, t = r % 4), which this step
+    // collects in cur[t]: head_dim 128: word w of chunk t; head_dim 64: word
+    // 2 (t % 2) + w of chunk t / 2.  The loads and the stores of finished
+    // words are volatile, so the compiler keeps one step's 16 input words
+    // live, not the whole row's.  Finished words go back into the row's first
+    // D / 2 bytes (input chunks no longer read), in chunk order.
     uint8_t* rb = reinterpret_cast<uint8_t*>(const_cast<uint4*>(row));
-    uint32_t sw[4];
+    uint32_t sw[NW];
 #pragma unroll
-    for (int w = 0; w < 4; ++w) {
-        uint32_t cur[4] = {0u, 0u, 0u, 0u};  // word w of output chunks 0..3
+    for (int w = 0; w < NW; ++w) {
+        uint32_t cur[4] = {0u, 0u, 0u, 0u};
         uint32_t sword = 0u;
 #pragma unroll
         for (int jj = 0; jj < 4; ++jj) {  // input chunk j = 4w + jj: dims 8j .. 8j + 7
@@ -326,7 +336,7 @@ __device__ __forceinline__ void lpv_encode_row_128(const uint4* row, bc_kv_plane
                     p.x = __uint_as_float(__float_as_uint(p.x) ^ ((~m[i] << 16) & 0x80000000u));
                     p.y = __uint_as_float(__float_as_uint(p.y) ^ (~m[i] & 0x80000000u));
                     const float2 q = add2_ftz(p, rnd2);
-                    const int e0 = 2 * i, e1 = 2 * i + 1;  // element e: chunk e % 4, high nibble for e >= 4
+                    const int e0 = 2 * i, e1 = 2 * i + 1;  // element e: word cur[e % 4], high nibble for e >= 4
                     cur[e0 & 3] = bfi32(__float_as_uint(q.x), cur[e0 & 3], 8 * jj + 4 * (e0 >> 2), 4);
                     cur[e1 & 3] = bfi32(__float_as_uint(q.y), cur[e1 & 3], 8 * jj + 4 * (e1 >> 2), 4);
                 }
@@ -335,30 +345,33 @@ __device__ __forceinline__ void lpv_encode_row_128(const uint4* row, bc_kv_plane
         sw[w] = sword;
         if constexpr (RES != BC_RES_NONE) {
 #pragma unroll
-            for (int c = 0; c < 4; ++c)
-                sts32_volatile(rb + 16 * c + 4 * w, live ? cur[c] ^ 0x88888888u : 0x88888888u);  // code + 8
+            for (int t = 0; t < 4; ++t)  // byte offset of the word in chunk order: 16t + 4w (128), 8t + 4w (64)
+                sts32_volatile(rb + (D == 128 ? 16 : 8) * t + 4 * w, live ? cur[t] ^ 0x88888888u : 0x88888888u);
         }
     }
     const int64_t slot = v / seq_len, pos = v - slot * seq_len;
     const int64_t r = slot * kv_stride + pos;
-    *reinterpret_cast<uint4*>(reinterpret_cast<uint32_t*>(P.sign) + r * 4) = make_uint4(sw[0], sw[1], sw[2], sw[3]);
+    if constexpr (NW == 4)
+        *reinterpret_cast<uint4*>(reinterpret_cast<uint32_t*>(P.sign) + r * 4) = make_uint4(sw[0], sw[1], sw[2], sw[3]);
+    else
+        *reinterpret_cast<uint2*>(reinterpret_cast<uint32_t*>(P.sign) + r * 2) = make_uint2(sw[0], sw[1]);
     reinterpret_cast<uint16_t*>(P.bscale)[r] = sb;
     if constexpr (RES != BC_RES_NONE) {
         uint8_t* nb = reinterpret_cast<uint8_t*>(P.nib);
 #pragma unroll
-        for (int c = 0; c < 4; ++c)
+        for (int c = 0; c < NW; ++c)
             *reinterpret_cast<uint4*>(nb + nib_chunk_offset(r, c, D)) = lds128_volatile(rb + 16 * c);
         reinterpret_cast<uint16_t*>(P.rscale)[r] = f2h_bits(absmax);
     }
 }
 
 // Encode the vector in shared-memory row `row` into plane row v (lane-local),
-// head dims below 128 (reference nibble order): three passes over the row.
+// head dims 32 and 96 (reference nibble order): three passes over the row.
 template <int NW, int RES>
 __device__ __forceinline__ void lpv_encode_row_small(const uint4* row, bc_kv_planes P, int64_t v, int seq_len,
                                                      int64_t kv_stride, int head_dim) {
     constexpr int D = 32 * NW;
-    static_assert(!nib_by_bit(D), "head_dim 128 has its own row encoder");
+    static_assert(!nib_by_bit(D), "head dims 64 and 128 have their own row encoder");
     const float mean_abs = lpv_abs_sum<D>(row) / (float)head_dim;
     const uint16_t sb = f2h_bits(mean_abs);
     const float sc = (RES == BC_RES_FP16_SCALE) ? __half2float(__ushort_as_half(sb)) : mean_abs;
@@ -431,8 +444,8 @@ __device__ __forceinline__ void lpv_encode_row_small(const uint4* row, bc_kv_pla
 template <int NW, int RES>
 __device__ __forceinline__ void lpv_encode_row(const uint4* row, bc_kv_planes P, int64_t v, int seq_len,
                                                int64_t kv_stride, int head_dim) {
-    if constexpr (NW == 4)
-        lpv_encode_row_128<RES>(row, P, v, seq_len, kv_stride, head_dim);
+    if constexpr (nib_by_bit(32 * NW))
+        lpv_encode_row_bybit<32 * NW, RES>(row, P, v, seq_len, kv_stride, head_dim);
     else
         lpv_encode_row_small<NW, RES>(row, P, v, seq_len, kv_stride, head_dim);
 }
@@ -531,14 +544,15 @@ __global__ void __launch_bounds__(kEncWarps * 32) k_records_to_planes(const uint
         const uint16_t* r = reinterpret_cast<const uint16_t*>(res + v * kResRecBytes);
         uint8_t* nib = reinterpret_cast<uint8_t*>(P.nib);
         if constexpr (nib_by_bit(32 * NW)) {
-            // lane j < 16: record word j holds dims 8j .. 8j + 7 (nibble r = dim 8j + r);
-            // plane byte j of chunk c takes nibbles c (low) and c + 4 (high)
-            if (lane < 16) {
+            // lane b < head_dim / 8: record word b holds dims 8b .. 8b + 7 (nibble t = dim 8b + t);
+            // the plane byte of (b, t) takes nibbles t (low) and t + 4 (high)
+            if (lane < 4 * NW) {
                 const uint32_t W = (uint32_t)r[2 * lane] | ((uint32_t)r[2 * lane + 1] << 16);
 #pragma unroll
-                for (int c = 0; c < 4; ++c)
-                    nib[nib_chunk_offset(v, c, 32 * NW) + lane] =
-                        (uint8_t)((((W >> (4 * c)) & 0xFu) | (((W >> (4 * c + 16)) & 0xFu) << 4)) ^ 0x88u);
+                for (int t = 0; t < 4; ++t)
+                    nib[nib_chunk_offset(v, nib_byte_chunk(32 * NW, lane, t), 32 * NW) +
+                        nib_byte_index(32 * NW, lane, t)] =
+                        (uint8_t)((((W >> (4 * t)) & 0xFu) | (((W >> (4 * t + 16)) & 0xFu) << 4)) ^ 0x88u);
             }
         } else {
             for (int i = lane; i < 8 * NW; i += 32)
@@ -562,18 +576,21 @@ __global__ void __launch_bounds__(kEncWarps * 32) k_planes_to_records(bc_kv_plan
         uint16_t* r = reinterpret_cast<uint16_t*>(res + v * kResRecBytes);
         const uint8_t* nib = reinterpret_cast<const uint8_t*>(P.nib);
         if constexpr (nib_by_bit(32 * NW)) {
-            // lane j < 16 rebuilds record word j (dims 8j .. 8j + 7) from byte j of the four chunks
-            if (lane < 16) {
+            // lane b < head_dim / 8 rebuilds record word b (dims 8b .. 8b + 7) from the
+            // plane bytes of (b, t), t < 4
+            if (lane < 4 * NW) {
                 uint32_t W = 0;
 #pragma unroll
-                for (int c = 0; c < 4; ++c) {
-                    const uint32_t b = nib[nib_chunk_offset(v, c, 32 * NW) + lane] ^ 0x88u;
-                    W |= ((b & 0xFu) << (4 * c)) | ((b >> 4) << (4 * c + 16));
+                for (int t = 0; t < 4; ++t) {
+                    const uint32_t b = nib[nib_chunk_offset(v, nib_byte_chunk(32 * NW, lane, t), 32 * NW) +
+                                           nib_byte_index(32 * NW, lane, t)] ^
+                                       0x88u;
+                    W |= ((b & 0xFu) << (4 * t)) | ((b >> 4) << (4 * t + 16));
                 }
                 r[2 * lane] = (uint16_t)W;
                 r[2 * lane + 1] = (uint16_t)(W >> 16);
             }
-            r[32 + lane] = 0;  // nibbles 64..127 of the record, unused at head_dim 128
+            for (int i = 8 * NW + lane; i < 64; i += 32) r[i] = 0;  // record nibbles beyond head_dim
         } else {
             for (int i = lane; i < 64; i += 32)
                 r[i] = (i < 8 * NW) ? (uint16_t)(*reinterpret_cast<const uint16_t*>(

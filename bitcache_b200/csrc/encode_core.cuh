@@ -51,9 +51,11 @@ __device__ __forceinline__ float tree_abs_sum(const float (&x)[NW]) {
 // online_encode.cu:85-119).  Codes are two's complement.
 //  PLANE = false (reference records): lanes 4m (m < 8) hold the 16-bit pair of
 //    bytes 16k+2m, 16k+2m+1 of the reference byte order in nh[k].
-//  PLANE = true (nibble planes): at head_dim 128 (by-bit order) lanes c < 4
-//    hold word k of chunk c in nw[k]; at other head dims lanes 8m (m < 4) hold
-//    word m of chunk k in nw[k] (8 codes, element 8j low nibble first).
+//  PLANE = true (nibble planes), by-bit order (head_dim 64, 128, 256): lanes
+//    L < 4 hold in nw[k] the word nib_word(NW, L, k) of nibble_chunk(NW, L, k)
+//    (head_dim 128: word k of chunk L; 256: word k % 4 of chunk 4 (k / 4) + L;
+//    64: word 2 (L % 2) + k of chunk L / 2); at other head dims lanes 8m
+//    (m < 4) hold word m of chunk k in nw[k] (8 codes, element 8j low nibble first).
 template <int NW, bool PLANE>
 __device__ __forceinline__ float quantise_residual(const float (&x)[NW], const uint32_t (&w)[NW], float s, int lane,
                                                    uint32_t (&nw)[NW], uint32_t (&nh)[NW]) {
@@ -76,8 +78,9 @@ __device__ __forceinline__ float quantise_residual(const float (&x)[NW], const u
         q = max(-7, min(7, q));
         const uint32_t nb = (uint32_t)q & 0xFu;
         if constexpr (PLANE && nib_by_bit(32 * NW)) {
-            // lane l holds dim 32k + l = 8(4k + b) + c + 4h with l = 8b + c + 4h:
-            // byte 4k + b of chunk c is (lane 8b + c, lane 8b + c + 4)
+            // lane l = 8b + L + 4h holds dim 32k + l, i.e. bit L + 4h of sign
+            // byte 4k + b; the nibble byte of (sign byte 4k + b, bits L, L + 4)
+            // is (lane 8b + L, lane 8b + L + 4), and lane L gathers b = 0..3
             const uint32_t byte = nb | (__shfl_down_sync(0xffffffffu, nb, 4) << 4);
             const uint32_t t1 = byte | (__shfl_down_sync(0xffffffffu, byte, 8) << 8);
             nw[k] = t1 | (__shfl_down_sync(0xffffffffu, t1, 16) << 16);
@@ -108,12 +111,30 @@ __device__ __forceinline__ void store_sign_row(uint32_t* row, const uint32_t (&w
 
 // The nibble chunks of plane row `row` from quantise_residual<NW, true>'s
 // words, interleaved layout, stored offset-binary (each nibble holds code + 8).
+// By-bit order: where lane L's words go (nibble chunk, first byte of the run),
+// the words being consecutive: head_dim 128: nw[0..3] -> chunk L; 256: nw[0..3]
+// -> chunk L, nw[4..7] -> chunk 4 + L; 64: nw[0..1] -> chunk L / 2 at byte 8 (L % 2).
+template <int NW>
+__device__ __forceinline__ void nib_words_to(uint8_t* dst_chunk0, int chunk_stride, const uint32_t (&nw)[NW], int L) {
+    if constexpr (NW == 4) {
+        *reinterpret_cast<uint4*>(dst_chunk0 + L * chunk_stride) =
+            make_uint4(nw[0] ^ 0x88888888u, nw[1] ^ 0x88888888u, nw[2] ^ 0x88888888u, nw[3] ^ 0x88888888u);
+    } else if constexpr (NW == 8) {
+        *reinterpret_cast<uint4*>(dst_chunk0 + L * chunk_stride) =
+            make_uint4(nw[0] ^ 0x88888888u, nw[1] ^ 0x88888888u, nw[2] ^ 0x88888888u, nw[3] ^ 0x88888888u);
+        *reinterpret_cast<uint4*>(dst_chunk0 + (4 + L) * chunk_stride) =
+            make_uint4(nw[4] ^ 0x88888888u, nw[5] ^ 0x88888888u, nw[6] ^ 0x88888888u, nw[7] ^ 0x88888888u);
+    } else {
+        static_assert(NW == 2, "by-bit nibble order: head_dim 64, 128 or 256");
+        *reinterpret_cast<uint2*>(dst_chunk0 + (L >> 1) * chunk_stride + 8 * (L & 1)) =
+            make_uint2(nw[0] ^ 0x88888888u, nw[1] ^ 0x88888888u);
+    }
+}
+
 template <int NW>
 __device__ __forceinline__ void store_nib_row(uint8_t* plane, int64_t row, const uint32_t (&nw)[NW], int lane) {
     if constexpr (nib_by_bit(32 * NW)) {
-        if (lane < 4)  // chunk `lane`: words 0..3
-            *reinterpret_cast<uint4*>(plane + nib_chunk_offset(row, lane, 32 * NW)) =
-                make_uint4(nw[0] ^ 0x88888888u, nw[1] ^ 0x88888888u, nw[2] ^ 0x88888888u, nw[3] ^ 0x88888888u);
+        if (lane < 4) nib_words_to<NW>(plane + nib_chunk_offset(row, 0, 32 * NW), 128, nw, lane);
     } else {
 #pragma unroll
         for (int k = 0; k < NW; ++k)

@@ -13,6 +13,7 @@ copies in the decode kernel need 16-byte aligned sources and sizes).
 """
 from __future__ import annotations
 
+import functools
 from dataclasses import dataclass
 
 import torch
@@ -89,22 +90,45 @@ class Planes:
 
 
 def _by_bit(head_dim: int) -> bool:
-    """Nibble order of the planes: at head_dim 128 byte j of chunk c holds dims 8j + c
-    (low nibble) and 8j + c + 4 (high); at other head dims dims 32c + 2j and 32c + 2j + 1,
-    the reference's order."""
-    return head_dim == 128
+    """Nibble order of the planes.  At head dims 64, 128 and 256 every plane byte holds
+    bits t and t + 4 (t < 4) of one sign byte b, i.e. dims 8b + t (low nibble) and
+    8b + t + 4 (high), placed so that one 16-byte chunk lines up with one 16-byte window
+    of the sign row (`_nib_dims` gives the placement).  Other head dims keep the
+    reference's order: byte j of chunk c holds dims 32c + 2j and 32c + 2j + 1."""
+    return head_dim in (64, 128, 256)
+
+
+@functools.lru_cache(maxsize=None)
+def _nib_dims(head_dim: int) -> tuple[torch.Tensor, torch.Tensor]:
+    """(low, high): the dim held by each nibble of a plane row in chunk order, byte
+    p = 16c + j (the same rule as the kernels' nib_dim)."""
+    c = torch.arange(head_dim // 2) // 16
+    j = torch.arange(head_dim // 2) % 16
+    if head_dim == 128:
+        lo = 8 * j + c
+    elif head_dim == 256:
+        lo = 128 * (c // 4) + 8 * j + c % 4
+    elif head_dim == 64:
+        lo = 8 * (j % 8) + 2 * c + j // 8
+    else:
+        return 32 * c + 2 * j, 32 * c + 2 * j + 1
+    return lo, lo + 4
+
+
+def _chunk_rows(nib: torch.Tensor, head_dim: int) -> torch.Tensor:
+    slots, stride = nib.shape[0], nib.shape[1]
+    return (nib.reshape(slots, stride // 8, head_dim // 32, 8, 16).permute(0, 1, 3, 2, 4)
+            .reshape(slots, stride, head_dim // 2))
 
 
 def nib_rows(nib: torch.Tensor, head_dim: int) -> torch.Tensor:
     """De-interleave a nibble plane [slots, kv_stride, head_dim/2] into per-position rows of
     the reference's byte format (two's-complement codes, element 2i in the low nibble)."""
-    slots, stride = nib.shape[0], nib.shape[1]
-    rows = (nib.reshape(slots, stride // 8, head_dim // 32, 8, 16).permute(0, 1, 3, 2, 4)
-            .reshape(slots, stride, head_dim // 2))
-    rows = torch.bitwise_xor(rows, 0x88)
-    if _by_bit(head_dim):  # [c][j] chunk bytes -> codes in dim order (8j + 4e + c) -> reference bytes
-        p = rows.reshape(slots, stride, 4, 16)
-        codes = torch.stack([p & 0xF, p >> 4], -1).permute(0, 1, 3, 4, 2).reshape(slots, stride, head_dim)
+    rows = torch.bitwise_xor(_chunk_rows(nib, head_dim), 0x88)
+    if _by_bit(head_dim):  # chunk-order bytes -> codes in dim order -> reference bytes
+        lo, hi = _nib_dims(head_dim)
+        order = torch.argsort(torch.cat([lo, hi])).to(rows.device)
+        codes = torch.cat([rows & 0xF, rows >> 4], -1).index_select(-1, order)
         rows = codes[..., 0::2] | (codes[..., 1::2] << 4)
     return rows.contiguous()
 
@@ -113,10 +137,10 @@ def nib_interleave(rows: torch.Tensor, head_dim: int) -> torch.Tensor:
     """Inverse of nib_rows: reference-format rows [slots, kv_stride, head_dim/2] -> plane bytes."""
     slots, stride = rows.shape[0], rows.shape[1]
     x = rows
-    if _by_bit(head_dim):  # reference bytes -> codes in dim order -> [c][j] chunk bytes
-        codes = torch.stack([x & 0xF, x >> 4], -1).reshape(slots, stride, 16, 2, 4)
-        p = codes.permute(0, 1, 4, 2, 3)  # [c][j][e]
-        x = (p[..., 0] | (p[..., 1] << 4)).reshape(slots, stride, head_dim // 2)
+    if _by_bit(head_dim):  # reference bytes -> codes in dim order -> chunk-order bytes
+        lo, hi = _nib_dims(head_dim)
+        codes = torch.stack([x & 0xF, x >> 4], -1).reshape(slots, stride, head_dim)
+        x = codes.index_select(-1, lo.to(x.device)) | (codes.index_select(-1, hi.to(x.device)) << 4)
     x = torch.bitwise_xor(x, 0x88)
     return (x.reshape(slots, stride // 8, 8, head_dim // 32, 16).permute(0, 1, 3, 2, 4)
             .reshape(slots, stride, head_dim // 2).contiguous())

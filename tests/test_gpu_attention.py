@@ -89,8 +89,9 @@ def test_c1_golden_vs_kernels(cuda):
 @pytest.mark.parametrize("d", [32, 64, 128, 256])
 @pytest.mark.parametrize("comp", [True, False])
 def test_gqa_vs_oracle(cuda, group, d, comp):
-    """Grouped-query heads, two per CTA: the tensor-core value phase at d = 128
-    (heads as MMA columns), 16-dim f32x2 value lanes at the other head dims."""
+    """Grouped-query heads, several per CTA: the tensor-core value phase (heads as
+    MMA columns) for compensated caches at d = 64, 128, 256 and binary ones at
+    d = 128; 16-dim f32x2 value lanes elsewhere."""
     slots, S = 3, 700
     g = torch.Generator().manual_seed(group * 10 + d)
     q = (torch.randn(slots * group, d, generator=g) * 0.5).half()
@@ -114,14 +115,15 @@ def test_gqa_vs_oracle(cuda, group, d, comp):
 
 @pytest.mark.parametrize("pattern", ["score_ramp", "value_jump"])
 @pytest.mark.parametrize("group", [1, 2])
-def test_growing_coefficients_vs_oracle(cuda, pattern, group):
+@pytest.mark.parametrize("d", [64, 128, 256])
+def test_growing_coefficients_vs_oracle(cuda, pattern, group, d):
     """Key coefficients that grow within a split: the tensor-core value phase
     must move its fixed-point unit and shift the accumulators down exactly.
     score_ramp: scores rise by ~30 log2 units over every 256 positions (a
     sawtooth, so every period's top keys carry equal weight); value_jump: the
     first half of every period holds values 2^12 times smaller."""
-    slots, S, d = 32, 8192, 128
-    g = torch.Generator().manual_seed(5 + group)
+    slots, S = 32, 8192
+    g = torch.Generator().manual_seed(5 + group + d)
     q = (torch.randn(slots * group, d, generator=g) * 0.5).half()
     pos = torch.arange(S, dtype=torch.float32)
     phase = (pos % 256) / 256.0
@@ -143,7 +145,7 @@ def test_growing_coefficients_vs_oracle(cuda, pattern, group):
                 "nib": X.nib_rows().cpu().numpy(), "rscale": X.rscale.cpu().numpy().view(np.uint16)}
 
     want = O.attention(q.numpy(), host(K), host(V), group, S, S, True).view(np.float16).astype(np.float32)
-    close(mine, want, f"{pattern} group={group}")
+    close(mine, want, f"{pattern} group={group} d={d}")
 
 
 @pytest.mark.parametrize("S", [0, 1, 7, 8, 9, 129, 1000])
