@@ -1523,7 +1523,8 @@ __device__ __forceinline__ void patch_stage_row(uint8_t* sb, int kk, const uint8
 
 // Stage layout of the adaptive kernel's binary-only segment on the tensor-core
 // path: four 128-key tiles per ring stage (sign words and scales only, 18 KB
-// at head_dim 128), so a binary CTA keeps four times the bytes in flight.
+// at head_dim 128, 10 KB at 64, 34 KB at 256), so a binary CTA keeps four
+// times the bytes in flight.
 template <int D>
 struct BinStageCfg {
     static constexpr int NWD = D / 32;
@@ -1583,7 +1584,7 @@ __global__ void __launch_bounds__(kDecThreads, DecCfg<D, GC, COMP>::MIN_CTAS)
     const int n_keys = max(0, s_end - s_begin);
     // keys per ring stage: one tile, or four in the binary segment of the
     // adaptive kernel's tensor-core path
-    constexpr bool BIN4 = ADA && Cfg::MMA && D == 128;
+    constexpr bool BIN4 = ADA && Cfg::MMA;
     if constexpr (BIN4) static_assert(BinStageCfg<D>::BYTES <= Cfg::STAGE_B, "binary stage exceeds the ring stage");
     const bool wide = BIN4 && seg_bin;
     const int TS = wide ? BinStageCfg<D>::KEYS : ((VAR == 0 || VAR == 2) ? Cfg::KEYS : T);

@@ -26,11 +26,15 @@
  *        nib    uint8  [slots][kv_stride][head_dim/2]    INT4 residual codes stored offset-binary
  *               (each nibble holds code + 8), interleaved in blocks of 8 positions: the
  *               16-byte chunk c of plane row r = slot*kv_stride + pos starts at byte
- *               (r/8)*(4*head_dim) + c*128 + (r%8)*16.  Byte j of chunk c holds
- *                 head_dim 128:   dims 8j + c (low nibble) and 8j + c + 4 (high nibble),
- *                                 the dims of bits c and c+4 of sign byte j;
- *                 other head_dim: dims 32c + 2j (low) and 32c + 2j + 1 (high), the
- *                                 reference's element order (its byte XOR 0x88).
+ *               (r/8)*(4*head_dim) + c*128 + (r%8)*16.  At head dims 64, 128 and 256
+ *               every byte holds the dims of bits t and t+4 (t < 4) of one sign byte b,
+ *               8b + t (low nibble) and 8b + t + 4 (high nibble); byte j of chunk c is
+ *                 head_dim 128:   b = j,               t = c
+ *                 head_dim 256:   b = 16*(c/4) + j,    t = c % 4
+ *                 head_dim 64:    b = j % 8,           t = 2c + j/8
+ *               (one chunk lines up with one 16-byte window of the sign row).  Other
+ *               head dims keep the reference's element order: byte j of chunk c holds
+ *               dims 32c + 2j (low) and 32c + 2j + 1 (high) (the reference's byte XOR 0x88).
  *        bscale fp16   [slots][kv_stride]                mean |x| (binary scale)
  *        rscale fp16   [slots][kv_stride]                residual absmax
  *    5*head_dim/8 + 4 bytes per vector (84 B at head_dim 128).  The field
