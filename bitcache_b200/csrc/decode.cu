@@ -181,8 +181,12 @@ struct DecCfg {
     static_assert(!MMA || DUMP_OFF + DUMP_B <= BODY_B, "accumulator dump exceeds the ring");
     // Resident CTAs per SM that shared memory allows at head_dim <= 128 with one
     // head per CTA; the register budget is held to it (0: no bound).
+    // (head_dim 64, one head: five, whose registers then match the five
+    // CTAs that shared memory allows)
     static constexpr int MIN_CTAS =
-        (D > 128) ? 0 : ((GC == 1 && !COMP) ? BC_DEC_MIN_CTAS_B1 : (GC == 1 ? BC_DEC_MIN_CTAS_C1 : 4)) * 128 / kDecThreads;
+        (D > 128) ? 0
+                  : ((GC == 1 && !COMP) ? BC_DEC_MIN_CTAS_B1
+                                        : (GC == 1 ? (D == 64 ? 5 : BC_DEC_MIN_CTAS_C1) : 4)) * 128 / kDecThreads;
 };
 
 struct DecodeArgs {
@@ -432,12 +436,14 @@ __device__ __forceinline__ void init_soft(SoftState<GC, NP>& st) {
 // accumulators: acc[n][t] is the m16n8 tile t (rows = dims, see
 // consume_warp_tile_mma) of column tile n (columns = head 2n + col / 4, byte
 // col % 4 of the key coefficient).  The sign bits and the INT4 codes of a dim
-// share its accumulator row: the sign bit enters with the coefficient 2 w
-// bscale, the code with w rscale / 7 (w = 2^(s - m)), both as 32-bit
-// fixed-point numbers in units of 2^U[g] (absolute, log2) split into four byte
-// columns, so the softmax's lazy max m never touches the accumulators; U
-// moves only when a coefficient would reach 2^31 units, and the accumulators
-// are then shifted down exactly.
+// share its accumulator row: the sign bit enters with the coefficient 2 e
+// bscale, the code with e rscale / 7, both as 32-bit fixed-point numbers split
+// into four byte columns, where e = 2^(s - U[g]) is the key's softmax weight
+// in units of 2^U[g] (absolute, log2).  U is the softmax's running reference
+// point as well: the weight sum l and the constant term t are kept in the
+// same units, so there is no separate running max.  U moves only when a
+// coefficient would reach 2^31 units; the accumulators are then shifted down
+// exactly and l, t scaled by the same power of two.
 constexpr int kUUnset = -0x40000000;
 
 // BITMAP: a binary-only cache, whose rows need not line up with the codes'
@@ -447,7 +453,7 @@ constexpr int kUUnset = -0x40000000;
 template <int GC, bool BITMAP = false, int NRT = 8>
 struct MmaState {
     static constexpr int NT = (GC + 1) / 2;
-    float m[GC];
+    float Uf[GC];  // U as a float, -inf while unset
     float l[GC], t[GC];
     int acc[NT][NRT][4];
     int U[GC];
@@ -458,7 +464,7 @@ template <int GC, bool BM, int NRT>
 __device__ __forceinline__ void init_soft(MmaState<GC, BM, NRT>& st) {
 #pragma unroll
     for (int g = 0; g < GC; ++g) {
-        st.m[g] = -INFINITY;
+        st.Uf[g] = -INFINITY;
         st.l[g] = 0.0f;
         st.t[g] = 0.0f;
         st.U[g] = kUUnset;
@@ -922,41 +928,43 @@ __device__ __forceinline__ void consume_warp_tile_mma(const QSmem& qs, MmaState<
     }
     const float vbs = valid ? __half2float(reinterpret_cast<const __half*>(sb + Cfg::OFF_VBS)[kk]) : 0.0f;
     const float vrs = (RES && valid) ? __half2float(reinterpret_cast<const __half*>(sb + Cfg::OFF_VRS)[kk]) : 0.0f;
+    // per-key weight multipliers: sign coefficient 2 bscale, code coefficient
+    // rscale / 7, constant term bscale + 8 rscale / 7 (bits {0,1} and codes + 8)
+    const float cs = 2.0f * vbs, cc = vrs * (1.0f / 7.0f), ct = vbs + 8.0f * cc;
 #pragma unroll
     for (int g = 0; g < GC; ++g) {
-        if (__any_sync(0xffffffffu, s2[g] > st.m[g] + kLazy)) {  // warp-uniform, rare after the first tile
-            float M = s2[g];
-#pragma unroll
-            for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
-            const float alpha = fast_exp2(st.m[g] - M);
-            st.m[g] = M;
-            st.l[g] *= alpha;
-            st.t[g] *= alpha;
-        }
-        const float wt = valid ? fast_exp2(s2[g] - st.m[g]) : 0.0f;
-        st.l[g] += wt;
-        const float ca = 2.0f * wt * vbs;            // sign bit coefficient
-        const float cr = wt * vrs * (1.0f / 7.0f);   // code coefficient
-        st.t[g] += wt * vbs + 8.0f * cr;
-        float f = fast_exp2(st.m[g] - (float)st.U[g]);
-        float xa = ca * f, xr = cr * f;
-        const float cmax = fmaxf(ca, cr);
-        if (__any_sync(0xffffffffu, st.U[g] == kUUnset || fmaxf(xa, xr) >= 2147483648.0f)) {
-            // new unit: the warp's largest coefficient lands in (2^21, 2^22]
-            float lg = cmax > 0.0f ? log2f(cmax) + st.m[g] : -INFINITY;
+        // e = 2^(s - U): the key's softmax weight in units of 2^U (while U is
+        // unset, Uf = -inf makes every valid e infinite and forces the choice)
+        float e = valid ? fast_exp2(s2[g] - st.Uf[g]) : 0.0f;
+        float xa = e * cs, xr = e * cc;
+        if (__any_sync(0xffffffffu, fmaxf(fmaxf(xa, xr), e * 0x1p-33f) >= 2147483648.0f)) {
+            // New unit (warp-uniform, rare after the first tile): the warp's
+            // largest coefficient lands in (2^21, 2^22] and every e below 2^62.
+            // A raise by delta divides the accumulators and l, t by 2^delta.
+            // (the floor 2^-40: keys whose coefficients are ~0 still bound e)
+            float lg = valid ? s2[g] + log2f(fmaxf(fmaxf(cs, cc), 0x1p-40f)) : -INFINITY;
 #pragma unroll
             for (int off = 16; off > 0; off >>= 1) lg = fmaxf(lg, __shfl_xor_sync(0xffffffffu, lg, off));
             if (lg > -INFINITY) {
-                const int Un = (int)ceilf(lg) - 22;
-                if (st.U[g] != kUUnset && Un > st.U[g]) mma_shift_down(st, g, Un - st.U[g]);
-                if (st.U[g] == kUUnset || Un > st.U[g]) st.U[g] = Un;
-                f = fast_exp2(st.m[g] - (float)st.U[g]);
-                xa = ca * f;
-                xr = cr * f;
+                int Un = (int)ceilf(lg) - 22;
+                if (st.U[g] != kUUnset) {
+                    Un = max(Un, st.U[g] + 1);
+                    const int delta = Un - st.U[g];
+                    mma_shift_down(st, g, delta);
+                    const float down = delta > 126 ? 0.0f : exp2i(-delta);
+                    st.l[g] *= down;
+                    st.t[g] *= down;
+                }
+                st.U[g] = Un;
+                st.Uf[g] = (float)Un;
+                e = valid ? fast_exp2(s2[g] - st.Uf[g]) : 0.0f;
+                xa = e * cs;
+                xr = e * cc;
             }
         }
-        const bool have = st.U[g] != kUUnset;
-        const uint32_t A = have ? __float2uint_rn(xa) : 0u, R = have ? __float2uint_rn(xr) : 0u;
+        st.l[g] += e;
+        st.t[g] = fmaf(e, ct, st.t[g]);
+        const uint32_t A = __float2uint_rn(xa), R = __float2uint_rn(xr);
         // head_dim 64: the sign fragments' k index of key `lane` (see above)
         const int sign_k = (D == 64) ? ((lane & 1) ? 16 : 0) + 4 * (lane >> 3) + ((lane & 7) >> 1) : lane;
 #pragma unroll
@@ -1233,12 +1241,12 @@ __device__ __forceinline__ void warp_records(float* mg, MmaState<GC, BM, NRT>& s
             t += __shfl_xor_sync(0xffffffffu, t, off);
         }
         float* rec = mg + ((size_t)warp * GC + g) * (D + 2);
+        // l, t and the accumulators are all in units of 2^U: U is the record's
+        // reference point (log2), -inf when the warp saw no key
         if (lane == 0) {
-            rec[0] = st.m[g];
+            rec[0] = st.Uf[g];
             rec[1] = l;
         }
-        // accumulator unit relative to the warp's max: 2^(U - m)
-        const float sc = (st.U[g] != kUUnset && st.m[g] > -INFINITY) ? exp2f((float)st.U[g] - st.m[g]) : 0.0f;
 #pragma unroll
         for (int e = 0; e < D / 32; ++e) {
             const int dim = (D / 32) * lane + e;
@@ -1252,7 +1260,7 @@ __device__ __forceinline__ void warp_records(float* mg, MmaState<GC, BM, NRT>& s
             const uint64_t v1 = (uint64_t)(uint32_t)lb[0] + ((uint64_t)(uint32_t)lb[1] << 8);
             const float unit = BM ? exp2i(-(dim & 7)) : (hi ? (1.0f / 16.0f) : 1.0f);
             const float v = ((float)v0 + 65536.0f * (float)v1) * unit;
-            rec[2 + dim] = v * sc - t;
+            rec[2 + dim] = v - t;
         }
     }
 }
