@@ -1124,12 +1124,12 @@ __device__ __forceinline__ void xchg_finish(const DecodeArgs& a, int slot, int h
     if (tid == 0) s_timeout = 0;
     __syncthreads();
     volatile int* gave_up = &s_timeout;
-    // One word, polled at most a.xspin times (after 4096 fast polls with
-    // 256 ns sleeps).  Once any thread of the CTA has given up, every other
-    // poll returns at once, so a missing rank costs one spin limit per CTA,
-    // not one per word.
-    auto wait_word = [&](const unsigned long long* p) -> float {
-        unsigned long long v = ld_relaxed_sys_u64(p);
+    // A word already loaded once (v), polled again at most a.xspin times
+    // (after 4096 fast polls with 256 ns sleeps) while it carries an older
+    // epoch.  Once any thread of the CTA has given up, every other poll
+    // returns at once, so a missing rank costs one spin limit per CTA, not
+    // one per word.
+    auto settle = [&](unsigned long long v, const unsigned long long* p) -> float {
         for (uint32_t it = 0; (int)((unsigned)(v >> 32) - a.xepoch) < 0; ++it) {
             if (it >= a.xspin || *gave_up) {
                 *gave_up = 1;
@@ -1143,15 +1143,27 @@ __device__ __forceinline__ void xchg_finish(const DecodeArgs& a, int slot, int h
     for (int idx = tid; idx < GC * D; idx += kDecThreads) {
         const int g = idx / D, i = idx % D;
         const int64_t h = head0 + g;
+        // all 3 xw words first, so that their loads are in flight together
+        // (one round trip, not 3 xw); then only the words that do not yet
+        // carry this call's epoch are polled again
+        unsigned long long w[8][3];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            if (j >= a.xw) break;
+            const unsigned long long* r = base + ((int64_t)j * n_heads + h) * (D + 2);
+            w[j][0] = ld_relaxed_sys_u64(r);
+            w[j][1] = ld_relaxed_sys_u64(r + 1);
+            w[j][2] = ld_relaxed_sys_u64(r + 2 + i);
+        }
         float mj[8], lj[8], oj[8];
         float M = -INFINITY;
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
             if (j >= a.xw) break;
             const unsigned long long* r = base + ((int64_t)j * n_heads + h) * (D + 2);
-            mj[j] = wait_word(r);
-            lj[j] = wait_word(r + 1);
-            oj[j] = wait_word(r + 2 + i);
+            mj[j] = settle(w[j][0], r);
+            lj[j] = settle(w[j][1], r + 1);
+            oj[j] = settle(w[j][2], r + 2 + i);
             if (lj[j] > 0.0f) M = fmaxf(M, mj[j]);
         }
         float L = 0.0f, O = 0.0f;
