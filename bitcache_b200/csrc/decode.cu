@@ -70,7 +70,7 @@ __device__ unsigned int g_bc_device_error = 0;
 #define BC_DEC_BIN_GC 4        // most query heads per CTA in binary grouped-query caches (binary C4: 4 heads 91 us, 2 heads 106 us)
 #endif
 #ifndef BC_DEC_GQA_GC
-#define BC_DEC_GQA_GC 4        // most query heads per CTA in compensated grouped-query caches at head_dim 128
+#define BC_DEC_GQA_GC 4        // most query heads per CTA in compensated grouped-query caches at head dims 64 and 128
 #endif
 #ifndef BC_DEC_KCOMB
 #define BC_DEC_KCOMB 8         // split partials each combining thread loads per L2 round trip

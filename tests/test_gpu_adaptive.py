@@ -100,6 +100,7 @@ def host_rows(P, rows_stride=None):
     (4, 1, 777, 128, 0.25),
     (3, 2, 1000, 64, 0.25),
     (2, 4, 513, 256, 0.5),
+    (2, 4, 900, 64, 0.25),
     (5, 1, 300, 128, 0.0),
     (2, 1, 129, 128, 1.0),
     (3, 8, 2048, 128, 0.25),

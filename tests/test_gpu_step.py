@@ -59,6 +59,8 @@ CASES = [
     (3, 4, 128, True, 777, 1024),     # grouped-query: head groups 1.. patch without storing
     (2, 8, 128, False, 2047, 4096),   # binary, four heads per CTA
     (2, 2, 256, True, 300, 512),
+    (3, 4, 64, True, 500, 1024),      # four heads per CTA at head_dim 64 (by-bit planes)
+    (2, 4, 256, True, 200, 512),      # two head groups of two at head_dim 256
     (5, 1, 32, True, 4095, 8192),
     (1, 1, 128, False, 65, 128),
 ]
