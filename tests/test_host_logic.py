@@ -205,3 +205,27 @@ def test_bench_job_partition_and_shared_config():
     assert [j.my_slots for j in jobs] == [16] * 8 and all(j.my_S == 32768 for j in jobs)
     c5 = bench.Job(SimpleNamespace(config="C5", head_dim=256, split="auto", binary=False), 1, 0)
     assert c5.d == 256 and c5.adaptive and "d=256" in c5.config()["workload"]
+
+
+@pytest.mark.parametrize("d", [32, 64, 96, 128, 160, 256])
+def test_nibble_plane_layout(d):
+    """The plane's nibble order (include/bitcache_b200.h): every dim once; at the
+    by-bit head dims each byte holds bits t and t + 4 (t < 4) of one sign byte b,
+    placed by the header's table, so that a 16-byte chunk lines up with one
+    16-byte window of the sign row; nib_rows inverts nib_interleave."""
+    from bitcache_b200 import planes
+    lo, hi = planes._nib_dims(d)
+    assert torch.equal(torch.cat([lo, hi]).sort().values, torch.arange(d))
+    for p in range(d // 2):
+        c, j = p // 16, p % 16
+        if planes._by_bit(d):
+            b, t = int(lo[p]) // 8, int(lo[p]) % 8
+            assert t < 4 and int(hi[p]) == int(lo[p]) + 4
+            want = {128: (j, c), 256: (16 * (c // 4) + j, c % 4), 64: (j % 8, 2 * c + j // 8)}[d]
+            assert (b, t) == want
+            assert b // 16 == (c // 4 if d == 256 else 0)  # the chunk's sign window
+        else:
+            assert (int(lo[p]), int(hi[p])) == (32 * c + 2 * j, 32 * c + 2 * j + 1)
+    g = torch.Generator().manual_seed(d)
+    rows = torch.randint(0, 256, (3, 16, d // 2), generator=g, dtype=torch.int64).to(torch.uint8)
+    assert torch.equal(planes.nib_rows(planes.nib_interleave(rows, d), d), rows)
