@@ -596,18 +596,25 @@ def main():
         # pinned host Q in, merged output out, the decode on the device
         qh = q_all.cpu().pin_memory()
         oh = torch.empty(q_all.shape, dtype=torch.float16).pin_memory()
-        qd = torch.empty_like(q_all)
-        od = torch.empty_like(out)
+        if seq_split:
+            qd = torch.empty_like(q_all)
+            od = torch.empty_like(out)
 
-        def e2e_step(j):
-            qd.copy_(qh, non_blocking=True)
-            full_step(j, qd, od)
-            oh.copy_(od, non_blocking=True)
+            def e2e_step(j):
+                qd.copy_(qh, non_blocking=True)
+                full_step(j, qd, od)
+                oh.copy_(od, non_blocking=True)
 
-        path = ("planes.decode_attention_adaptive on the compact cache" if adaptive
-                else "dist.PeerExchange.decode (one launch per rank)" if xchg is not None
-                else "planes.decode_attention + NCCL all-gather + planes.lse_merge")
-        path += ", pinned host Q copied in and the output copied out every step"
+            path = ("planes.decode_attention + NCCL all-gather + planes.lse_merge, pinned host Q copied in and "
+                    "the output copied out every step")
+        else:
+            def e2e_step(j):
+                full_step(j, qh, oh)  # Q staged by one bc_stage_rows launch; the kernel writes oh over the host link
+
+            path = ("planes.decode_attention_adaptive on the compact cache" if adaptive
+                    else "dist.PeerExchange.decode (one decode launch per rank)")
+            path += (" on pinned host Q and output: one staging launch copies Q to the device (bc_stage_rows), "
+                     "the decode writes the output over the host link")
         h2d, d2h = qh.numel() * 2 * world, oh.numel() * 2 * world
     else:
         cache = BitCache(1 if world > 1 else job.batch, my_slots * G if world > 1 else job.n_heads, d,
@@ -650,7 +657,7 @@ def main():
     assert _lib.device_error() == 0, "device-side timeout during the end-to-end leg"
     e2e = {"value": job.bytes_total / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s", "ms_per_step": e2e_ms,
            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "path": path,
-           "gpu_launches_per_step": 2 if (seq_split or not (adaptive or job.split in ("seq", "seqx"))) else 1}
+           "gpu_launches_per_step": 2}
 
     # ---- prefill encode throughput (fused binary + INT4 residual into planes) ----
     prefill = None

@@ -148,7 +148,10 @@ class PeerExchange:
 
     def decode(self, q: torch.Tensor, K, V, seq_len: int, mode: int, out: torch.Tensor | None = None) -> torch.Tensor:
         """One sequence-split decode step: this rank's slice [K, V] of every slot,
-        the merged output of all heads on every rank."""
+        the merged output of all heads on every rank.  q and out may be pinned
+        host tensors: q is staged to the device first (planes.device_query), and
+        the kernel writes out over the host link itself."""
+        from . import planes
         lib = self._lib.load()
         d = q.shape[-1]
         n_heads = q.numel() // d
@@ -162,6 +165,11 @@ class PeerExchange:
                                f"called with {n_heads} heads of dim {d}")
         if group * n_slots != n_heads:
             raise RuntimeError("number of query heads must be a multiple of the number of KV slots")
+        if out is not None:
+            planes._check_half_dev_or_pinned(out, "out")
+            if out.numel() < n_heads * d:
+                raise RuntimeError(f"out holds {out.numel()} elements, the call writes {n_heads * d}")
+        q = planes.device_query(q, K.sign.device)
         if out is None:
             out = torch.empty((n_heads, d), dtype=torch.float16, device=q.device)
         st = self._lib.stream_of(q.device)

@@ -170,6 +170,30 @@ def _check_half_dev_or_pinned(x: torch.Tensor, name: str) -> None:
         raise RuntimeError(f"{name} must be float16")
 
 
+# Device buffers that pinned host queries are staged into, per (device, stream, elements).
+_qstage: dict[tuple, torch.Tensor] = {}
+
+
+def device_query(q: torch.Tensor, device: torch.device) -> torch.Tensor:
+    """q itself when it is on the GPU; a pinned host q is copied to a device buffer
+    (one per device, stream and size, reused by later calls) by one bc_stage_rows launch on
+    the current stream.  That kernel reads the host before it waits for the previous
+    kernel in the stream, so the host must not rewrite q while earlier steps that
+    read it are still queued."""
+    if q.is_cuda:
+        _check_half(q, "Q")
+        return q
+    _check_half_dev_or_pinned(q, "Q")
+    if q.data_ptr() % 16 or (2 * q.numel()) % 16:
+        raise RuntimeError("a pinned host Q must be 16-byte aligned and a multiple of 16 bytes")
+    key = (device, _lib.stream_of(device), q.numel())  # per stream: calls on one stream are ordered
+    buf = _qstage.get(key)
+    if buf is None:
+        buf = _qstage[key] = torch.empty(q.numel(), dtype=torch.float16, device=device)
+    stage_rows([(q.reshape(-1), buf)])
+    return buf.view(q.shape)
+
+
 def encode_planes(src: torch.Tensor, out: Planes, residual_mode: int = RES_FP16_SCALE) -> None:
     """Prefill: encode src fp16 [n_slots, seq_len, head_dim] into rows [slot, 0:seq_len] of out."""
     _check_half(src, "src")
@@ -407,8 +431,12 @@ def compact_adaptive(K: Planes, V: Planes, keep: torch.Tensor, seq_len: int, n_k
 
 def decode_attention_adaptive(q: torch.Tensor, Kc: Planes, Vc: Planes, seq_len: int, n_keep: int,
                               out: torch.Tensor | None = None) -> torch.Tensor:
-    """Decode attention over a compact adaptive cache (bc_decode_attention_adaptive)."""
-    _check_half(q, "Q")
+    """Decode attention over a compact adaptive cache (bc_decode_attention_adaptive).
+    q and out may be pinned host tensors: q is staged to the device first
+    (device_query), and the kernel writes out over the host link itself."""
+    if out is not None:
+        _check_half_dev_or_pinned(out, "out")
+    q = device_query(q, Kc.sign.device)
     d = q.shape[-1]
     n_heads = q.numel() // d
     n_slots = Kc.n_slots
@@ -417,6 +445,8 @@ def decode_attention_adaptive(q: torch.Tensor, Kc: Planes, Vc: Planes, seq_len: 
         raise RuntimeError("number of query heads must be a multiple of the number of KV slots")
     if out is None:
         out = torch.empty((n_heads, d), dtype=torch.float16, device=q.device)
+    elif out.numel() < n_heads * d:
+        raise RuntimeError(f"out holds {out.numel()} elements, the call writes {n_heads * d}")
     lib = _lib.load()
     st = _stream(q)
     wsb = lib.bc_decode_adaptive_workspace_bytes(n_slots, group, seq_len, n_keep, d)

@@ -158,3 +158,30 @@ def test_compact_adaptive_c5_shape_bytes(cuda):
     out = planes.decode_attention_adaptive(q, Kc, Vc, S, n_keep)
     torch.cuda.synchronize()
     assert torch.isfinite(out.float()).all()
+
+
+@pytest.mark.parametrize("slots,S", [(3, 1000), (64, 512)])
+def test_adaptive_with_pinned_host_query_and_output(cuda, slots, S):
+    """Pinned host Q and output (the end-to-end form of the call): Q is staged to
+    the device by one launch and the kernel writes the output over the host link;
+    the result is bit-identical to the all-device call, twice in a row."""
+    d, group = 128, 2
+    K, _ = build(cuda, slots, S, S, d, seed=11)
+    V, _ = build(cuda, slots, S, S, d, seed=12)
+    n_keep = planes.keep_count(S, 0.25)
+    keep = planes.select_positions_topk(K, V, S, n_keep)
+    Kc, Vc = planes.compact_adaptive(K, V, keep, S, n_keep)
+    g = torch.Generator().manual_seed(slots)
+    q = (torch.randn(slots * group, d, generator=g) / d ** 0.5).half()
+    want = planes.decode_attention_adaptive(q.to(cuda), Kc, Vc, S, n_keep).cpu()
+    qh = q.pin_memory()
+    oh = torch.zeros(slots * group, d, dtype=torch.float16).pin_memory()
+    for _ in range(2):
+        oh.zero_()
+        planes.decode_attention_adaptive(qh, Kc, Vc, S, n_keep, out=oh)
+        torch.cuda.synchronize()
+        assert torch.equal(oh, want)
+    with pytest.raises(RuntimeError):
+        planes.decode_attention_adaptive(qh, Kc, Vc, S, n_keep, out=torch.empty(4, d, dtype=torch.float16).pin_memory())
+    with pytest.raises(RuntimeError):
+        planes.decode_attention_adaptive(q, Kc, Vc, S, n_keep)  # pageable host Q

@@ -102,3 +102,26 @@ def test_exchange_refuses_calls_larger_than_its_buffers(cuda):
         assert _lib.device_error() == 0
     finally:
         x.close()
+
+
+def test_exchange_one_rank_with_pinned_host_query_and_output(cuda):
+    """PeerExchange with one rank on pinned host Q and output (the end-to-end form
+    of the sequence split): bit-identical to the same exchange on device tensors
+    and to the plain decode, on consecutive epochs."""
+    slots, S, d = 8, 2048, 128
+    q, K, V = _cache(cuda, slots, S, d, seed=7)
+    want = planes.decode_attention(q, K, V, S).cpu()
+    x = bdist.PeerExchange(slots, d)
+    try:
+        dev_out = x.decode(q, K, V, S, planes.MODE_COMPENSATED).cpu()
+        assert torch.equal(dev_out, want)
+        qh = q.cpu().pin_memory()
+        oh = torch.zeros(slots, d, dtype=torch.float16).pin_memory()
+        for _ in range(2):
+            oh.zero_()
+            x.decode(qh, K, V, S, planes.MODE_COMPENSATED, out=oh)
+            torch.cuda.synchronize()
+            assert torch.equal(oh, want)
+        assert _lib.device_error() == 0
+    finally:
+        x.close()
