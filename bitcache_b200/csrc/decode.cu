@@ -703,7 +703,7 @@ __device__ __forceinline__ void consume_warp_tile(const QState<D, GC>& qs, SoftS
 //
 // Score: the XNOR popcount stays on SIMT, one lane per key.  The INT4
 // residual dot sum_d u_d Q16_d of the warp's 32 keys and all GC heads is one
-// set of sixteen mma.sync m16n8k32 s8 x u8 -> s32 (residual_dots_mma): A = the
+// set of d / 8 mma.sync m16n8k32 s8 x u8 -> s32 (residual_dots_mma): A = the
 // query's balanced hi/lo digits (rows), B = the offset-binary codes (keys).
 //
 // Values: per warp and tile, D[dims x (head, byte)] += A[dims x 32 keys] .
@@ -717,8 +717,9 @@ __device__ __forceinline__ void consume_warp_tile(const QState<D, GC>& qs, SoftS
 // shifted down by c and masked with 0x01 (0x10) per byte; and the low (high)
 // nibble of byte g8 + 8h of nibble chunk c, which in the by-bit nibble order
 // holds exactly those two dims.  So the sign bits and the codes of a dim
-// accumulate in the same row, with the sign coefficient 2 w bscale and the
-// code coefficient w rscale / 7 as their B operands.  Each lane writes its
+// accumulate in the same row, with the sign coefficient 2 e bscale and the
+// code coefficient e rscale / 7 as their B operands (e = 2^(s - U), the key's
+// weight in the fixed-point unit: see MmaState).  Each lane writes its
 // key's fixed-point coefficient bytes to the warp's scratch
 // ([part][head * 4 + byte][key]) and reads its B fragments (column g8 of
 // column tile n: head 2n + g8 / 4, byte g8 % 4; keys 4q.., 4q + 16..) as two
