@@ -446,11 +446,8 @@ __device__ __forceinline__ void init_soft(SoftState<GC, NP>& st) {
 // exactly and l, t scaled by the same power of two.
 constexpr int kUUnset = -0x40000000;
 
-// BITMAP: a binary-only cache, whose rows need not line up with the codes'
-// (head_dim 128: row tile t = sign bit t of bytes g8 / g8 + 8, 2^t units per
-// unit: one mask per fragment instead of a shift and a mask).  NRT: row
-// tiles (head_dim / 16).
-template <int GC, bool BITMAP = false, int NRT = 8>
+// NRT: row tiles (head_dim / 16).
+template <int GC, int NRT = 8>
 struct MmaState {
     static constexpr int NT = (GC + 1) / 2;
     float Uf[GC];  // U as a float, -inf while unset
@@ -460,8 +457,8 @@ struct MmaState {
     float em[GC], ez[GC], ew[GC];
 };
 
-template <int GC, bool BM, int NRT>
-__device__ __forceinline__ void init_soft(MmaState<GC, BM, NRT>& st) {
+template <int GC, int NRT>
+__device__ __forceinline__ void init_soft(MmaState<GC, NRT>& st) {
 #pragma unroll
     for (int g = 0; g < GC; ++g) {
         st.Uf[g] = -INFINITY;
@@ -473,7 +470,7 @@ __device__ __forceinline__ void init_soft(MmaState<GC, BM, NRT>& st) {
         st.ew[g] = 0.0f;
     }
 #pragma unroll
-    for (int n = 0; n < MmaState<GC, BM, NRT>::NT; ++n)
+    for (int n = 0; n < MmaState<GC, NRT>::NT; ++n)
 #pragma unroll
         for (int t = 0; t < NRT; ++t)
 #pragma unroll
@@ -845,8 +842,8 @@ __device__ __forceinline__ void residual_dots_mma(const uint8_t* knib, int kw, c
 // dropped low bits: each (row, tile) value is rebuilt from its four byte
 // columns (lanes with q = 2 (g % 2), 2 (g % 2) + 1 of column tile g / 2),
 // shifted, and split back into byte columns.
-template <int GC, bool BM, int NRT>
-__device__ __forceinline__ void mma_shift_down(MmaState<GC, BM, NRT>& st, int g, int delta) {
+template <int GC, int NRT>
+__device__ __forceinline__ void mma_shift_down(MmaState<GC, NRT>& st, int g, int delta) {
     const int q = threadIdx.x & 3;
     const bool mine = (q >> 1) == (g & 1), upper = q & 1;
     const int n = g >> 1;
@@ -868,12 +865,18 @@ __device__ __forceinline__ void mma_shift_down(MmaState<GC, BM, NRT>& st, int g,
 // One warp consumes its 32 keys (kw .. kw + 31) of a tile on the tensor-core
 // path.  RES = false: binary-only keys (a binary cache, or the adaptive
 // cache's second segment): no residual score, the sign part alone.
+// BM: the binary row map, for binary-only keys (a binary cache, or the
+// adaptive cache's binary-only segment), whose rows need not line up with
+// the codes': row tile 8w + t = sign bit t of bytes 16w + g8 / 16w + g8 + 8
+// of sign window w, 2^t units per unit (one mask per fragment instead of a
+// shift and a mask).  Not at head_dim 64, whose fragments hold one sign byte
+// per row pair.
 template <int D, int GC, typename Cfg, bool ENT = false, bool RES = true, bool BM = false, int NRT = 8>
-__device__ __forceinline__ void consume_warp_tile_mma(const QSmem& qs, MmaState<GC, BM, NRT>& st, const uint8_t* sb,
+__device__ __forceinline__ void consume_warp_tile_mma(const QSmem& qs, MmaState<GC, NRT>& st, const uint8_t* sb,
                                                       int kw, int nk, uint8_t* wb, int* dotb) {
     static_assert(nib_by_bit(D) && NRT == D / 16, "tensor-core path: head dims 64, 128, 256");
-    static_assert(!(BM && RES) && !(BM && D != 128), "the binary row map: head_dim 128, no codes");
-    constexpr int NT = MmaState<GC, BM, NRT>::NT, NWD = D / 32;
+    static_assert(!(BM && RES) && !(BM && D == 64), "the binary row map: no codes, not at head_dim 64");
+    constexpr int NT = MmaState<GC, NRT>::NT, NWD = D / 32;
     constexpr int WB_PART = 8 * NT * Cfg::WB_ROW;
     const int lane = threadIdx.x & 31;
     const int kk = kw + lane;
@@ -987,14 +990,18 @@ __device__ __forceinline__ void consume_warp_tile_mma(const QSmem& qs, MmaState<
         br[n][1] = (RES && ok) ? *reinterpret_cast<const uint32_t*>(rs + WB_PART + 16) : 0u;
     }
     // ---- sign part: bits c and c + 4 of sign bytes g8, g8 + 8 -------------------
-    if constexpr (BM) {  // binary row map: tile t = bit t of sign bytes g8, g8 + 8
-        uint32_t r0, r1, r2, r3;
-        ldsm_x2_trans_b8(sb + Cfg::OFF_VSIGN + kk * (D / 8), r0, r1, r2, r3);
+    if constexpr (BM) {  // binary row map: tile 8w + t = bit t of sign bytes 16w + g8, 16w + g8 + 8
 #pragma unroll
-        for (int t = 0; t < 8; ++t) {
-            const uint32_t mk = 0x01010101u << t;
+        for (int w = 0; w < D / 128; ++w) {
+            uint32_t r0, r1, r2, r3;
+            ldsm_x2_trans_b8(sb + Cfg::OFF_VSIGN + kk * (D / 8) + 16 * w, r0, r1, r2, r3);
 #pragma unroll
-            for (int n = 0; n < NT; ++n) mma_u8(st.acc[n][t], r0 & mk, r1 & mk, r2 & mk, r3 & mk, bs[n][0], bs[n][1]);
+            for (int t = 0; t < 8; ++t) {
+                const uint32_t mk = 0x01010101u << t;
+#pragma unroll
+                for (int n = 0; n < NT; ++n)
+                    mma_u8(st.acc[n][8 * w + t], r0 & mk, r1 & mk, r2 & mk, r3 & mk, bs[n][0], bs[n][1]);
+            }
         }
     } else if constexpr (D == 64) {  // tile t: bits t, t + 4 of sign byte g8; keys in sign_k order
         uint32_t r0, r1;
@@ -1191,7 +1198,7 @@ __device__ __forceinline__ void xchg_finish(const DecodeArgs& a, int slot, int h
 // Per-warp record (m, l, o[d] - t) of each head into mg[warp][g][d + 2]:
 // f32x2 accumulators, reduced over the lanes holding the same dims.
 template <int D, int GC, typename Cfg>
-__device__ __forceinline__ void warp_records(float* mg, SoftState<GC, Cfg::NP>& st) {
+__device__ __forceinline__ void warp_records(float* mg, SoftState<GC, Cfg::NP>& st, bool /*bm*/) {
     constexpr int KPW = Cfg::KPW, DL = Cfg::DL, NP = Cfg::NP;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, qt = lane / KPW;
 #pragma unroll
@@ -1233,9 +1240,11 @@ __device__ __forceinline__ void warp_records(float* mg, SoftState<GC, Cfg::NP>& 
 // tile 8 w + 2c + h (head_dim 64: tile c + 2 h', dim = 8 g8 + 2 h' + c' + 4 hi,
 // i.e. tile dim % 4), row g8 + 8 hi (16 units per unit when hi), column tile
 // g / 2, byte columns 0-1 in lane 4 g8 + 2 (g % 2) and 2-3 in the lane after it.
-template <int D, int GC, typename Cfg, bool BM, int NRT>
-__device__ __forceinline__ void warp_records(float* mg, MmaState<GC, BM, NRT>& st) {
-    constexpr int NT = MmaState<GC, BM, NRT>::NT, DS = Cfg::DUMP_STRIDE;
+// bm: the accumulators were filled with the binary row map (dim = 128 w +
+// 64 h + 8 g8 + t in tile 8 w + t, row g8 + 8 h, 2^t units per unit).
+template <int D, int GC, typename Cfg, int NRT>
+__device__ __forceinline__ void warp_records(float* mg, MmaState<GC, NRT>& st, bool bm) {
+    constexpr int NT = MmaState<GC, NRT>::NT, DS = Cfg::DUMP_STRIDE;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     int* dump = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(mg) + Cfg::DUMP_OFF) + warp * 32 * DS;
 #pragma unroll
@@ -1265,13 +1274,13 @@ __device__ __forceinline__ void warp_records(float* mg, MmaState<GC, BM, NRT>& s
             const int dim = (D / 32) * lane + e;
             const int h = (dim >> 6) & 1, w = dim >> 7, g8 = (dim >> 3) & 7, c = dim & 3, hi = (dim >> 2) & 1;
             // shared map: tile 8w + 2c + h (head_dim 64: tile c), row g8 + 8 hi;
-            // binary map (head_dim 128): tile dim % 8, row g8 + 8 h
-            const int tile = BM ? (dim & 7) : (D == 64 ? c : 8 * w + 2 * c + h), upper = BM ? h : hi;
+            // binary map: tile 8w + dim % 8, row g8 + 8 h
+            const int tile = bm ? 8 * w + (dim & 7) : (D == 64 ? c : 8 * w + 2 * c + h), upper = bm ? h : hi;
             const int* la = dump + (4 * g8 + 2 * (g & 1)) * DS + 4 * NRT * (g >> 1) + 4 * tile + 2 * upper;
             const int* lb = la + DS;
             const uint64_t v0 = (uint64_t)(uint32_t)la[0] + ((uint64_t)(uint32_t)la[1] << 8);
             const uint64_t v1 = (uint64_t)(uint32_t)lb[0] + ((uint64_t)(uint32_t)lb[1] << 8);
-            const float unit = BM ? exp2i(-(dim & 7)) : (hi ? (1.0f / 16.0f) : 1.0f);
+            const float unit = bm ? exp2i(-(dim & 7)) : (hi ? (1.0f / 16.0f) : 1.0f);
             const float v = ((float)v0 + 65536.0f * (float)v1) * unit;
             rec[2 + dim] = v - t;
         }
@@ -1279,11 +1288,12 @@ __device__ __forceinline__ void warp_records(float* mg, MmaState<GC, BM, NRT>& s
 }
 
 template <int D, int GC, typename Cfg, bool ENT = false, typename St>
-__device__ __forceinline__ void finish_cta(const DecodeArgs& a, int slot, int hg, int split, uint8_t* smem, St& st) {
+__device__ __forceinline__ void finish_cta(const DecodeArgs& a, int slot, int hg, int split, uint8_t* smem, St& st,
+                                           bool bm = false) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     __syncthreads();  // ring no longer in use
     float* mg = reinterpret_cast<float*>(smem);  // [warps][GC][D+2]
-    warp_records<D, GC, Cfg>(mg, st);
+    warp_records<D, GC, Cfg>(mg, st, bm);
     __shared__ EntPart s_ent[ENT ? kWarps : 1][ENT ? GC : 1];
     if constexpr (ENT) {
 #pragma unroll
@@ -1731,7 +1741,11 @@ __global__ void __launch_bounds__(kDecThreads, DecCfg<D, GC, COMP>::MIN_CTAS)
     // the tensor-core value phase (in adaptive caches the binary-only
     // segment runs its sign part alone)
     constexpr bool MMA = Cfg::MMA;
-    std::conditional_t<MMA, MmaState<GC, Cfg::BM, Cfg::NRT>, SoftState<GC, Cfg::NP>> st;
+    std::conditional_t<MMA, MmaState<GC, Cfg::NRT>, SoftState<GC, Cfg::NP>> st;
+    // the binary row map for binary-only keys: a binary cache, or the binary
+    // segment of an adaptive cache (its CTAs see no code), not at head_dim 64
+    constexpr bool BIN_BM = D != 64;
+    const bool bm = Cfg::BM || (ADA && seg_bin && BIN_BM);
     init_soft(st);
 
     int it = 0;
@@ -1765,16 +1779,17 @@ __global__ void __launch_bounds__(kDecThreads, DecCfg<D, GC, COMP>::MIN_CTAS)
             if (wide) {
                 if constexpr (BIN4) {
                     for (int j = 0; j < BinStageCfg<D>::TILES && j * T < nk; ++j)
-                        consume_warp_tile_mma<D, GC, BinStageCfg<D>, false, false>(qsm, st, sbuf, j * T + warp * 32, nk,
-                                                                                   wb, dotb);
+                        consume_warp_tile_mma<D, GC, BinStageCfg<D>, false, false, BIN_BM>(qsm, st, sbuf,
+                                                                                           j * T + warp * 32, nk, wb,
+                                                                                           dotb);
                 }
             } else if (Cfg::TPS > 1 && TS > T) {
                 for (int j = 0; j < Cfg::TPS && j * T < nk; ++j)
-                    consume_warp_tile_mma<D, GC, Cfg, ENT, COMP>(qsm, st, sbuf, j * T + warp * 32, nk, wb, dotb);
+                    consume_warp_tile_mma<D, GC, Cfg, ENT, COMP, Cfg::BM>(qsm, st, sbuf, j * T + warp * 32, nk, wb, dotb);
             } else if (ADA && seg_bin)
-                consume_warp_tile_mma<D, GC, Cfg, false, false>(qsm, st, sbuf, warp * 32, nk, wb, dotb);
+                consume_warp_tile_mma<D, GC, Cfg, false, false, BIN_BM>(qsm, st, sbuf, warp * 32, nk, wb, dotb);
             else
-                consume_warp_tile_mma<D, GC, Cfg, ENT, COMP>(qsm, st, sbuf, warp * 32, nk, wb, dotb);
+                consume_warp_tile_mma<D, GC, Cfg, ENT, COMP, Cfg::BM>(qsm, st, sbuf, warp * 32, nk, wb, dotb);
         } else {
             if (ADA && seg_bin)
                 consume_warp_tile<D, GC, false, Cfg>(qs, st, smem + stage * Cfg::STAGE_B, warp * 32, nk);
@@ -1799,7 +1814,7 @@ __global__ void __launch_bounds__(kDecThreads, DecCfg<D, GC, COMP>::MIN_CTAS)
         }
         return;
     }
-    finish_cta<D, GC, Cfg, ENT>(a, slot, hg, split, smem, st);
+    finish_cta<D, GC, Cfg, ENT>(a, slot, hg, split, smem, st, bm);
 }
 
 // ---------------------------------------------------------------------------
