@@ -64,7 +64,7 @@ __device__ unsigned int g_bc_device_error = 0;
 #define BC_DEC_MIN_CTAS_C1 4   // resident CTAs per SM the compensated one-head kernel is held to
 #endif
 #ifndef BC_DEC_MIN_CTAS_B1
-#define BC_DEC_MIN_CTAS_B1 5   // resident CTAs per SM the binary one-head kernel is held to
+#define BC_DEC_MIN_CTAS_B1 4   // resident CTAs per SM the binary one-head tensor-core kernel is held to (C3 binary: 4 21.4 us, 5 22.9 us)
 #endif
 #ifndef BC_DEC_BIN_GC
 #define BC_DEC_BIN_GC 4        // most query heads per CTA in binary grouped-query caches (binary C4: 4 heads 91 us, 2 heads 106 us)
@@ -185,7 +185,7 @@ struct DecCfg {
     // CTAs that shared memory allows)
     static constexpr int MIN_CTAS =
         (D > 128) ? 0
-                  : ((GC == 1 && !COMP) ? BC_DEC_MIN_CTAS_B1
+                  : ((GC == 1 && !COMP) ? (D == 128 ? BC_DEC_MIN_CTAS_B1 : 5)
                                         : (GC == 1 ? (D == 64 ? 5 : BC_DEC_MIN_CTAS_C1) : 4)) * 128 / kDecThreads;
 };
 
