@@ -180,11 +180,14 @@ struct DecCfg {
     static constexpr int SMEM_B = SCR_OFF + SCR_B + 128;       // + slack to align the base to 128 B
     static_assert(!MMA || DUMP_OFF + DUMP_B <= BODY_B, "accumulator dump exceeds the ring");
     // Resident CTAs per SM that shared memory allows at head_dim <= 128 with one
-    // head per CTA; the register budget is held to it (0: no bound).
+    // head per CTA; the register budget is held to it.
     // (head_dim 64, one head: five, whose registers then match the five
     // CTAs that shared memory allows)
+    // (head_dim 256: two, which shared memory allows anyway, so the kernel may
+    // use up to 255 registers: C5 d=256 466 -> 455 us against the compiler's
+    // own choice of 128)
     static constexpr int MIN_CTAS =
-        (D > 128) ? 0
+        (D > 128) ? 2
                   : ((GC == 1 && !COMP) ? (D == 128 ? BC_DEC_MIN_CTAS_B1 : 5)
                                         : (GC == 1 ? (D == 64 ? 5 : BC_DEC_MIN_CTAS_C1) : 4)) * 128 / kDecThreads;
 };
