@@ -131,6 +131,28 @@ def test_peer_exchange_refuses_other_shapes():
         x.decode(torch.zeros(4, 64, dtype=torch.float16), SimpleNamespace(n_slots=4), K, 64, 1)
 
 
+def test_host_operands_must_be_pinned():
+    """Host-resident Q and output are read and written by the GPU directly, so
+    the adaptive and exchange decodes refuse pageable host tensors (and a
+    too-small output) before any device work."""
+    from types import SimpleNamespace
+
+    from bitcache_b200 import dist as bdist
+    from bitcache_b200 import planes
+
+    q = torch.zeros(4, 128, dtype=torch.float16)  # pageable host memory
+    with pytest.raises(RuntimeError, match="pinned host tensor"):
+        planes.device_query(q, torch.device("cpu"))
+    x = object.__new__(bdist.PeerExchange)
+    x._lib = _lib
+    x.n_heads, x.head_dim = 4, 128
+    K = SimpleNamespace(n_slots=4, sign=SimpleNamespace(device=torch.device("cpu")))
+    with pytest.raises(RuntimeError, match="pinned host tensor"):
+        x.decode(q, K, K, 64, 1)
+    with pytest.raises(RuntimeError, match="pinned host tensor"):
+        x.decode(q, K, K, 64, 1, out=torch.zeros(4, 128, dtype=torch.float16))
+
+
 def test_bitcache_import_name():
     """The reference's import name gives this implementation."""
     import bitcache
