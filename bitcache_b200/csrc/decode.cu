@@ -183,11 +183,11 @@ struct DecCfg {
     // head per CTA; the register budget is held to it.
     // (head_dim 64, one head: five, whose registers then match the five
     // CTAs that shared memory allows)
-    // (head_dim 256: two, which shared memory allows anyway, so the kernel may
-    // use up to 255 registers: C5 d=256 466 -> 455 us against the compiler's
-    // own choice of 128)
+    // (head_dim 256, compensated: two, which shared memory allows anyway, so
+    // the kernel may use up to 255 registers: C5 d=256 466 -> 455 us against
+    // the compiler's own choice of 128; binary: no bound, the compiler's choice)
     static constexpr int MIN_CTAS =
-        (D > 128) ? 2
+        (D > 128) ? (COMP ? 2 : 0)
                   : ((GC == 1 && !COMP) ? (D == 128 ? BC_DEC_MIN_CTAS_B1 : 5)
                                         : (GC == 1 ? (D == 64 ? 5 : BC_DEC_MIN_CTAS_C1) : 4)) * 128 / kDecThreads;
 };
